@@ -1,0 +1,172 @@
+/*
+ * spinn_cuda.h -- C ABI of libspinn_cuda.so, the B200 (sm_100a) implementation of SPINN's
+ * dense-contraction hot path (Conv / Gemm / MatMul and the Conv+BN/ReLU/SiLU/Add fusions).
+ *
+ * Two levels, both plain C (pointers, sizes, status codes; no C++ or torch types):
+ *
+ *  1. Operator level: drop-in replacements for the reference operators, with the
+ *     reference's SpinnOpKernel signature, so SPINN's own runtime (spinn_load / spinn_plan /
+ *     spinn_run) can dispatch Conv, Gemm and MatMul to the GPU unchanged.  Tensor data may
+ *     be host memory (the reference arena) or device memory; results are written where
+ *     out[0]->data points.
+ *
+ *  2. Model level: a device-resident executor for a whole .ennf model that mirrors the
+ *     reference's three stages (load -> plan -> run): one device arena, weights uploaded
+ *     once and pre-transformed, every node on the GPU, the node list replayed as a CUDA
+ *     graph.
+ *
+ * Every entry point returns 0 on success and a negative SPINN_CUDA_E* code on failure;
+ * spinn_cuda_last_error() gives the message of the most recent failure on the calling thread.
+ * The reference runtime ignores operator return codes (SPINN/run_time/spinn_runtime.c:331-345);
+ * these do not.
+ */
+#ifndef SPINN_CUDA_H
+#define SPINN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ shared types */
+
+/* Runtime tensor record.  Byte-for-byte the reference's SpinnTensor
+ * (SPINN/run_time/spinn_runtime.h:25-40): 72 bytes on LP64, `data` at offset 56. */
+#define SPINN_CUDA_MAX_DIMS 8
+typedef struct {
+    uint16_t id;
+    uint8_t dtype;
+    uint8_t ndim;
+    uint32_t dims[SPINN_CUDA_MAX_DIMS];
+    uint32_t elem_count;
+    uint8_t is_weight;
+    uint8_t ref_count;
+    uint32_t size;
+    uint32_t offset;
+    void *data;
+    void *packed_data; /* never touched here: the reference runtime free()s it */
+} SpinnTensor;
+
+/* Operator kernel signature (SPINN/run_time/spinn_ops.h:31-33). */
+typedef int (*SpinnOpKernel)(SpinnTensor **in, int n_in, void *params, uint16_t params_size,
+                             SpinnTensor **out, int n_out);
+
+/* Status codes. */
+#define SPINN_CUDA_OK 0
+#define SPINN_CUDA_EINVAL (-1)     /* bad argument, shape or parameter block */
+#define SPINN_CUDA_ENOMEM (-2)     /* device or host allocation failed / arena budget exceeded */
+#define SPINN_CUDA_ECUDA (-3)      /* CUDA runtime or driver error */
+#define SPINN_CUDA_EUNSUPPORTED (-4) /* operator or configuration not implemented */
+#define SPINN_CUDA_ETIMEOUT (-5)   /* a kernel's bounded wait expired (device error flag set) */
+#define SPINN_CUDA_EFORMAT (-6)    /* malformed .ennf image */
+#define SPINN_CUDA_ESTATE (-7)     /* call out of order (e.g. run before plan) */
+
+/* ------------------------------------------------------------------ device session */
+
+/* Selects `device` for the calling thread, creates its stream and a scratch pool of
+ * `scratch_bytes` (0 = grow on demand).  Must precede the operator-level entry points.
+ * Replaces nothing in the reference (it has no device); called once per GPU thread. */
+int spinn_cuda_init(int device, size_t scratch_bytes);
+
+/* Waits for all work queued by this thread's session; returns the first deferred error. */
+int spinn_cuda_sync(void);
+
+/* Releases the calling thread's session (stream, scratch, cached weights). */
+void spinn_cuda_shutdown(void);
+
+/* Message of the last failure on this thread ("" if none).  Never NULL. */
+const char *spinn_cuda_last_error(void);
+
+/* Installs spinn_cuda_conv2d / _gemm / _matmul into a registry through `register_op`
+ * (op_type: ENNF_OpType value; Conv=60, Gemm=160, MatMul=161, SPINN/ennf_op_types.h:79,134,135).
+ * The reference registry is a file-static array (SPINN/run_time/spinn_ops.c:17); the
+ * setter it needs is shown in INTEGRATION.md.  Returns the number of operators installed. */
+int spinn_cuda_register(int (*register_op)(uint16_t op_type, SpinnOpKernel fn));
+
+/* ------------------------------------------------------------------ operator level */
+
+/* ONNX Conv (2-D, NCHW) with the fused post-op in ENNF_ConvParams.reserved
+ * (0 none, 1 ReLU, 3 SiLU, 4 +residual, 5 +residual then ReLU; residual = last input).
+ * Replaces op_conv2d (SPINN/run_time/ops/conv/conv2d.c:92-232; declared ops/kernels.h:75).
+ * Unlike the reference's group==1 path (gemm_kernel.c:497-590) the fused post-op is applied. */
+int spinn_cuda_conv2d(SpinnTensor **in, int n_in, void *params, uint16_t params_size,
+                      SpinnTensor **out, int n_out);
+
+/* ONNX Gemm Y = alpha*op(A)*op(B) + beta*C (C: length-N vector or MxN).
+ * Replaces op_gemm (SPINN/run_time/ops/mm/gemm.c:7-78; declared ops/kernels.h:80).
+ * Implements ONNX semantics for every M; the reference multiplies beta*C by alpha too when
+ * M > 1 (gemm.c:62-69 with gemm_kernel.c:298-301). */
+int spinn_cuda_gemm(SpinnTensor **in, int n_in, void *params, uint16_t params_size,
+                    SpinnTensor **out, int n_out);
+
+/* MatMul: 2-D, batched A with broadcast 2-D B, or equal batch counts.
+ * Replaces op_matmul (SPINN/run_time/ops/mm/matmul.c:6-62; declared ops/kernels.h:81). */
+int spinn_cuda_matmul(SpinnTensor **in, int n_in, void *params, uint16_t params_size,
+                      SpinnTensor **out, int n_out);
+
+/* ------------------------------------------------------------------ model level */
+
+typedef struct SpinnCudaModel SpinnCudaModel;
+
+/* Stage 1: parse a .ennf file / in-memory image (copied).  Mirrors spinn_load
+ * (SPINN/run_time/spinn_runtime.h:107-112).  NULL on failure (see spinn_cuda_last_error). */
+SpinnCudaModel *spinn_cuda_load(const char *path);
+SpinnCudaModel *spinn_cuda_load_buffer(const void *data, size_t size);
+
+/* Stage 2: plan and allocate on `device`: one device arena (64-bit offsets; budget
+ * max_arena_bytes, 0 = unlimited), weights uploaded and pre-transformed, kernels chosen.
+ * Mirrors spinn_plan (spinn_runtime.h:114-123; SPINN_MEM_ERR_NOMEM -> SPINN_CUDA_ENOMEM).
+ * flags: bit 0 = do not capture a CUDA graph; bit 1 = profile per node (CUDA events);
+ *        bit 2 = keep activations fp32 on store (no tf32 rounding of conv outputs). */
+#define SPINN_CUDA_PLAN_NO_GRAPH 1
+#define SPINN_CUDA_PLAN_PROFILE 2
+#define SPINN_CUDA_PLAN_NO_ROUND 4
+int spinn_cuda_plan(SpinnCudaModel *m, int device, uint64_t max_arena_bytes, int flags);
+
+/* Stage 3: run one inference.  Copies input 0 (NCHW fp32, host memory) to the device, runs
+ * every node, and copies output 0 back to `output` (host).  Mirrors spinn_run
+ * (spinn_runtime.h:125-131).  Synchronous. */
+int spinn_cuda_run(SpinnCudaModel *m, const void *input, void *output);
+
+/* Device-resident run: inputs are taken from, and outputs left in, the model's device
+ * buffers (spinn_cuda_io_ptr); work is queued on `stream` (NULL = the model's stream) and
+ * not waited for. */
+int spinn_cuda_run_device(SpinnCudaModel *m, void *stream);
+
+/* Device buffer of graph input (is_output=0) or output (is_output=1) number `index`,
+ * NCHW fp32 as the .ennf declares it, and its size in bytes. */
+void *spinn_cuda_io_ptr(SpinnCudaModel *m, int is_output, int index, size_t *bytes);
+
+/* Number of graph inputs / outputs, and the dims of one (returns ndim, fills dims[8]). */
+int spinn_cuda_io_count(SpinnCudaModel *m, int is_output);
+int spinn_cuda_io_dims(SpinnCudaModel *m, int is_output, int index, uint32_t *dims);
+
+/* Planned sizes: device arena bytes and pre-transformed weight bytes. */
+int spinn_cuda_plan_info(SpinnCudaModel *m, uint64_t *arena_bytes, uint64_t *weight_bytes,
+                         int *num_steps, int *num_kernels);
+
+/* Per-node device times of the last run (plan flag PROFILE): fills up to `cap` entries of
+ * op_type / milliseconds / algorithmic FLOPs; returns the number of entries. */
+int spinn_cuda_profile(SpinnCudaModel *m, int *op_types, float *ms, double *flops, int cap);
+
+/* Kernel id of step `i` (for reporting): 0 none/alias, 1 tcgen05 conv, 2 tcgen05 gemm,
+ * 3 depthwise, 4 direct conv, 5 pool, 6 elementwise, 7 layout, 8 winograd. */
+int spinn_cuda_step_kind(SpinnCudaModel *m, int i);
+
+/* Stage 4: free everything the model owns.  Mirrors spinn_free (spinn_runtime.h:133). */
+void spinn_cuda_free(SpinnCudaModel *m);
+
+/* Page-locked host memory for fast host<->device copies (cudaHostAlloc / cudaFreeHost). */
+void *spinn_cuda_host_alloc(size_t bytes);
+void spinn_cuda_host_free(void *p);
+
+/* Library version string. */
+const char *spinn_cuda_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPINN_CUDA_H */

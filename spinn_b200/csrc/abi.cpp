@@ -1,0 +1,613 @@
+// abi.cpp -- operator-level C ABI: drop-in SpinnOpKernel implementations of Conv, Gemm and
+// MatMul for SPINN's runtime, plus the per-thread device session they run in.
+//
+// The reference operators (SPINN/run_time/ops/conv/conv2d.c, ops/mm/gemm.c, ops/mm/matmul.c)
+// read NCHW fp32 tensors from host memory.  These wrappers accept the same SpinnTensor
+// records with host or device data pointers (told apart with cudaPointerGetAttributes),
+// convert activations to NHWC on the device, run the tcgen05 kernels (or the CUDA-core
+// depthwise / grouped kernels), and write NCHW results back where out[0]->data points.
+// Constant weights are pre-transformed once and cached per (pointer, size, layout); the
+// reference keeps its packed copy in SpinnTensor.packed_data, which spinn_free() releases
+// with free(), so the device copies live in this library's cache instead.
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
+
+#include "internal.h"
+
+namespace spinn {
+namespace {
+
+constexpr uint16_t kOpConv = 60, kOpGemm = 160, kOpMatMul = 161;
+
+int round4(int c) { return (c + 3) & ~3; }
+
+struct DevWeight {
+  float* w = nullptr;
+  float* b = nullptr;
+  int kpad = 0;
+};
+
+struct Session {
+  bool ready = false;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint8_t* scratch = nullptr;
+  size_t scratch_cap = 0;
+  size_t scratch_used = 0;
+  std::map<std::tuple<const void*, uint64_t, int, int>, DevWeight> wcache;
+};
+
+thread_local Session g_sess;
+
+int ensure_session() {
+  if (g_sess.ready) return 0;
+  return spinn_cuda_init(0, 0);
+}
+
+// Bump allocator over the session scratch; `reserve` sizes it for one operator call.
+int scratch_reserve(size_t bytes) {
+  Session& S = g_sess;
+  S.scratch_used = 0;
+  if (bytes <= S.scratch_cap) return 0;
+  SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));
+  if (S.scratch) cudaFree(S.scratch);
+  S.scratch = nullptr;
+  S.scratch_cap = 0;
+  const size_t cap = bytes + (bytes >> 2) + (1 << 20);
+  SPINN_CUDA_TRY(cudaMalloc(&S.scratch, cap));
+  S.scratch_cap = cap;
+  return 0;
+}
+float* scratch_take(size_t bytes) {
+  Session& S = g_sess;
+  const size_t off = (S.scratch_used + 255) & ~size_t(255);
+  S.scratch_used = off + bytes;
+  return reinterpret_cast<float*>(S.scratch + off);
+}
+size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
+
+bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// Host copy of a tensor's data (for weight preparation).
+int fetch_host(const SpinnTensor* t, std::vector<float>* out) {
+  out->resize(t->elem_count);
+  if (is_device_ptr(t->data)) {
+    SPINN_CUDA_TRY(cudaMemcpy(out->data(), t->data, (size_t)t->elem_count * 4, cudaMemcpyDeviceToHost));
+  } else {
+    std::memcpy(out->data(), t->data, (size_t)t->elem_count * 4);
+  }
+  return 0;
+}
+
+// Device pointer holding `bytes` of tensor data: the data itself, or a scratch copy.
+int to_device(const SpinnTensor* t, size_t bytes, const float** dptr) {
+  if (is_device_ptr(t->data)) {
+    *dptr = static_cast<const float*>(t->data);
+    return 0;
+  }
+  float* d = scratch_take(bytes);
+  SPINN_CUDA_TRY(cudaMemcpyAsync(d, t->data, bytes, cudaMemcpyHostToDevice, g_sess.stream));
+  *dptr = d;
+  return 0;
+}
+
+enum WKind { W_TC = 0, W_DW = 1, W_GROUPED = 2, W_GEMM_B = 3 };
+
+// Conv weights for the chosen kernel, cached.
+int conv_weights(const SpinnTensor* W, const SpinnTensor* B, int kind, int C, int cpad, int OC, int KH, int KW, int G,
+                 DevWeight** out) {
+  Session& S = g_sess;
+  auto key = std::make_tuple((const void*)W->data, (uint64_t)W->elem_count * 1000003ull + (B ? (uint64_t)(uintptr_t)B->data : 0),
+                             kind, cpad);
+  auto it = S.wcache.find(key);
+  if (it != S.wcache.end()) {
+    *out = &it->second;
+    return 0;
+  }
+  std::vector<float> w, b;
+  int rc = fetch_host(W, &w);
+  if (rc) return rc;
+  if (B) {
+    rc = fetch_host(B, &b);
+    if (rc) return rc;
+  }
+  const int ocpad = round4(OC);
+  std::vector<float> hw;
+  DevWeight dw;
+  if (kind == W_TC) {
+    const int K = KH * KW * cpad;
+    dw.kpad = tc_num_kb(K) * 32;
+    hw.assign((size_t)ocpad * dw.kpad, 0.0f);
+    for (int o = 0; o < OC; ++o)
+      for (int c = 0; c < C; ++c)
+        for (int r = 0; r < KH; ++r)
+          for (int s = 0; s < KW; ++s)
+            hw[(size_t)o * dw.kpad + (r * KW + s) * cpad + c] = host_round_tf32(w[(((size_t)o * C + c) * KH + r) * KW + s]);
+  } else if (kind == W_DW) {
+    hw.assign((size_t)KH * KW * ocpad, 0.0f);
+    for (int o = 0; o < OC; ++o)
+      for (int t = 0; t < KH * KW; ++t) hw[(size_t)t * ocpad + o] = w[(size_t)o * KH * KW + t];
+  } else {
+    const int cg = C / G;
+    hw.assign((size_t)OC * KH * KW * cg, 0.0f);
+    for (int o = 0; o < OC; ++o)
+      for (int c = 0; c < cg; ++c)
+        for (int r = 0; r < KH; ++r)
+          for (int s = 0; s < KW; ++s)
+            hw[(((size_t)o * KH + r) * KW + s) * cg + c] = w[(((size_t)o * cg + c) * KH + r) * KW + s];
+  }
+  SPINN_CUDA_TRY(cudaMalloc(&dw.w, hw.size() * 4));
+  SPINN_CUDA_TRY(cudaMemcpy(dw.w, hw.data(), hw.size() * 4, cudaMemcpyHostToDevice));
+  std::vector<float> hb(ocpad, 0.0f);
+  for (int o = 0; o < OC && B; ++o) hb[o] = b[o];
+  SPINN_CUDA_TRY(cudaMalloc(&dw.b, hb.size() * 4));
+  SPINN_CUDA_TRY(cudaMemcpy(dw.b, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice));
+  auto ins = S.wcache.emplace(key, dw);
+  *out = &ins.first->second;
+  return 0;
+}
+
+int finish_output(SpinnTensor* Y, const float* dev_y, size_t bytes) {
+  // dev_y is scratch when Y is host memory
+  if (!is_device_ptr(Y->data)) {
+    SPINN_CUDA_TRY(cudaMemcpyAsync(Y->data, dev_y, bytes, cudaMemcpyDeviceToHost, g_sess.stream));
+    SPINN_CUDA_TRY(cudaStreamSynchronize(g_sess.stream));
+    return check_device_error_flag(g_sess.device, g_sess.stream);
+  }
+  return 0;
+}
+
+struct ConvGeom {
+  int N, C, H, W, OC, KC, KH, KW, SH, SW, PH, PW, DH, DW, G, OH, OW, act;
+};
+
+// Parameter decoding of op_conv2d (SPINN/run_time/ops/conv/conv2d.c:97-142).
+int conv_geom(SpinnTensor** in, int n_in, void* params, uint16_t params_size, SpinnTensor** out, ConvGeom* g) {
+  const SpinnTensor* X = in[0];
+  const SpinnTensor* W = in[1];
+  SPINN_CHECK_ARG(X->ndim == 4 && W->ndim == 4 && out[0]->ndim == 4, "conv2d: X, W and Y must be 4-D");
+  g->N = X->dims[0];
+  g->C = X->dims[1];
+  g->H = X->dims[2];
+  g->W = X->dims[3];
+  g->OC = W->dims[0];
+  g->KC = W->dims[1];
+  g->KH = W->dims[2];
+  g->KW = W->dims[3];
+  g->SH = g->SW = 1;
+  g->PH = g->PW = 0;
+  g->DH = g->DW = 1;
+  g->G = 1;
+  g->act = 0;
+  g->OH = out[0]->dims[2];
+  g->OW = out[0]->dims[3];
+  if (params && params_size >= 44) {
+    const uint16_t* u = static_cast<const uint16_t*>(params);
+    const uint8_t* b = static_cast<const uint8_t*>(params);
+    if (u[20] > 0) g->G = u[20];
+    if (u[0] > 0) g->KH = u[0];
+    if (u[1] > 0) g->KW = u[1];
+    if (u[4] > 0) g->SH = u[4];
+    if (u[5] > 0) g->SW = u[5];
+    g->PH = u[8];
+    g->PW = u[9];
+    if (u[16] > 0) g->DH = u[16];
+    if (u[17] > 0) g->DW = u[17];
+    const int auto_pad = b[42];
+    g->act = b[43];
+    if (auto_pad == 1 || auto_pad == 2) {
+      int ph = (g->OH - 1) * g->SH + g->KH - g->H;
+      if (ph < 0) ph = 0;
+      int pw = (g->OW - 1) * g->SW + g->KW - g->W;
+      if (pw < 0) pw = 0;
+      g->PH = auto_pad == 1 ? ph / 2 : (ph + 1) / 2;
+      g->PW = auto_pad == 1 ? pw / 2 : (pw + 1) / 2;
+    }
+  }
+  SPINN_CHECK_ARG(g->C == g->KC * g->G && g->OC % g->G == 0, "conv2d: channels %d / group %d / weight %d mismatch", g->C,
+                  g->G, g->KC);
+  SPINN_CHECK_ARG((int)out[0]->dims[1] == g->OC && (int)out[0]->dims[0] == g->N, "conv2d: output shape mismatch");
+  (void)n_in;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+__attribute__((visibility("default"))) int spinn_cuda_init(int device, size_t scratch_bytes) {
+  Session& S = g_sess;
+  if (S.ready && S.device == device) return 0;
+  if (S.ready) spinn_cuda_shutdown();
+  SPINN_CUDA_TRY(cudaSetDevice(device));
+  S.device = device;
+  SPINN_CUDA_TRY(cudaStreamCreateWithFlags(&S.stream, cudaStreamNonBlocking));
+  S.ready = true;
+  if (scratch_bytes) {
+    int rc = scratch_reserve(scratch_bytes);
+    if (rc) return rc;
+  }
+  if (!device_error_flag(device)) {
+    set_error("spinn_cuda_init: cannot allocate the device error flag");
+    return SPINN_CUDA_ENOMEM;
+  }
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_sync(void) {
+  Session& S = g_sess;
+  if (!S.ready) return 0;
+  SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));
+  return check_device_error_flag(S.device, S.stream);
+}
+
+__attribute__((visibility("default"))) void spinn_cuda_shutdown(void) {
+  Session& S = g_sess;
+  if (!S.ready) return;
+  cudaSetDevice(S.device);
+  cudaStreamSynchronize(S.stream);
+  for (auto& kv : S.wcache) {
+    cudaFree(kv.second.w);
+    cudaFree(kv.second.b);
+  }
+  S.wcache.clear();
+  if (S.scratch) cudaFree(S.scratch);
+  S.scratch = nullptr;
+  S.scratch_cap = 0;
+  cudaStreamDestroy(S.stream);
+  S.stream = nullptr;
+  S.ready = false;
+}
+
+__attribute__((visibility("default"))) const char* spinn_cuda_last_error(void) { return get_error(); }
+
+__attribute__((visibility("default"))) const char* spinn_cuda_version(void) { return "spinn_b200 0.1 (sm_100a)"; }
+
+__attribute__((visibility("default"))) void* spinn_cuda_host_alloc(size_t bytes) {
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, bytes, cudaHostAllocDefault) != cudaSuccess) {
+    set_error("cudaHostAlloc(%zu) failed", bytes);
+    return nullptr;
+  }
+  return p;
+}
+
+__attribute__((visibility("default"))) void spinn_cuda_host_free(void* p) {
+  if (p) cudaFreeHost(p);
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_conv2d(SpinnTensor** in, int n_in, void* params,
+                                                             uint16_t params_size, SpinnTensor** out, int n_out) {
+  if (!in || !out || n_in < 2 || n_out < 1 || !in[0] || !in[1] || !out[0] || !in[0]->data || !in[1]->data ||
+      !out[0]->data) {
+    set_error("conv2d: need X, W and Y with data");
+    return SPINN_CUDA_EINVAL;
+  }
+  int rc = ensure_session();
+  if (rc) return rc;
+  ConvGeom g;
+  rc = conv_geom(in, n_in, params, params_size, out, &g);
+  if (rc) return rc;
+  const bool has_res = g.act == 4 || g.act == 5;
+  const int n_real = has_res ? n_in - 1 : n_in;
+  const SpinnTensor* B = (n_real > 2 && in[2] && in[2]->data) ? in[2] : nullptr;
+  const SpinnTensor* R = has_res ? in[n_in - 1] : nullptr;
+  SPINN_CHECK_ARG(!has_res || (R && R->data && R->elem_count == out[0]->elem_count), "conv2d: residual shape mismatch");
+  const int cpad = round4(g.C), ocpad = round4(g.OC);
+  const size_t xb = (size_t)g.N * g.C * g.H * g.W * 4, yb = (size_t)g.N * g.OC * g.OH * g.OW * 4;
+  const size_t xnb = (size_t)g.N * g.H * g.W * cpad * 4, ynb = (size_t)g.N * g.OH * g.OW * ocpad * 4;
+  rc = scratch_reserve(pad256(xb) + pad256(xnb) + 2 * pad256(ynb) + pad256(yb) + pad256(yb) + 4096);
+  if (rc) return rc;
+  cudaStream_t st = g_sess.stream;
+  const float* x;
+  rc = to_device(in[0], xb, &x);
+  if (rc) return rc;
+  float* xn = scratch_take(xnb);
+  rc = launch_nchw_to_nhwc(x, xn, g.N, g.C, g.H, g.W, cpad, st);
+  if (rc) return rc;
+  float* rn = nullptr;
+  if (R) {
+    const float* r;
+    rc = to_device(R, yb, &r);
+    if (rc) return rc;
+    rn = scratch_take(ynb);
+    rc = launch_nchw_to_nhwc(r, rn, g.N, g.OC, g.OH, g.OW, ocpad, st);
+    if (rc) return rc;
+  }
+  float* yn = scratch_take(ynb);
+  DevWeight* dw = nullptr;
+  if (g.G == 1) {
+    rc = conv_weights(in[1], B, W_TC, g.C, cpad, g.OC, g.KH, g.KW, 1, &dw);
+    if (rc) return rc;
+    TcGemmArgs a;
+    a.a_mode = 0;
+    a.x = xn;
+    a.n = g.N;
+    a.h = g.H;
+    a.w = g.W;
+    a.cpad = cpad;
+    a.kh = g.KH;
+    a.kw = g.KW;
+    a.sh = g.SH;
+    a.sw = g.SW;
+    a.ph = g.PH;
+    a.pw = g.PW;
+    a.dh = g.DH;
+    a.dw = g.DW;
+    a.oh = g.OH;
+    a.ow = g.OW;
+    a.M = g.N * g.OH * g.OW;
+    a.K = g.KH * g.KW * cpad;
+    a.wt = dw->w;
+    a.kpad = dw->kpad;
+    a.N = ocpad;
+    a.bias = B ? dw->b : nullptr;
+    a.res = rn;
+    a.ldr = ocpad;
+    a.y = yn;
+    a.ldy = ocpad;
+    a.act = g.act;
+    rc = tc_gemm_launch(a, st);
+  } else if (g.G == g.C && g.G == g.OC) {
+    rc = conv_weights(in[1], B, W_DW, g.C, cpad, g.OC, g.KH, g.KW, g.G, &dw);
+    if (rc) return rc;
+    rc = launch_depthwise_nhwc(xn, dw->w, dw->b, rn, yn, g.N, g.H, g.W, ocpad, g.OH, g.OW, g.KH, g.KW, g.SH, g.SW, g.PH,
+                               g.PW, g.DH, g.DW, g.act, 0, st);
+  } else {
+    rc = conv_weights(in[1], B, W_GROUPED, g.C, cpad, g.OC, g.KH, g.KW, g.G, &dw);
+    if (rc) return rc;
+    rc = launch_grouped_nhwc(xn, dw->w, B ? dw->b : nullptr, rn, yn, g.N, g.H, g.W, g.C, cpad, g.OH, g.OW, g.OC, ocpad,
+                             g.KH, g.KW, g.SH, g.SW, g.PH, g.PW, g.DH, g.DW, g.G, g.act, 0, st);
+  }
+  if (rc) return rc;
+  const bool dev_out = is_device_ptr(out[0]->data);
+  float* y = dev_out ? static_cast<float*>(out[0]->data) : scratch_take(yb);
+  rc = launch_nhwc_to_nchw(yn, y, g.N, g.OC, g.OH, g.OW, ocpad, st);
+  if (rc) return rc;
+  return finish_output(out[0], y, yb);
+}
+
+// Shared GEMM path: Y[M][N] = alpha * A[M][K] * Bt[N][K]^T + bias + res, all device pointers,
+// with A row-major (lda = K rounded to 4) and Bt K-major with kpad columns.
+static int gemm_core(const float* A, int lda, const float* Bt, int kpad, int M, int N, int K, float alpha,
+                     const float* bias, const float* res, float* Y, cudaStream_t st) {
+  const int Np = round4(N);
+  float* yt = Y;
+  if (Np != N) yt = scratch_take((size_t)M * Np * 4);
+  const float* rr = res;
+  if (res && Np != N) {
+    float* rt = scratch_take((size_t)M * Np * 4);
+    SPINN_CUDA_TRY(cudaMemset2DAsync(rt, (size_t)Np * 4, 0, (size_t)Np * 4, M, st));
+    SPINN_CUDA_TRY(cudaMemcpy2DAsync(rt, (size_t)Np * 4, res, (size_t)N * 4, (size_t)N * 4, M, cudaMemcpyDeviceToDevice, st));
+    rr = rt;
+  }
+  TcGemmArgs g;
+  g.a_mode = 1;
+  g.x = A;
+  g.M = M;
+  g.K = K;
+  g.lda = lda;
+  g.wt = Bt;
+  g.kpad = kpad;
+  g.N = Np;
+  g.bias = bias;
+  g.res = rr;
+  g.ldr = Np;
+  g.y = yt;
+  g.ldy = Np;
+  g.alpha = alpha;
+  int rc = tc_gemm_launch(g, st);
+  if (rc) return rc;
+  if (yt != Y)
+    SPINN_CUDA_TRY(cudaMemcpy2DAsync(Y, (size_t)N * 4, yt, (size_t)Np * 4, (size_t)N * 4, M, cudaMemcpyDeviceToDevice, st));
+  return 0;
+}
+
+// Row-major [rows][cols] device matrix re-pitched to [rows][ld] (ld >= cols, zero tail).
+static int repitch(const float* src, int rows, int cols, int ld, float** dst, cudaStream_t st) {
+  float* d = scratch_take((size_t)rows * ld * 4);
+  if (ld != cols) SPINN_CUDA_TRY(cudaMemsetAsync(d, 0, (size_t)rows * ld * 4, st));
+  SPINN_CUDA_TRY(cudaMemcpy2DAsync(d, (size_t)ld * 4, src, (size_t)cols * 4, (size_t)cols * 4, rows,
+                                   cudaMemcpyDeviceToDevice, st));
+  *dst = d;
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_gemm(SpinnTensor** in, int n_in, void* params,
+                                                           uint16_t params_size, SpinnTensor** out, int n_out) {
+  if (!in || !out || n_in < 2 || n_out < 1 || !in[0] || !in[1] || !out[0] || !in[0]->data || !in[1]->data ||
+      !out[0]->data) {
+    set_error("gemm: need A, B and Y with data");
+    return SPINN_CUDA_EINVAL;
+  }
+  int rc = ensure_session();
+  if (rc) return rc;
+  int transA = 0, transB = 0;
+  float alpha = 1.0f, beta = 1.0f;
+  if (params && params_size >= 12) {  // ENNF_GemmParams (SPINN/ennf_op_params.h:134-140)
+    std::memcpy(&alpha, params, 4);
+    std::memcpy(&beta, static_cast<uint8_t*>(params) + 4, 4);
+    transA = static_cast<uint8_t*>(params)[8];
+    transB = static_cast<uint8_t*>(params)[9];
+  }
+  const SpinnTensor *A = in[0], *Bt = in[1];
+  const SpinnTensor* Cb = (n_in > 2 && in[2] && in[2]->data) ? in[2] : nullptr;
+  SPINN_CHECK_ARG(A->ndim == 2 && Bt->ndim == 2, "gemm: A and B must be 2-D");
+  const int M = transA ? A->dims[1] : A->dims[0];
+  const int K = transA ? A->dims[0] : A->dims[1];
+  const int N = transB ? Bt->dims[0] : Bt->dims[1];
+  const int K2 = transB ? Bt->dims[1] : Bt->dims[0];
+  SPINN_CHECK_ARG(K == K2, "gemm: inner dimensions %d and %d differ", K, K2);
+  SPINN_CHECK_ARG(out[0]->elem_count == (uint32_t)M * N, "gemm: output has %u elements, expected %d", out[0]->elem_count,
+                  M * N);
+  const bool c_vec = Cb && Cb->elem_count == (uint32_t)N;
+  SPINN_CHECK_ARG(!Cb || c_vec || Cb->elem_count == (uint32_t)M * N, "gemm: C must have N or M*N elements");
+  const int Kp = round4(K), Np = round4(N), kpad = tc_num_kb(K) * 32;
+  const size_t ab = (size_t)M * K * 4, bb = (size_t)N * K * 4, yb = (size_t)M * N * 4;
+  rc = scratch_reserve(pad256(ab) * 2 + pad256((size_t)M * Kp * 4) + pad256(bb) * 2 + pad256((size_t)Np * kpad * 4) +
+                       pad256(yb) * 2 + 3 * pad256((size_t)M * Np * 4) + pad256((size_t)Np * 4) + 8192);
+  if (rc) return rc;
+  cudaStream_t st = g_sess.stream;
+  // A -> row-major [M][Kp]
+  const float* a;
+  rc = to_device(A, ab, &a);
+  if (rc) return rc;
+  const float* a_rm = a;
+  if (transA) {
+    float* t = scratch_take(ab);
+    rc = launch_transpose(a, t, 1, K, M, st);
+    if (rc) return rc;
+    a_rm = t;
+  }
+  float* a_use = const_cast<float*>(a_rm);
+  if (Kp != K) {
+    rc = repitch(a_rm, M, K, Kp, &a_use, st);
+    if (rc) return rc;
+  }
+  // B -> K-major [Np][kpad], tf32-rounded; cached when B is a weight
+  const float* bt = nullptr;
+  if (Bt->is_weight) {
+    Session& S = g_sess;
+    auto key = std::make_tuple((const void*)Bt->data, (uint64_t)Bt->elem_count, (int)W_GEMM_B, transB);
+    auto it = S.wcache.find(key);
+    if (it == S.wcache.end()) {
+      std::vector<float> hb;
+      rc = fetch_host(Bt, &hb);
+      if (rc) return rc;
+      std::vector<float> w((size_t)Np * kpad, 0.0f);
+      for (int n = 0; n < N; ++n)
+        for (int k = 0; k < K; ++k)
+          w[(size_t)n * kpad + k] = host_round_tf32(transB ? hb[(size_t)n * K + k] : hb[(size_t)k * N + n]);
+      DevWeight dw;
+      dw.kpad = kpad;
+      SPINN_CUDA_TRY(cudaMalloc(&dw.w, w.size() * 4));
+      SPINN_CUDA_TRY(cudaMemcpy(dw.w, w.data(), w.size() * 4, cudaMemcpyHostToDevice));
+      it = S.wcache.emplace(key, dw).first;
+    }
+    bt = it->second.w;
+  } else {
+    const float* b;
+    rc = to_device(Bt, bb, &b);
+    if (rc) return rc;
+    const float* b_nk = b;
+    if (!transB) {
+      float* t = scratch_take(bb);
+      rc = launch_transpose(b, t, 1, K, N, st);
+      if (rc) return rc;
+      b_nk = t;
+    }
+    float* bp = scratch_take((size_t)Np * kpad * 4);
+    SPINN_CUDA_TRY(cudaMemsetAsync(bp, 0, (size_t)Np * kpad * 4, st));
+    SPINN_CUDA_TRY(cudaMemcpy2DAsync(bp, (size_t)kpad * 4, b_nk, (size_t)K * 4, (size_t)K * 4, N,
+                                     cudaMemcpyDeviceToDevice, st));
+    rc = launch_round_tf32(bp, (long)Np * kpad, st);
+    if (rc) return rc;
+    bt = bp;
+  }
+  // C: beta*C as bias (vector) or residual (matrix)
+  const float* bias = nullptr;
+  const float* res = nullptr;
+  if (Cb && beta != 0.0f) {
+    std::vector<float> hc;
+    rc = fetch_host(Cb, &hc);
+    if (rc) return rc;
+    for (auto& v : hc) v *= beta;
+    if (c_vec) hc.resize(Np, 0.0f);  // the kernel reads bias for every padded column
+    float* d = scratch_take(hc.size() * 4);
+    SPINN_CUDA_TRY(cudaMemcpyAsync(d, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice, st));
+    SPINN_CUDA_TRY(cudaStreamSynchronize(st));  // hc is a temporary host buffer
+    if (c_vec)
+      bias = d;
+    else
+      res = d;
+  }
+  const bool dev_out = is_device_ptr(out[0]->data);
+  float* y = dev_out ? static_cast<float*>(out[0]->data) : scratch_take(yb);
+  rc = gemm_core(a_use, Kp, bt, kpad, M, N, K, alpha, bias, res, y, st);
+  if (rc) return rc;
+  return finish_output(out[0], y, yb);
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_matmul(SpinnTensor** in, int n_in, void* params,
+                                                             uint16_t params_size, SpinnTensor** out, int n_out) {
+  (void)params;
+  (void)params_size;
+  if (!in || !out || n_in < 2 || n_out < 1 || !in[0] || !in[1] || !out[0] || !in[0]->data || !in[1]->data ||
+      !out[0]->data) {
+    set_error("matmul: need A, B and Y with data");
+    return SPINN_CUDA_EINVAL;
+  }
+  int rc = ensure_session();
+  if (rc) return rc;
+  const SpinnTensor *A = in[0], *B = in[1];
+  SPINN_CHECK_ARG(A->ndim >= 2 && B->ndim >= 2, "matmul: operands must be at least 2-D");
+  const int M = A->dims[A->ndim - 2], K = A->dims[A->ndim - 1];
+  const int K2 = B->dims[B->ndim - 2], N = B->dims[B->ndim - 1];
+  SPINN_CHECK_ARG(K == K2, "matmul: inner dimensions %d and %d differ", K, K2);
+  long batch = 1, batch_b = 1;
+  for (int i = 0; i < A->ndim - 2; ++i) batch *= A->dims[i];
+  for (int i = 0; i < B->ndim - 2; ++i) batch_b *= B->dims[i];
+  SPINN_CHECK_ARG(batch_b == 1 || batch_b == batch, "matmul: batch counts %ld and %ld differ", batch, batch_b);
+  SPINN_CHECK_ARG(out[0]->elem_count == (uint64_t)batch * M * N, "matmul: output element count mismatch");
+  const int Kp = round4(K), Np = round4(N), kpad = tc_num_kb(K) * 32;
+  const size_t ab = (size_t)batch * M * K * 4, bb = (size_t)batch_b * K * N * 4, yb = (size_t)batch * M * N * 4;
+  rc = scratch_reserve(pad256(ab) + pad256((size_t)batch * M * Kp * 4) + 2 * pad256(bb) +
+                       pad256((size_t)batch_b * Np * kpad * 4) + pad256(yb) + 2 * pad256((size_t)M * Np * 4) + 8192);
+  if (rc) return rc;
+  cudaStream_t st = g_sess.stream;
+  const float* a;
+  rc = to_device(A, ab, &a);
+  if (rc) return rc;
+  float* a_use = const_cast<float*>(a);
+  if (Kp != K) {
+    rc = repitch(a, (int)(batch * M), K, Kp, &a_use, st);
+    if (rc) return rc;
+  }
+  const float* b;
+  rc = to_device(B, bb, &b);
+  if (rc) return rc;
+  float* bt = scratch_take(bb);
+  rc = launch_transpose(b, bt, (int)batch_b, K, N, st);  // [K][N] -> [N][K] per batch
+  if (rc) return rc;
+  float* bp = scratch_take((size_t)batch_b * Np * kpad * 4);
+  SPINN_CUDA_TRY(cudaMemsetAsync(bp, 0, (size_t)batch_b * Np * kpad * 4, st));
+  for (long i = 0; i < batch_b; ++i)
+    SPINN_CUDA_TRY(cudaMemcpy2DAsync(bp + (size_t)i * Np * kpad, (size_t)kpad * 4, bt + (size_t)i * N * K, (size_t)K * 4,
+                                     (size_t)K * 4, N, cudaMemcpyDeviceToDevice, st));
+  rc = launch_round_tf32(bp, (long)batch_b * Np * kpad, st);
+  if (rc) return rc;
+  const bool dev_out = is_device_ptr(out[0]->data);
+  float* y = dev_out ? static_cast<float*>(out[0]->data) : scratch_take(yb);
+  const size_t mark = g_sess.scratch_used;
+  for (long i = 0; i < batch; ++i) {
+    g_sess.scratch_used = mark;  // per-batch temporaries are reused
+    rc = gemm_core(a_use + (size_t)i * M * Kp, Kp, bp + (size_t)(batch_b == 1 ? 0 : i) * Np * kpad, kpad, M, N, K, 1.0f,
+                   nullptr, nullptr, y + (size_t)i * M * N, st);
+    if (rc) return rc;
+  }
+  return finish_output(out[0], y, yb);
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_register(int (*register_op)(uint16_t, SpinnOpKernel)) {
+  if (!register_op) {
+    set_error("spinn_cuda_register: null registrar");
+    return SPINN_CUDA_EINVAL;
+  }
+  int n = 0;
+  if (register_op(kOpConv, spinn_cuda_conv2d) == 0) ++n;
+  if (register_op(kOpGemm, spinn_cuda_gemm) == 0) ++n;
+  if (register_op(kOpMatMul, spinn_cuda_matmul) == 0) ++n;
+  return n;
+}
+
+}  // extern "C"
+}  // namespace spinn

@@ -1,0 +1,398 @@
+// glue.cu -- memory-bound kernels around the tensor-core path: NCHW<->NHWC layout
+// conversion, pooling, elementwise operators, depthwise / grouped direct convolution,
+// transposes.  All of them are HBM-bound; they move 16-byte vectors along the contiguous
+// channel dimension of NHWC tensors and size grids to fill every SM.
+//
+// Semantics follow the reference operators cited at each kernel; layouts are NHWC with the
+// channel dimension padded to `cpad` (a multiple of 4) where the tensor-core path needs it.
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace spinn {
+
+namespace {
+
+constexpr int kEltThreads = 256;
+
+inline int grid_for(long work, int threads, int max_blocks = 148 * 32) {
+  long b = (work + threads - 1) / threads;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return (int)b;
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == 1 || act == 5) return v < 0.0f ? 0.0f : v;
+  if (act == 3) return v / (1.0f + expf(-v));
+  return v;
+}
+
+// [n][c][hw] -> [n][hw][cpad] through a 32x33 shared tile; channels >= c are written as 0.
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int c, int hw, int cpad) {
+  __shared__ float tile[32][33];
+  const int n = blockIdx.z;
+  const int hw0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* xn = x + (size_t)n * c * hw;
+  float* yn = y + (size_t)n * hw * cpad;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int cc = c0 + i, p = hw0 + threadIdx.x;
+    tile[i][threadIdx.x] = (cc < c && p < hw) ? xn[(size_t)cc * hw + p] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int p = hw0 + i, cc = c0 + threadIdx.x;
+    if (p < hw && cc < cpad) yn[(size_t)p * cpad + cc] = tile[threadIdx.x][i];
+  }
+}
+
+__global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, float* __restrict__ y, int c, int hw, int cpad) {
+  __shared__ float tile[32][33];
+  const int n = blockIdx.z;
+  const int hw0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* xn = x + (size_t)n * hw * cpad;
+  float* yn = y + (size_t)n * c * hw;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int p = hw0 + i, cc = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (p < hw && cc < c) ? xn[(size_t)p * cpad + cc] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int cc = c0 + i, p = hw0 + threadIdx.x;
+    if (cc < c && p < hw) yn[(size_t)cc * hw + p] = tile[threadIdx.x][i];
+  }
+}
+
+// MaxPool (SPINN/run_time/ops/pool/maxpool.c:5-49): -1e30 start, padded taps skipped.
+__global__ void maxpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
+                                    int c4, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw) {
+  const long total = (long)n * oh * ow * c4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int cq = (int)(i % c4);
+    long t = i / c4;
+    const int ox = (int)(t % ow);
+    t /= ow;
+    const int oy = (int)(t % oh);
+    const int b = (int)(t / oh);
+    float4 m = make_float4(-1e30f, -1e30f, -1e30f, -1e30f);
+    for (int r = 0; r < kh; ++r) {
+      const int iy = oy * sh - ph + r;
+      if (iy < 0 || iy >= h) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int ix = ox * sw - pw + s;
+        if (ix < 0 || ix >= w) continue;
+        const float4 v = x[(((size_t)b * h + iy) * w + ix) * c4 + cq];
+        m.x = v.x > m.x ? v.x : m.x;
+        m.y = v.y > m.y ? v.y : m.y;
+        m.z = v.z > m.z ? v.z : m.z;
+        m.w = v.w > m.w ? v.w : m.w;
+      }
+    }
+    y[i] = m;
+  }
+}
+
+// AveragePool (SPINN/run_time/ops/pool/avgpool.c): divisor = window taps inside the image,
+// or the full window when count_include_pad.
+__global__ void avgpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
+                                    int c4, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw,
+                                    int include_pad) {
+  const long total = (long)n * oh * ow * c4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int cq = (int)(i % c4);
+    long t = i / c4;
+    const int ox = (int)(t % ow);
+    t /= ow;
+    const int oy = (int)(t % oh);
+    const int b = (int)(t / oh);
+    float4 acc = make_float4(0, 0, 0, 0);
+    int cnt = 0;
+    for (int r = 0; r < kh; ++r) {
+      const int iy = oy * sh - ph + r;
+      for (int s = 0; s < kw; ++s) {
+        const int ix = ox * sw - pw + s;
+        if (iy < 0 || iy >= h || ix < 0 || ix >= w) continue;
+        const float4 v = x[(((size_t)b * h + iy) * w + ix) * c4 + cq];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+        ++cnt;
+      }
+    }
+    const float d = include_pad ? (float)(kh * kw) : (float)(cnt > 0 ? cnt : 1);
+    y[i] = make_float4(acc.x / d, acc.y / d, acc.z / d, acc.w / d);
+  }
+}
+
+// GlobalAveragePool (SPINN/run_time/ops/pool/global_avg_pool.c:4-28): sequential fp32 sum
+// over the spatial positions in order, then one division -- the reference's exact order.
+__global__ void gap_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int n, int hw, int cpad) {
+  const long total = (long)n * cpad;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cpad);
+    const long b = i / cpad;
+    const float* p = x + (size_t)b * hw * cpad + c;
+    float s = 0.0f;
+    for (int k = 0; k < hw; ++k) s += p[(size_t)k * cpad];
+    y[i] = s / (float)hw;
+  }
+}
+
+__global__ void binary_kernel(const float* __restrict__ a, long na, const float* __restrict__ b, long nb,
+                              float* __restrict__ y, long n, int op, int act) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float u = a[na == n ? i : i % na], v = b[nb == n ? i : i % nb];
+    float r;
+    switch (op) {
+      case ELT_MUL: r = u * v; break;
+      case ELT_SUB: r = u - v; break;
+      case ELT_DIV: r = u / v; break;
+      default: r = u + v; break;
+    }
+    y[i] = act ? (r < 0.0f ? 0.0f : r) : r;
+  }
+}
+
+__global__ void unary_kernel(const float* __restrict__ x, float* __restrict__ y, long n, int op) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    float r;
+    switch (op) {
+      case UN_RELU: r = v > 0.0f ? v : 0.0f; break;
+      case UN_SIGMOID: r = 1.0f / (1.0f + expf(-v)); break;
+      case UN_SILU: r = v / (1.0f + expf(-v)); break;
+      default: r = v; break;
+    }
+    y[i] = r;
+  }
+}
+
+// op_batch_norm (SPINN/run_time/ops/norm/batch_norm.c:17-76) with precomputed scale/shift.
+__global__ void channel_affine_kernel(const float* __restrict__ x, float* __restrict__ y, long pixels, int cpad,
+                                      const float* __restrict__ scale, const float* __restrict__ shift) {
+  const long total = pixels * cpad;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cpad);
+    y[i] = fmaf(x[i], scale[c], shift[c]);
+  }
+}
+
+// Depthwise convolution, NHWC, four channels per thread (16-B loads along C).
+// w is [kh*kw][cpad]; bias [cpad]; residual NHWC like y.
+__global__ void depthwise_kernel(const float4* __restrict__ x, const float4* __restrict__ w,
+                                 const float4* __restrict__ bias, const float4* __restrict__ res,
+                                 float4* __restrict__ y, int n, int h, int wd, int c4, int oh, int ow, int kh, int kw,
+                                 int sh, int sw, int ph, int pw, int dh, int dw, int act, int round_out) {
+  const long total = (long)n * oh * ow * c4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int cq = (int)(i % c4);
+    long t = i / c4;
+    const int ox = (int)(t % ow);
+    t /= ow;
+    const int oy = (int)(t % oh);
+    const int b = (int)(t / oh);
+    float4 acc = make_float4(0, 0, 0, 0);
+    for (int r = 0; r < kh; ++r) {
+      const int iy = oy * sh - ph + r * dh;
+      if (iy < 0 || iy >= h) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int ix = ox * sw - pw + s * dw;
+        if (ix < 0 || ix >= wd) continue;
+        const float4 v = x[(((size_t)b * h + iy) * wd + ix) * c4 + cq];
+        const float4 k = w[(size_t)(r * kw + s) * c4 + cq];
+        acc.x = fmaf(v.x, k.x, acc.x);
+        acc.y = fmaf(v.y, k.y, acc.y);
+        acc.z = fmaf(v.z, k.z, acc.z);
+        acc.w = fmaf(v.w, k.w, acc.w);
+      }
+    }
+    if (bias) {
+      const float4 bb = bias[cq];
+      acc.x += bb.x;
+      acc.y += bb.y;
+      acc.z += bb.z;
+      acc.w += bb.w;
+    }
+    if (res && (act == 4 || act == 5)) {
+      const float4 rr = res[i];
+      acc.x += rr.x;
+      acc.y += rr.y;
+      acc.z += rr.z;
+      acc.w += rr.w;
+    }
+    acc.x = apply_act(acc.x, act);
+    acc.y = apply_act(acc.y, act);
+    acc.z = apply_act(acc.z, act);
+    acc.w = apply_act(acc.w, act);
+    if (round_out) {
+      acc.x = to_tf32_rna(acc.x);
+      acc.y = to_tf32_rna(acc.y);
+      acc.z = to_tf32_rna(acc.z);
+      acc.w = to_tf32_rna(acc.w);
+    }
+    y[i] = acc;
+  }
+}
+
+// Generic grouped direct convolution, NHWC, one output element per thread (CUDA cores).
+// w is [oc][kh][kw][c/group].
+__global__ void grouped_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               const float* __restrict__ bias, const float* __restrict__ res, float* __restrict__ y,
+                               int n, int h, int wd, int c, int cpad, int oh, int ow, int oc, int ocpad, int kh, int kw,
+                               int sh, int sw, int ph, int pw, int dh, int dw, int group, int act, int round_out) {
+  const int cg = c / group, ocg = oc / group;
+  const long total = (long)n * oh * ow * ocpad;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int o = (int)(i % ocpad);
+    long t = i / ocpad;
+    const int ox = (int)(t % ow);
+    t /= ow;
+    const int oy = (int)(t % oh);
+    const int b = (int)(t / oh);
+    if (o >= oc) {
+      y[i] = 0.0f;
+      continue;
+    }
+    const int g = o / ocg;
+    float acc = 0.0f;
+    for (int r = 0; r < kh; ++r) {
+      const int iy = oy * sh - ph + r * dh;
+      if (iy < 0 || iy >= h) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int ix = ox * sw - pw + s * dw;
+        if (ix < 0 || ix >= wd) continue;
+        const float* xp = x + (((size_t)b * h + iy) * wd + ix) * cpad + g * cg;
+        const float* wp = w + (((size_t)o * kh + r) * kw + s) * cg;
+        for (int k = 0; k < cg; ++k) acc = fmaf(xp[k], wp[k], acc);
+      }
+    }
+    if (bias) acc += bias[o];
+    if (res && (act == 4 || act == 5)) acc += res[i];
+    acc = apply_act(acc, act);
+    y[i] = round_out ? to_tf32_rna(acc) : acc;
+  }
+}
+
+__global__ void transpose_kernel(const float* __restrict__ x, float* __restrict__ y, int rows, int cols) {
+  __shared__ float tile[32][33];
+  const size_t off = (size_t)blockIdx.z * rows * cols;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, cc = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (r < rows && cc < cols) ? x[off + (size_t)r * cols + cc] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int cc = c0 + i, r = r0 + threadIdx.x;
+    if (cc < cols && r < rows) y[off + (size_t)cc * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+__global__ void round_tf32_kernel(float* x, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    x[i] = to_tf32_rna(x[i]);
+}
+
+}  // namespace
+
+#define SPINN_LAUNCH_CHECK()                                                        \
+  do {                                                                              \
+    cudaError_t e_ = cudaGetLastError();                                            \
+    if (e_ != cudaSuccess) {                                                        \
+      set_error("%s: launch failed: %s", __func__, cudaGetErrorString(e_));         \
+      return SPINN_CUDA_ECUDA;                                                      \
+    }                                                                               \
+    return 0;                                                                       \
+  } while (0)
+
+int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s) {
+  const int hw = h * w;
+  dim3 grid((hw + 31) / 32, (cpad + 31) / 32, n), block(32, 8);
+  nchw_to_nhwc_kernel<<<grid, block, 0, s>>>(x, y, c, hw, cpad);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_nhwc_to_nchw(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s) {
+  const int hw = h * w;
+  dim3 grid((hw + 31) / 32, (c + 31) / 32, n), block(32, 8);
+  nhwc_to_nchw_kernel<<<grid, block, 0, s>>>(x, y, c, hw, cpad);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh, int kw,
+                        int sh, int sw, int ph, int pw, cudaStream_t s) {
+  SPINN_CHECK_ARG(cpad % 4 == 0, "maxpool: channel stride %d not a multiple of 4", cpad);
+  const long work = (long)n * oh * ow * (cpad / 4);
+  maxpool_nhwc_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow, kh, kw, sh, sw, ph, pw);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_avgpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh, int kw,
+                        int sh, int sw, int ph, int pw, int count_include_pad, cudaStream_t s) {
+  SPINN_CHECK_ARG(cpad % 4 == 0, "avgpool: channel stride %d not a multiple of 4", cpad);
+  const long work = (long)n * oh * ow * (cpad / 4);
+  avgpool_nhwc_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow, kh, kw, sh, sw, ph, pw,
+      count_include_pad);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_gap_nhwc(const float* x, float* y, int n, int hw, int cpad, cudaStream_t s) {
+  const long work = (long)n * cpad;
+  gap_nhwc_kernel<<<grid_for(work, 128), 128, 0, s>>>(x, y, n, hw, cpad);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_binary(const float* a, long na, const float* b, long nb, float* y, long n, int op, int act, cudaStream_t s) {
+  SPINN_CHECK_ARG(na > 0 && nb > 0, "binary: empty operand");
+  binary_kernel<<<grid_for(n, kEltThreads), kEltThreads, 0, s>>>(a, na, b, nb, y, n, op, act);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_unary(const float* x, float* y, long n, int op, cudaStream_t s) {
+  unary_kernel<<<grid_for(n, kEltThreads), kEltThreads, 0, s>>>(x, y, n, op);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_channel_affine_nhwc(const float* x, float* y, long pixels, int cpad, const float* scale,
+                               const float* shift, cudaStream_t s) {
+  channel_affine_kernel<<<grid_for(pixels * cpad, kEltThreads), kEltThreads, 0, s>>>(x, y, pixels, cpad, scale, shift);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_depthwise_nhwc(const float* x, const float* w, const float* bias, const float* res, float* y, int n, int h,
+                          int wd, int cpad, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int dh,
+                          int dw, int act, int round_out, cudaStream_t s) {
+  SPINN_CHECK_ARG(cpad % 4 == 0, "depthwise: channel stride %d not a multiple of 4", cpad);
+  const long work = (long)n * oh * ow * (cpad / 4);
+  depthwise_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(w), reinterpret_cast<const float4*>(bias),
+      reinterpret_cast<const float4*>(res), reinterpret_cast<float4*>(y), n, h, wd, cpad / 4, oh, ow, kh, kw, sh, sw, ph,
+      pw, dh, dw, act, round_out);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_grouped_nhwc(const float* x, const float* w, const float* bias, const float* res, float* y, int n, int h,
+                        int wd, int c, int cpad, int oh, int ow, int oc, int ocpad, int kh, int kw, int sh, int sw,
+                        int ph, int pw, int dh, int dw, int group, int act, int round_out, cudaStream_t s) {
+  SPINN_CHECK_ARG(group >= 1 && c % group == 0 && oc % group == 0, "grouped conv: bad group %d", group);
+  const long work = (long)n * oh * ow * ocpad;
+  grouped_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(x, w, bias, res, y, n, h, wd, c, cpad, oh, ow, oc,
+                                                                    ocpad, kh, kw, sh, sw, ph, pw, dh, dw, group, act,
+                                                                    round_out);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_transpose(const float* x, float* y, int batch, int rows, int cols, cudaStream_t s) {
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32, batch), block(32, 8);
+  transpose_kernel<<<grid, block, 0, s>>>(x, y, rows, cols);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_round_tf32(float* x, long n, cudaStream_t s) {
+  round_tf32_kernel<<<grid_for(n, kEltThreads), kEltThreads, 0, s>>>(x, n);
+  SPINN_LAUNCH_CHECK();
+}
+
+}  // namespace spinn

@@ -1,0 +1,127 @@
+// internal.h -- declarations shared by the translation units of libspinn_cuda.so.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/spinn_cuda.h"
+
+namespace spinn {
+
+// ------------------------------------------------------------------ errors
+// Thread-local message of the last failure (spinn_cuda_last_error).
+void set_error(const char* fmt, ...);
+const char* get_error();
+
+#define SPINN_CUDA_TRY(expr)                                                                \
+  do {                                                                                      \
+    cudaError_t e_ = (expr);                                                                \
+    if (e_ != cudaSuccess) {                                                                \
+      ::spinn::set_error("%s:%d: %s: %s", __FILE__, __LINE__, #expr, cudaGetErrorString(e_)); \
+      return SPINN_CUDA_ECUDA;                                                              \
+    }                                                                                       \
+  } while (0)
+
+#define SPINN_CHECK_ARG(cond, ...)        \
+  do {                                    \
+    if (!(cond)) {                        \
+      ::spinn::set_error(__VA_ARGS__);    \
+      return SPINN_CUDA_EINVAL;           \
+    }                                     \
+  } while (0)
+
+// ------------------------------------------------------------------ tensor maps
+// Wrappers over cuTensorMapEncodeTiled / cuTensorMapEncodeIm2col obtained through
+// cudaGetDriverEntryPoint (no link-time dependency on libcuda).  fp32 only.
+int encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle swizzle);
+int encode_im2col_4d(CUtensorMap* map, const void* base, int n, int h, int w, int c,
+                     int lower_w, int lower_h, int upper_w, int upper_h, int channels_per_pixel,
+                     int pixels_per_column, int stride_w, int stride_h, CUtensorMapSwizzle swizzle);
+
+// Device properties cached per device.
+int sm_count(int device);
+
+// Device word that kernels set when a bounded wait expires (one per device).
+int* device_error_flag(int device);
+// Reads and clears the flag; SPINN_CUDA_ETIMEOUT if it was set.
+int check_device_error_flag(int device, cudaStream_t stream);
+
+// ------------------------------------------------------------------ tcgen05 GEMM / conv
+// Y[M][ldy] = epilogue( A * W^T ), W stored K-major [N][kpad].
+//   a_mode 0 (im2col): A is the implicit im2col matrix of an NHWC activation
+//     x[n][h][w][cpad] for a (kh,kw) filter with stride/pad/dilation; M = n*oh*ow and
+//     K index = ((r*kw)+s)*cpad + c.
+//   a_mode 1 (tiled): A is a row-major [M][lda] matrix, K columns.
+// Epilogue per element: v = alpha*acc + bias[col] (+ res[row][col]); act; optional tf32 RN.
+struct TcGemmArgs {
+  int a_mode = 0;
+  const float* x = nullptr;
+  int n = 0, h = 0, w = 0, cpad = 0;
+  int kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, oh = 0, ow = 0;
+  int M = 0, K = 0, lda = 0;
+  const float* wt = nullptr;
+  int kpad = 0;
+  int N = 0;
+  const float* bias = nullptr;
+  const float* res = nullptr;
+  int ldr = 0;
+  float* y = nullptr;
+  int ldy = 0;
+  float alpha = 1.0f;
+  int act = 0;
+  int round_out = 0;
+  int bn = 0;  // 0 = choose
+};
+// Checks whether the tcgen05 path accepts the problem (alignment, corner ranges ...).
+bool tc_gemm_supported(const TcGemmArgs& a, std::string* why);
+int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);
+// Number of K blocks (32 wide) and padded K the weight matrix must have.
+inline int tc_num_kb(int K) { return (K + 31) / 32; }
+
+// ------------------------------------------------------------------ glue kernels (glue.cu)
+int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s);
+int launch_nhwc_to_nchw(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s);
+int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh,
+                        int kw, int sh, int sw, int ph, int pw, cudaStream_t s);
+int launch_avgpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh,
+                        int kw, int sh, int sw, int ph, int pw, int count_include_pad, cudaStream_t s);
+int launch_gap_nhwc(const float* x, float* y, int n, int hw, int cpad, cudaStream_t s);
+// y = op(a, b) elementwise with modulo broadcast (SPINN/run_time/ops/math/add.c:4-22).
+enum EltOp { ELT_ADD = 0, ELT_MUL = 1, ELT_SUB = 2, ELT_DIV = 3 };
+int launch_binary(const float* a, long na, const float* b, long nb, float* y, long n, int op, int act,
+                  cudaStream_t s);
+enum UnaryOp { UN_RELU = 0, UN_SIGMOID = 1, UN_SILU = 2, UN_COPY = 3 };
+int launch_unary(const float* x, float* y, long n, int op, cudaStream_t s);
+// Per-channel affine on NHWC: y = x*scale[c] + shift[c] (standalone BatchNormalization).
+int launch_channel_affine_nhwc(const float* x, float* y, long pixels, int cpad, const float* scale,
+                               const float* shift, cudaStream_t s);
+// Depthwise (group == C == OC) and generic grouped direct convolution on NHWC, CUDA cores.
+// w layout: [kh*kw][oc] for depthwise; [oc][kh][kw][c/group] for grouped.
+int launch_depthwise_nhwc(const float* x, const float* w, const float* bias, const float* res, float* y,
+                          int n, int h, int wd, int cpad, int oh, int ow, int kh, int kw, int sh, int sw,
+                          int ph, int pw, int dh, int dw, int act, int round_out, cudaStream_t s);
+int launch_grouped_nhwc(const float* x, const float* w, const float* bias, const float* res, float* y,
+                        int n, int h, int wd, int c, int cpad, int oh, int ow, int oc, int ocpad, int kh,
+                        int kw, int sh, int sw, int ph, int pw, int dh, int dw, int group, int act,
+                        int round_out, cudaStream_t s);
+// Row-major transpose of `batch` matrices [rows][cols] -> [cols][rows].
+int launch_transpose(const float* x, float* y, int batch, int rows, int cols, cudaStream_t s);
+// tf32 round-to-nearest-away in place (weights).
+int launch_round_tf32(float* x, long n, cudaStream_t s);
+
+// Host-side tf32 RN (ties away), same rounding as cvt.rna.tf32.f32.
+inline float host_round_tf32(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+}  // namespace spinn

@@ -1,0 +1,1211 @@
+// runtime.cpp -- device-resident executor for .ennf models (load -> plan -> run).
+//
+// Mirrors the reference runtime's three stages (SPINN/run_time/spinn_runtime.c: spinn_load
+// :21-124, spinn_plan :129-155, spinn_run :298-355) with every node on the GPU:
+//
+//  * load: parses the ENNF v2 image (header, dense WeightEntry table at header.reserved[0],
+//    graph meta, node table, tensor meta; SPINN/ennf_def.h) into host tables.
+//  * plan: assigns each activation a device layout (NHWC with the channel dimension padded
+//    to a multiple of 4 for everything that feeds a convolution, row-major otherwise),
+//    inserts the NCHW<->NHWC conversions at the graph edges, pre-transforms weights once
+//    (K-major, tap-major, tf32-rounded; transposed Gemm operands; depthwise tap-major),
+//    and packs every activation into ONE device arena with the reference planner's
+//    best-fit/free-at-last-use algorithm (spinn_memory_planner.c:56-241) but 64-bit
+//    offsets and 256-B alignment -- the reference clamps the arena to INT_MAX
+//    (spinn_memory_planner.c:251) and stores 32-bit offsets (spinn_runtime.h:36-37).
+//  * run: input H2D, the compiled step list (captured once into a CUDA graph), output D2H.
+//
+// Unlike the reference dispatcher (spinn_ops.c:224-226), an operator without a device
+// implementation fails the plan instead of being skipped.
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <functional>
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "internal.h"
+
+namespace spinn {
+
+// ------------------------------------------------------------------ ENNF constants
+enum : uint16_t {
+  OP_ADD = 4, OP_DIV = 23, OP_MUL = 39, OP_SUB = 50, OP_CONV = 60, OP_AVGPOOL = 80, OP_GAP = 81, OP_MAXPOOL = 85,
+  OP_BN = 100, OP_RELU = 130, OP_SIGMOID = 133, OP_GEMM = 160, OP_MATMUL = 161, OP_FLATTEN = 189,
+  OP_IDENTITY = 193, OP_RESHAPE = 197
+};
+constexpr uint32_t kMagic = 0x454E4E46;
+
+#pragma pack(push, 1)
+struct EnnfHeader {  // SPINN/ennf_def.h:70-95
+  uint32_t magic;
+  uint16_t vmaj, vmin;
+  uint32_t num_nodes, num_tensors, num_weights, total_weight_bytes;
+  uint16_t num_inputs, num_outputs, opset, flags;
+  uint32_t graph_meta_offset, node_table_offset, tensor_meta_offset, weight_data_offset, string_table_offset;
+  uint32_t reserved[3];
+};
+#pragma pack(pop)
+static_assert(sizeof(EnnfHeader) == 64, "ENNF header is 64 bytes");
+
+struct EnnfMeta {  // SPINN/ennf_def.h:130-139 as compiled (44 bytes)
+  uint16_t tensor_id;
+  uint8_t dtype, ndim;
+  uint32_t dims[8];
+  uint32_t elem_count;
+  uint8_t is_weight, ref_count, pad[2];
+};
+static_assert(sizeof(EnnfMeta) == 44, "ENNF tensor meta is 44 bytes");
+
+struct ConvParams {  // SPINN/ennf_op_params.h:23-31
+  uint16_t kernel_shape[4], strides[4], pads[8], dilations[4], group;
+  uint8_t auto_pad, fused_act;
+};
+static_assert(sizeof(ConvParams) == 44, "ENNF_ConvParams is 44 bytes");
+struct PoolParams {  // ennf_op_params.h:45-56
+  uint16_t kernel_shape[4], strides[4], pads[8], dilations[4];
+  uint8_t auto_pad, ceil_mode, count_include_pad, storage_order;
+  int32_t p;
+};
+static_assert(sizeof(PoolParams) == 48, "ENNF_PoolParams is 48 bytes");
+struct GemmParams {  // ennf_op_params.h:134-140
+  float alpha, beta;
+  uint8_t transA, transB, reserved[2];
+};
+struct BnParams {
+  float epsilon, momentum;
+  uint8_t training_mode, reserved[3];
+};
+
+}  // namespace spinn
+
+using namespace spinn;
+
+struct TensorRec {
+  uint16_t id = 0;
+  uint8_t dtype = 0, ndim = 0;
+  uint32_t dims[8] = {0};
+  uint64_t elems = 0;
+  bool is_weight = false;
+  const float* host = nullptr;  // weights: into the file image
+  uint64_t host_bytes = 0;
+};
+
+struct NodeRec {
+  uint16_t op = 0;
+  uint8_t flags = 0;
+  std::vector<uint16_t> in, out;
+  std::vector<uint8_t> params;
+};
+
+enum Layout { LAY_NONE = 0, LAY_ROW = 1, LAY_NHWC = 2 };
+
+struct Buf {
+  Layout lay = LAY_NONE;
+  int n = 0, c = 0, h = 0, w = 0, cpad = 0;  // NHWC geometry
+  uint64_t bytes = 0;
+  int alias = -1;          // storage shared with this buffer index (resolved to a root)
+  int external = 0;        // 1: lives outside the arena (graph input/output staging)
+  int64_t offset = -1;
+  float* ptr = nullptr;
+  int first = -1, last = -1;  // step interval of use
+};
+
+struct StepRec {
+  int kind = 0;
+  int node = -1;
+  uint16_t op = 0;
+  double flops = 0;
+  std::function<int(cudaStream_t)> run;
+};
+
+struct SpinnCudaModel {
+  std::vector<uint8_t> image;
+  EnnfHeader hdr{};
+  std::vector<TensorRec> tensors;
+  std::vector<NodeRec> nodes;
+  std::vector<uint16_t> inputs, outputs;
+  // plan
+  bool planned = false;
+  int device = -1;
+  int flags = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<Buf> bufs;           // [0, num_tensors) = ENNF tensors, then temporaries
+  std::vector<int> in_buf, out_buf;  // NCHW staging buffer per graph input / output
+  uint8_t* arena = nullptr;
+  uint64_t arena_bytes = 0;
+  float* wdev = nullptr;
+  uint64_t wbytes = 0;
+  std::vector<float> whost;        // pre-transformed weights before upload
+  std::vector<StepRec> steps;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+  std::vector<cudaEvent_t> events;
+  std::vector<float> step_ms;
+  int kernels = 0;
+};
+
+namespace spinn {
+namespace {
+
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+int round4(int c) { return (c + 3) & ~3; }
+
+// ------------------------------------------------------------------ load
+int parse_image(SpinnCudaModel* m) {
+  const auto& img = m->image;
+  auto need = [&](uint64_t off, uint64_t len) { return off + len <= img.size(); };
+  if (!need(0, sizeof(EnnfHeader))) {
+    set_error("ennf: image shorter than the header");
+    return SPINN_CUDA_EFORMAT;
+  }
+  std::memcpy(&m->hdr, img.data(), sizeof(EnnfHeader));
+  const EnnfHeader& h = m->hdr;
+  if (h.magic != kMagic) {
+    set_error("ennf: bad magic 0x%08x", h.magic);
+    return SPINN_CUDA_EFORMAT;
+  }
+  if (h.num_tensors == 0 || h.num_tensors > 65536 || h.num_nodes > 1000000) {
+    set_error("ennf: implausible counts (%u tensors, %u nodes)", h.num_tensors, h.num_nodes);
+    return SPINN_CUDA_EFORMAT;
+  }
+  // graph meta
+  uint64_t p = h.graph_meta_offset;
+  auto rd16 = [&](uint16_t* v) {
+    if (!need(p, 2)) return false;
+    std::memcpy(v, img.data() + p, 2);
+    p += 2;
+    return true;
+  };
+  uint16_t ni = 0, no = 0, v = 0;
+  if (!rd16(&ni)) goto bad;
+  for (int i = 0; i < ni; ++i) {
+    if (!rd16(&v)) goto bad;
+    m->inputs.push_back(v);
+  }
+  if (!rd16(&no)) goto bad;
+  for (int i = 0; i < no; ++i) {
+    if (!rd16(&v)) goto bad;
+    m->outputs.push_back(v);
+  }
+  // tensor meta
+  m->tensors.resize(h.num_tensors);
+  for (uint32_t i = 0; i < h.num_tensors; ++i) {
+    const uint64_t off = (uint64_t)h.tensor_meta_offset + (uint64_t)i * sizeof(EnnfMeta);
+    if (!need(off, sizeof(EnnfMeta))) goto bad;
+    EnnfMeta mt;
+    std::memcpy(&mt, img.data() + off, sizeof(mt));
+    if (mt.tensor_id >= h.num_tensors || mt.ndim > 8) goto bad;
+    TensorRec& t = m->tensors[mt.tensor_id];
+    t.id = mt.tensor_id;
+    t.dtype = mt.dtype;
+    t.ndim = mt.ndim;
+    std::memcpy(t.dims, mt.dims, sizeof(t.dims));
+    t.elems = 1;
+    for (int d = 0; d < mt.ndim; ++d) t.elems *= mt.dims[d];
+    t.is_weight = mt.is_weight != 0;
+  }
+  // weights (dense entry table, SPINN/run_time/spinn_runtime.c:363-407)
+  for (uint32_t i = 0; i < h.num_tensors; ++i) {
+    TensorRec& t = m->tensors[i];
+    if (!t.is_weight) continue;
+    const uint64_t eoff = (uint64_t)h.reserved[0] + (uint64_t)i * 16;
+    if (!need(eoff, 16)) goto bad;
+    uint32_t doff = 0, dsize = 0;
+    std::memcpy(&doff, img.data() + eoff + 4, 4);
+    std::memcpy(&dsize, img.data() + eoff + 8, 4);
+    if (dsize == 0) continue;
+    const uint64_t woff = (uint64_t)h.weight_data_offset + doff;
+    if (!need(woff, dsize) || (woff & 3)) goto bad;
+    t.host = reinterpret_cast<const float*>(img.data() + woff);
+    t.host_bytes = dsize;
+  }
+  // nodes
+  p = h.node_table_offset;
+  for (uint32_t i = 0; i < h.num_nodes; ++i) {
+    if (!need(p, 8)) goto bad;
+    NodeRec n;
+    const uint8_t* b = img.data() + p;
+    std::memcpy(&n.op, b, 2);
+    const uint8_t nin = b[2], nout = b[3];
+    uint16_t psz;
+    std::memcpy(&psz, b + 4, 2);
+    n.flags = b[6];
+    p += 8;
+    for (int k = 0; k < nin; ++k) {
+      if (!rd16(&v) || v >= h.num_tensors) goto bad;
+      n.in.push_back(v);
+    }
+    for (int k = 0; k < nout; ++k) {
+      if (!rd16(&v) || v >= h.num_tensors) goto bad;
+      n.out.push_back(v);
+    }
+    if (!need(p, psz)) goto bad;
+    n.params.assign(img.data() + p, img.data() + p + psz);
+    p += psz;
+    m->nodes.push_back(std::move(n));
+  }
+  for (auto id : m->inputs)
+    if (id >= h.num_tensors) goto bad;
+  for (auto id : m->outputs)
+    if (id >= h.num_tensors) goto bad;
+  return 0;
+bad:
+  set_error("ennf: truncated or inconsistent image");
+  return SPINN_CUDA_EFORMAT;
+}
+
+// ------------------------------------------------------------------ plan helpers
+struct Planner {
+  SpinnCudaModel* m;
+  int round_out;
+  explicit Planner(SpinnCudaModel* mm) : m(mm), round_out(!(mm->flags & SPINN_CUDA_PLAN_NO_ROUND)) {}
+
+  int new_buf(const Buf& b) {
+    m->bufs.push_back(b);
+    return (int)m->bufs.size() - 1;
+  }
+  int root(int b) const {
+    while (m->bufs[b].alias >= 0) b = m->bufs[b].alias;
+    return b;
+  }
+  void touch(int b, int step) {
+    b = root(b);
+    Buf& x = m->bufs[b];
+    if (x.first < 0 || step < x.first) x.first = step;
+    if (step > x.last) x.last = step;
+  }
+  const TensorRec& T(int id) const { return m->tensors[id]; }
+
+  // weight staging: returns element offset into whost (256-B aligned)
+  uint64_t wreserve(uint64_t elems) {
+    uint64_t off = align_up(m->whost.size(), 64);
+    m->whost.resize(off + elems, 0.0f);
+    return off;
+  }
+};
+
+// NHWC geometry of a 4-D tensor id.
+void set_nhwc(Buf& b, const TensorRec& t) {
+  b.lay = LAY_NHWC;
+  b.n = t.dims[0];
+  b.c = t.dims[1];
+  b.h = t.dims[2];
+  b.w = t.dims[3];
+  b.cpad = round4(b.c);
+  b.bytes = (uint64_t)b.n * b.h * b.w * b.cpad * 4;
+}
+void set_row(Buf& b, const TensorRec& t) {
+  b.lay = LAY_ROW;
+  b.bytes = t.elems * 4;
+}
+
+// Best-fit allocation over the step intervals (reference algorithm, 64-bit).
+int plan_arena(SpinnCudaModel* m, int nsteps, uint64_t budget) {
+  struct Blk {
+    uint64_t off, size;
+  };
+  std::vector<Blk> freel{{0, budget ? budget : ~0ull >> 1}};
+  uint64_t peak = 0;
+  std::vector<std::vector<int>> born(nsteps + 1), dies(nsteps + 1);
+  for (int i = 0; i < (int)m->bufs.size(); ++i) {
+    Buf& b = m->bufs[i];
+    if (b.alias >= 0 || b.external || b.bytes == 0 || b.first < 0) continue;
+    born[b.first].push_back(i);
+    dies[b.last].push_back(i);
+  }
+  auto alloc = [&](uint64_t size, uint64_t* off) {
+    size = align_up(size, 256);
+    int best = -1;
+    for (int k = 0; k < (int)freel.size(); ++k)
+      if (freel[k].size >= size && (best < 0 || freel[k].size < freel[best].size)) best = k;
+    if (best < 0) return false;
+    *off = freel[best].off;
+    if (freel[best].size == size)
+      freel.erase(freel.begin() + best);
+    else {
+      freel[best].off += size;
+      freel[best].size -= size;
+    }
+    return true;
+  };
+  auto release = [&](uint64_t off, uint64_t size) {
+    size = align_up(size, 256);
+    auto it = std::lower_bound(freel.begin(), freel.end(), off, [](const Blk& b, uint64_t o) { return b.off < o; });
+    it = freel.insert(it, Blk{off, size});
+    size_t k = it - freel.begin();
+    if (k + 1 < freel.size() && freel[k].off + freel[k].size == freel[k + 1].off) {
+      freel[k].size += freel[k + 1].size;
+      freel.erase(freel.begin() + k + 1);
+    }
+    if (k > 0 && freel[k - 1].off + freel[k - 1].size == freel[k].off) {
+      freel[k - 1].size += freel[k].size;
+      freel.erase(freel.begin() + k);
+    }
+  };
+  for (int s = 0; s <= nsteps; ++s) {
+    for (int i : born[s]) {
+      uint64_t off;
+      if (!alloc(m->bufs[i].bytes, &off)) {
+        set_error("plan: arena budget %llu bytes exceeded", (unsigned long long)budget);
+        return SPINN_CUDA_ENOMEM;
+      }
+      m->bufs[i].offset = (int64_t)off;
+      peak = std::max(peak, off + align_up(m->bufs[i].bytes, 256));
+    }
+    for (int i : dies[s]) release(m->bufs[i].offset, m->bufs[i].bytes);
+  }
+  m->arena_bytes = peak;
+  return 0;
+}
+
+double conv_flops(const TensorRec& w, const TensorRec& y) {
+  // 2 * N*OC*OH*OW * (C/g)*KH*KW
+  return 2.0 * (double)y.elems * w.dims[1] * w.dims[2] * w.dims[3];
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ plan
+static int compile_model(SpinnCudaModel* m, uint64_t budget) {
+  Planner P(m);
+  const int nt = (int)m->tensors.size();
+  m->bufs.assign(nt, Buf());
+  std::vector<int> produced(nt, 0);
+  int step = 0;
+  // pass-1 records: lambdas that build the closure once pointers are known
+  std::vector<std::function<int(StepRec&)>> builders;
+
+  auto add_step = [&](int node, uint16_t op, int kind, double flops, std::function<int(StepRec&)> b) {
+    StepRec s;
+    s.node = node;
+    s.op = op;
+    s.kind = kind;
+    s.flops = flops;
+    m->steps.push_back(std::move(s));
+    builders.push_back(std::move(b));
+    return step++;
+  };
+
+  // graph inputs: NCHW staging (external); 4-D inputs get an NHWC arena copy
+  for (size_t i = 0; i < m->inputs.size(); ++i) {
+    const int id = m->inputs[i];
+    const TensorRec& t = m->tensors[id];
+    Buf st;
+    st.lay = LAY_ROW;
+    st.bytes = t.elems * 4;
+    st.external = 1;
+    const int sb = P.new_buf(st);
+    m->in_buf.push_back(sb);
+    if (t.ndim == 4) {
+      set_nhwc(m->bufs[id], t);
+      const int s = add_step(-1, 0, 7, 0, [m, sb, id](StepRec& r) {
+        const Buf& x = m->bufs[sb];
+        const Buf& y = m->bufs[id];
+        r.run = [&x, &y](cudaStream_t st) { return launch_nchw_to_nhwc(x.ptr, y.ptr, y.n, y.c, y.h, y.w, y.cpad, st); };
+        return 0;
+      });
+      P.touch(id, s);
+    } else {
+      m->bufs[id] = m->bufs[sb];
+      m->bufs[id].external = 0;
+      m->bufs[id].alias = sb;
+    }
+    produced[id] = 1;
+  }
+
+  auto ensure_nhwc = [&](int id, int node) -> int {
+    // returns a buffer index holding tensor `id` in NHWC layout
+    Buf& b = m->bufs[id];
+    if (b.lay == LAY_NHWC) return id;
+    const TensorRec& t = m->tensors[id];
+    if (t.ndim != 4) return -1;
+    Buf nb;
+    set_nhwc(nb, t);
+    const int tb = P.new_buf(nb);
+    const int s = add_step(node, 0, 7, 0, [m, id, tb](StepRec& r) {
+      const Buf& x = m->bufs[id];
+      const Buf& y = m->bufs[tb];
+      r.run = [&x, &y](cudaStream_t st) { return launch_nchw_to_nhwc(x.ptr, y.ptr, y.n, y.c, y.h, y.w, y.cpad, st); };
+      return 0;
+    });
+    P.touch(id, s);
+    P.touch(tb, s);
+    return tb;
+  };
+  auto ensure_row = [&](int id, int node) -> int {
+    Buf& b = m->bufs[id];
+    if (b.lay == LAY_ROW) return id;
+    const TensorRec& t = m->tensors[id];
+    Buf nb;
+    set_row(nb, t);
+    const int tb = P.new_buf(nb);
+    const int s = add_step(node, 0, 7, 0, [m, id, tb](StepRec& r) {
+      const Buf& x = m->bufs[id];
+      const Buf& y = m->bufs[tb];
+      r.run = [&x, &y](cudaStream_t st) { return launch_nhwc_to_nchw(x.ptr, y.ptr, x.n, x.c, x.h, x.w, x.cpad, st); };
+      return 0;
+    });
+    P.touch(id, s);
+    P.touch(tb, s);
+    return tb;
+  };
+
+  for (int ni = 0; ni < (int)m->nodes.size(); ++ni) {
+    const NodeRec& nd = m->nodes[ni];
+    for (auto id : nd.in) {
+      const TensorRec& t = m->tensors[id];
+      if (!t.is_weight && !produced[id] && t.elems > 0) {
+        set_error("plan: node %d (op %d) reads tensor %d before it is produced", ni, nd.op, id);
+        return SPINN_CUDA_EFORMAT;
+      }
+    }
+    switch (nd.op) {
+      case OP_CONV: {
+        if (nd.in.size() < 2 || nd.out.empty()) {
+          set_error("plan: Conv node %d has too few inputs", ni);
+          return SPINN_CUDA_EFORMAT;
+        }
+        ConvParams cp{};
+        if (nd.params.size() >= sizeof(ConvParams)) std::memcpy(&cp, nd.params.data(), sizeof(cp));
+        const int act = cp.fused_act;
+        const bool has_res = act == 4 || act == 5;
+        const int n_real = has_res ? (int)nd.in.size() - 1 : (int)nd.in.size();
+        const TensorRec& X = m->tensors[nd.in[0]];
+        const TensorRec& W = m->tensors[nd.in[1]];
+        const TensorRec& Y = m->tensors[nd.out[0]];
+        if (X.ndim != 4 || W.ndim != 4 || Y.ndim != 4 || !W.host) {
+          set_error("plan: Conv node %d needs 4-D X/W/Y and constant weights", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int N = X.dims[0], C = X.dims[1], H = X.dims[2], Wd = X.dims[3];
+        const int OC = W.dims[0], KC = W.dims[1];
+        int KH = W.dims[2], KW = W.dims[3], SH = 1, SW = 1, PH = 0, PW = 0, DH = 1, DW = 1, G = 1;
+        if (nd.params.size() >= sizeof(ConvParams)) {
+          if (cp.group > 0) G = cp.group;
+          if (cp.kernel_shape[0]) KH = cp.kernel_shape[0];
+          if (cp.kernel_shape[1]) KW = cp.kernel_shape[1];
+          if (cp.strides[0]) SH = cp.strides[0];
+          if (cp.strides[1]) SW = cp.strides[1];
+          if (cp.dilations[0]) DH = cp.dilations[0];
+          if (cp.dilations[1]) DW = cp.dilations[1];
+          PH = cp.pads[0];
+          PW = cp.pads[1];
+          if (cp.auto_pad == 1 || cp.auto_pad == 2) {  // SAME (conv2d.c:134-141)
+            int ph = ((int)Y.dims[2] - 1) * SH + KH - H;
+            if (ph < 0) ph = 0;
+            int pw = ((int)Y.dims[3] - 1) * SW + KW - Wd;
+            if (pw < 0) pw = 0;
+            PH = cp.auto_pad == 1 ? ph / 2 : (ph + 1) / 2;
+            PW = cp.auto_pad == 1 ? pw / 2 : (pw + 1) / 2;
+          }
+        }
+        const int OH = Y.dims[2], OW = Y.dims[3];
+        if ((int)Y.dims[1] != OC || (int)Y.dims[0] != N || C != KC * G || OC % G) {
+          set_error("plan: Conv node %d shape mismatch", ni);
+          return SPINN_CUDA_EFORMAT;
+        }
+        const int xb = ensure_nhwc(nd.in[0], ni);
+        int rb = -1;
+        if (has_res) {
+          rb = ensure_nhwc(nd.in.back(), ni);
+          if (rb < 0) {
+            set_error("plan: Conv node %d residual is not 4-D", ni);
+            return SPINN_CUDA_EUNSUPPORTED;
+          }
+        }
+        const int yb = nd.out[0];
+        set_nhwc(m->bufs[yb], Y);
+        const int cpad = round4(C), ocpad = round4(OC);
+        const TensorRec* B = (n_real > 2 && m->tensors[nd.in[2]].host) ? &m->tensors[nd.in[2]] : nullptr;
+        const double fl = conv_flops(W, Y);
+        const int rnd = P.round_out;
+        if (G == 1) {
+          // tcgen05 implicit GEMM: weights [ocpad][kpad], k = (r*KW + s)*cpad + c
+          const int K = KH * KW * cpad;
+          const int kpad = tc_num_kb(K) * 32;
+          const uint64_t woff = P.wreserve((uint64_t)ocpad * kpad);
+          for (int o = 0; o < OC; ++o)
+            for (int c = 0; c < C; ++c)
+              for (int r = 0; r < KH; ++r)
+                for (int s = 0; s < KW; ++s)
+                  m->whost[woff + (uint64_t)o * kpad + (r * KW + s) * cpad + c] =
+                      host_round_tf32(W.host[(((uint64_t)o * C + c) * KH + r) * KW + s]);
+          uint64_t boff = ~0ull;
+          if (B) {
+            boff = P.wreserve(ocpad);
+            for (int o = 0; o < OC; ++o) m->whost[boff + o] = B->host[o];
+          }
+          const int s = add_step(ni, OP_CONV, 1, fl, [=](StepRec& r) {
+            TcGemmArgs a;
+            a.a_mode = 0;
+            a.n = N;
+            a.h = H;
+            a.w = Wd;
+            a.cpad = cpad;
+            a.kh = KH;
+            a.kw = KW;
+            a.sh = SH;
+            a.sw = SW;
+            a.ph = PH;
+            a.pw = PW;
+            a.dh = DH;
+            a.dw = DW;
+            a.oh = OH;
+            a.ow = OW;
+            a.M = N * OH * OW;
+            a.K = KH * KW * cpad;
+            a.kpad = kpad;
+            a.N = ocpad;
+            a.ldy = ocpad;
+            a.ldr = ocpad;
+            a.act = act;
+            a.round_out = rnd;
+            const Buf* xbp = &m->bufs[xb];
+            const Buf* ybp = &m->bufs[yb];
+            const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
+            r.run = [m, a, xbp, ybp, rbp, woff, boff](cudaStream_t st) mutable {
+              a.x = xbp->ptr;
+              a.y = ybp->ptr;
+              a.res = rbp ? rbp->ptr : nullptr;
+              a.wt = m->wdev + woff;
+              a.bias = boff != ~0ull ? m->wdev + boff : nullptr;
+              return tc_gemm_launch(a, st);
+            };
+            return 0;
+          });
+          P.touch(xb, s);
+          P.touch(yb, s);
+          if (rb >= 0) P.touch(rb, s);
+        } else if (G == C && G == OC) {
+          // depthwise: weights [KH*KW][ocpad]
+          const uint64_t woff = P.wreserve((uint64_t)KH * KW * ocpad);
+          for (int o = 0; o < OC; ++o)
+            for (int t = 0; t < KH * KW; ++t) m->whost[woff + (uint64_t)t * ocpad + o] = W.host[(uint64_t)o * KH * KW + t];
+          const uint64_t boff = P.wreserve(ocpad);
+          if (B)
+            for (int o = 0; o < OC; ++o) m->whost[boff + o] = B->host[o];
+          const int s = add_step(ni, OP_CONV, 3, fl, [=](StepRec& r) {
+            const Buf* xbp = &m->bufs[xb];
+            const Buf* ybp = &m->bufs[yb];
+            const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
+            r.run = [=](cudaStream_t st) {
+              return launch_depthwise_nhwc(xbp->ptr, m->wdev + woff, m->wdev + boff, rbp ? rbp->ptr : nullptr, ybp->ptr,
+                                           N, H, Wd, ocpad, OH, OW, KH, KW, SH, SW, PH, PW, DH, DW, act, rnd, st);
+            };
+            return 0;
+          });
+          P.touch(xb, s);
+          P.touch(yb, s);
+          if (rb >= 0) P.touch(rb, s);
+        } else {
+          const int cg = C / G;
+          const uint64_t woff = P.wreserve((uint64_t)OC * KH * KW * cg);
+          for (int o = 0; o < OC; ++o)
+            for (int c = 0; c < cg; ++c)
+              for (int r = 0; r < KH; ++r)
+                for (int s = 0; s < KW; ++s)
+                  m->whost[woff + (((uint64_t)o * KH + r) * KW + s) * cg + c] = W.host[(((uint64_t)o * cg + c) * KH + r) * KW + s];
+          uint64_t boff = ~0ull;
+          if (B) {
+            boff = P.wreserve(ocpad);
+            for (int o = 0; o < OC; ++o) m->whost[boff + o] = B->host[o];
+          }
+          const int s = add_step(ni, OP_CONV, 4, fl, [=](StepRec& r) {
+            const Buf* xbp = &m->bufs[xb];
+            const Buf* ybp = &m->bufs[yb];
+            const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
+            r.run = [=](cudaStream_t st) {
+              return launch_grouped_nhwc(xbp->ptr, m->wdev + woff, boff != ~0ull ? m->wdev + boff : nullptr,
+                                         rbp ? rbp->ptr : nullptr, ybp->ptr, N, H, Wd, C, cpad, OH, OW, OC, ocpad, KH,
+                                         KW, SH, SW, PH, PW, DH, DW, G, act, rnd, st);
+            };
+            return 0;
+          });
+          P.touch(xb, s);
+          P.touch(yb, s);
+          if (rb >= 0) P.touch(rb, s);
+        }
+        produced[yb] = 1;
+        break;
+      }
+      case OP_MAXPOOL:
+      case OP_AVGPOOL: {
+        PoolParams pp{};
+        if (nd.params.size() >= sizeof(PoolParams)) std::memcpy(&pp, nd.params.data(), sizeof(pp));
+        const TensorRec& X = m->tensors[nd.in[0]];
+        const TensorRec& Y = m->tensors[nd.out[0]];
+        if (X.ndim != 4 || Y.ndim != 4) {
+          set_error("plan: pool node %d needs 4-D tensors", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int xb = ensure_nhwc(nd.in[0], ni);
+        const int yb = nd.out[0];
+        set_nhwc(m->bufs[yb], Y);
+        const int KH = pp.kernel_shape[0] ? pp.kernel_shape[0] : 1, KW = pp.kernel_shape[1] ? pp.kernel_shape[1] : 1;
+        const int SH = pp.strides[0] ? pp.strides[0] : 1, SW = pp.strides[1] ? pp.strides[1] : 1;
+        const int PH = pp.pads[0], PW = pp.pads[1], cip = pp.count_include_pad;
+        const bool is_max = nd.op == OP_MAXPOOL;
+        const int s = add_step(ni, nd.op, 5, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[xb];
+          const Buf* y = &m->bufs[yb];
+          r.run = [=](cudaStream_t st) {
+            return is_max ? launch_maxpool_nhwc(x->ptr, y->ptr, x->n, x->h, x->w, x->cpad, y->h, y->w, KH, KW, SH, SW,
+                                                PH, PW, st)
+                          : launch_avgpool_nhwc(x->ptr, y->ptr, x->n, x->h, x->w, x->cpad, y->h, y->w, KH, KW, SH, SW,
+                                                PH, PW, cip, st);
+          };
+          return 0;
+        });
+        P.touch(xb, s);
+        P.touch(yb, s);
+        produced[yb] = 1;
+        break;
+      }
+      case OP_GAP: {
+        const TensorRec& Y = m->tensors[nd.out[0]];
+        const int xb = ensure_nhwc(nd.in[0], ni);
+        if (xb < 0) {
+          set_error("plan: GlobalAveragePool node %d needs a 4-D input", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int yb = nd.out[0];
+        set_nhwc(m->bufs[yb], Y);  // [N, C, 1, 1] -> NHWC == [N][cpad]
+        const int s = add_step(ni, nd.op, 5, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[xb];
+          const Buf* y = &m->bufs[yb];
+          r.run = [=](cudaStream_t st) { return launch_gap_nhwc(x->ptr, y->ptr, x->n, x->h * x->w, x->cpad, st); };
+          return 0;
+        });
+        P.touch(xb, s);
+        P.touch(yb, s);
+        produced[yb] = 1;
+        break;
+      }
+      case OP_FLATTEN:
+      case OP_RESHAPE:
+      case OP_IDENTITY: {
+        const int xid = nd.in[0], yid = nd.out[0];
+        const TensorRec& Y = m->tensors[yid];
+        Buf& xbuf = m->bufs[xid];
+        const bool nhwc_trivial = xbuf.lay == LAY_NHWC && xbuf.h * xbuf.w == 1 && xbuf.cpad == xbuf.c;
+        int src = xid;
+        if (xbuf.lay == LAY_NHWC && !nhwc_trivial) src = ensure_row(xid, ni);
+        set_row(m->bufs[yid], Y);
+        m->bufs[yid].alias = src;  // same bytes, row-major view
+        const int s = add_step(ni, nd.op, 0, 0, [](StepRec& r) {
+          r.run = [](cudaStream_t) { return 0; };
+          return 0;
+        });
+        P.touch(src, s);
+        produced[yid] = 1;
+        break;
+      }
+      case OP_GEMM: {
+        GemmParams gp{1.0f, 1.0f, 0, 0, {0, 0}};
+        if (nd.params.size() >= sizeof(GemmParams)) std::memcpy(&gp, nd.params.data(), sizeof(gp));
+        const TensorRec& A = m->tensors[nd.in[0]];
+        const TensorRec& Bw = m->tensors[nd.in[1]];
+        const TensorRec& Y = m->tensors[nd.out[0]];
+        if (A.ndim != 2 || Bw.ndim != 2 || !Bw.host || A.is_weight) {
+          set_error("plan: Gemm node %d: activation A and constant 2-D B required", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int M = gp.transA ? A.dims[1] : A.dims[0];
+        const int K = gp.transA ? A.dims[0] : A.dims[1];
+        const int N = gp.transB ? Bw.dims[0] : Bw.dims[1];
+        const int Np = round4(N), Kp = round4(K);
+        const int kpad = tc_num_kb(K) * 32;
+        const uint64_t woff = P.wreserve((uint64_t)Np * kpad);
+        for (int n = 0; n < N; ++n)
+          for (int k = 0; k < K; ++k)
+            m->whost[woff + (uint64_t)n * kpad + k] =
+                host_round_tf32(gp.transB ? Bw.host[(uint64_t)n * K + k] : Bw.host[(uint64_t)k * N + n]);
+        uint64_t boff = ~0ull, roff = ~0ull;
+        const TensorRec* Cb = nd.in.size() > 2 ? &m->tensors[nd.in[2]] : nullptr;
+        if (Cb && Cb->host && gp.beta != 0.0f) {
+          if (Cb->elems == (uint64_t)N) {
+            boff = P.wreserve(Np);
+            for (int n = 0; n < N; ++n) m->whost[boff + n] = gp.beta * Cb->host[n];
+          } else if (Cb->elems == (uint64_t)M * N) {
+            roff = P.wreserve((uint64_t)M * Np);
+            for (int i = 0; i < M; ++i)
+              for (int n = 0; n < N; ++n) m->whost[roff + (uint64_t)i * Np + n] = gp.beta * Cb->host[(uint64_t)i * N + n];
+          } else {
+            set_error("plan: Gemm node %d: C must be [N] or [M,N]", ni);
+            return SPINN_CUDA_EUNSUPPORTED;
+          }
+        }
+        if (gp.transA && Kp != K) {
+          set_error("plan: Gemm node %d: transA with K=%d not a multiple of 4 is not supported", ni, K);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        int ab = ensure_row(nd.in[0], ni);
+        // A operand: row-major [M][Kp]; transposed or misaligned inputs go through a temp
+        int at = -1;
+        if (gp.transA || Kp != K) {
+          Buf tb;
+          tb.lay = LAY_ROW;
+          tb.bytes = (uint64_t)M * Kp * 4;
+          at = P.new_buf(tb);
+        }
+        int yt = -1;
+        const int yb = nd.out[0];
+        set_row(m->bufs[yb], Y);
+        if (Np != N) {
+          Buf tb;
+          tb.lay = LAY_ROW;
+          tb.bytes = (uint64_t)M * Np * 4;
+          yt = P.new_buf(tb);
+        }
+        const float alpha = gp.alpha;
+        const int transA = gp.transA;
+        const int s = add_step(ni, OP_GEMM, 2, 2.0 * M * N * K, [=](StepRec& r) {
+          const Buf* a = &m->bufs[ab];
+          const Buf* atp = at >= 0 ? &m->bufs[at] : nullptr;
+          const Buf* y = &m->bufs[yb];
+          const Buf* ytp = yt >= 0 ? &m->bufs[yt] : nullptr;
+          r.run = [=](cudaStream_t st) {
+            const float* A_ = a->ptr;
+            if (atp) {
+              if (transA) {
+                int rc = launch_transpose(a->ptr, atp->ptr, 1, K, M, st);
+                if (rc) return rc;
+              } else {
+                SPINN_CUDA_TRY(cudaMemcpy2DAsync(atp->ptr, (size_t)Kp * 4, a->ptr, (size_t)K * 4, (size_t)K * 4, M,
+                                                 cudaMemcpyDeviceToDevice, st));
+              }
+              A_ = atp->ptr;
+            }
+            TcGemmArgs g;
+            g.a_mode = 1;
+            g.x = A_;
+            g.M = M;
+            g.K = K;
+            g.lda = Kp;
+            g.wt = m->wdev + woff;
+            g.kpad = kpad;
+            g.N = Np;
+            g.bias = boff != ~0ull ? m->wdev + boff : nullptr;
+            g.res = roff != ~0ull ? m->wdev + roff : nullptr;
+            g.ldr = Np;
+            g.y = ytp ? ytp->ptr : y->ptr;
+            g.ldy = Np;
+            g.alpha = alpha;
+            int rc = tc_gemm_launch(g, st);
+            if (rc) return rc;
+            if (ytp)
+              SPINN_CUDA_TRY(cudaMemcpy2DAsync(y->ptr, (size_t)N * 4, ytp->ptr, (size_t)Np * 4, (size_t)N * 4, M,
+                                               cudaMemcpyDeviceToDevice, st));
+            return 0;
+          };
+          return 0;
+        });
+        P.touch(ab, s);
+        P.touch(yb, s);
+        if (at >= 0) P.touch(at, s);
+        if (yt >= 0) P.touch(yt, s);
+        produced[yb] = 1;
+        break;
+      }
+      case OP_ADD:
+      case OP_MUL:
+      case OP_SUB:
+      case OP_DIV: {
+        const int aid = nd.in[0], bid = nd.in[1], yid = nd.out[0];
+        const TensorRec& Ta = m->tensors[aid];
+        const TensorRec& Tb = m->tensors[bid];
+        const TensorRec& Ty = m->tensors[yid];
+        const int op = nd.op == OP_ADD ? ELT_ADD : nd.op == OP_MUL ? ELT_MUL : nd.op == OP_SUB ? ELT_SUB : ELT_DIV;
+        // fast path: both operands activations of the output's shape, same NHWC layout
+        const bool same = !Ta.is_weight && !Tb.is_weight && Ta.elems == Ty.elems && Tb.elems == Ty.elems &&
+                          m->bufs[aid].lay == LAY_NHWC && m->bufs[bid].lay == LAY_NHWC && op != ELT_DIV;
+        int ab, bb;
+        uint64_t wa = ~0ull, wb = ~0ull;
+        if (same) {
+          ab = aid;
+          bb = bid;
+          set_nhwc(m->bufs[yid], Ty);
+        } else {
+          if (Ta.is_weight) {
+            wa = P.wreserve(Ta.elems);
+            std::memcpy(&m->whost[wa], Ta.host, Ta.elems * 4);
+            ab = -1;
+          } else {
+            ab = ensure_row(aid, ni);
+          }
+          if (Tb.is_weight) {
+            wb = P.wreserve(Tb.elems);
+            std::memcpy(&m->whost[wb], Tb.host, Tb.elems * 4);
+            bb = -1;
+          } else {
+            bb = ensure_row(bid, ni);
+          }
+          set_row(m->bufs[yid], Ty);
+        }
+        const long na = (long)Ta.elems, nbv = (long)Tb.elems;
+        const int s = add_step(ni, nd.op, 6, 0, [=](StepRec& r) {
+          const Buf* a = ab >= 0 ? &m->bufs[ab] : nullptr;
+          const Buf* b = bb >= 0 ? &m->bufs[bb] : nullptr;
+          const Buf* y = &m->bufs[yid];
+          r.run = [=](cudaStream_t st) {
+            const float* pa = a ? a->ptr : m->wdev + wa;
+            const float* pb = b ? b->ptr : m->wdev + wb;
+            if (same) {
+              const long n = (long)y->bytes / 4;
+              return launch_binary(pa, n, pb, n, y->ptr, n, op, 0, st);
+            }
+            return launch_binary(pa, na, pb, nbv, y->ptr, (long)(y->bytes / 4), op, 0, st);
+          };
+          return 0;
+        });
+        if (ab >= 0) P.touch(ab, s);
+        if (bb >= 0) P.touch(bb, s);
+        P.touch(yid, s);
+        produced[yid] = 1;
+        break;
+      }
+      case OP_RELU:
+      case OP_SIGMOID: {
+        const int xid = nd.in[0], yid = nd.out[0];
+        Buf& xb = m->bufs[xid];
+        if (xb.lay == LAY_NHWC)
+          set_nhwc(m->bufs[yid], m->tensors[yid]);
+        else
+          set_row(m->bufs[yid], m->tensors[yid]);
+        const int op = nd.op == OP_RELU ? UN_RELU : UN_SIGMOID;
+        // Sigmoid of a zero pad channel is 0.5: row layout keeps no pad channels.
+        int src = xid;
+        if (op == UN_SIGMOID && xb.lay == LAY_NHWC && xb.cpad != xb.c) {
+          src = ensure_row(xid, ni);
+          set_row(m->bufs[yid], m->tensors[yid]);
+        }
+        const int s = add_step(ni, nd.op, 6, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[src];
+          const Buf* y = &m->bufs[yid];
+          r.run = [=](cudaStream_t st) { return launch_unary(x->ptr, y->ptr, (long)(y->bytes / 4), op, st); };
+          return 0;
+        });
+        P.touch(src, s);
+        P.touch(yid, s);
+        produced[yid] = 1;
+        break;
+      }
+      case OP_BN: {
+        // standalone BatchNormalization (op_batch_norm, SPINN/run_time/ops/norm/batch_norm.c:17-76)
+        BnParams bp{1e-5f, 0.9f, 0, {0, 0, 0}};
+        if (nd.params.size() >= sizeof(BnParams)) std::memcpy(&bp, nd.params.data(), sizeof(bp));
+        if (nd.in.size() < 5) {
+          set_error("plan: BatchNormalization node %d needs 5 inputs", ni);
+          return SPINN_CUDA_EFORMAT;
+        }
+        const TensorRec &g = m->tensors[nd.in[1]], &b = m->tensors[nd.in[2]], &mu = m->tensors[nd.in[3]],
+                        &var = m->tensors[nd.in[4]];
+        if (!g.host || !b.host || !mu.host || !var.host) {
+          set_error("plan: BatchNormalization node %d needs constant statistics", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int xb = ensure_nhwc(nd.in[0], ni);
+        if (xb < 0) {
+          set_error("plan: BatchNormalization node %d needs a 4-D input", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int yid = nd.out[0];
+        set_nhwc(m->bufs[yid], m->tensors[yid]);
+        const int C = m->bufs[yid].c, cpad = m->bufs[yid].cpad;
+        const uint64_t so = P.wreserve(cpad), ho = P.wreserve(cpad);
+        for (int c = 0; c < C; ++c) {
+          const float a = g.host[c] / std::sqrt(var.host[c] + bp.epsilon);
+          m->whost[so + c] = a;
+          m->whost[ho + c] = b.host[c] - mu.host[c] * a;
+        }
+        const int s = add_step(ni, nd.op, 6, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[xb];
+          const Buf* y = &m->bufs[yid];
+          r.run = [=](cudaStream_t st) {
+            return launch_channel_affine_nhwc(x->ptr, y->ptr, (long)y->n * y->h * y->w, y->cpad, m->wdev + so,
+                                              m->wdev + ho, st);
+          };
+          return 0;
+        });
+        P.touch(xb, s);
+        P.touch(yid, s);
+        produced[yid] = 1;
+        break;
+      }
+      default:
+        set_error("plan: operator %d (node %d) has no device implementation", nd.op, ni);
+        return SPINN_CUDA_EUNSUPPORTED;
+    }
+  }
+
+  // graph outputs: NCHW / row-major staging outside the arena
+  for (size_t i = 0; i < m->outputs.size(); ++i) {
+    const int id = m->outputs[i];
+    if (!produced[id]) {
+      set_error("plan: graph output %d is never produced", id);
+      return SPINN_CUDA_EFORMAT;
+    }
+    const TensorRec& t = m->tensors[id];
+    Buf st;
+    st.lay = LAY_ROW;
+    st.bytes = t.elems * 4;
+    st.external = 1;
+    const int sb = P.new_buf(st);
+    m->out_buf.push_back(sb);
+    const int src = P.root(id);
+    const bool nhwc = m->bufs[id].lay == LAY_NHWC;
+    const int s = add_step(-1, 0, 7, 0, [m, id, sb, nhwc](StepRec& r) {
+      const Buf* x = &m->bufs[id];
+      const Buf* xr = x;
+      while (xr->alias >= 0) xr = &m->bufs[xr->alias];
+      const Buf* y = &m->bufs[sb];
+      r.run = [x, xr, y, nhwc](cudaStream_t st) -> int {
+        if (nhwc) return launch_nhwc_to_nchw(xr->ptr, y->ptr, x->n, x->c, x->h, x->w, x->cpad, st);
+        SPINN_CUDA_TRY(cudaMemcpyAsync(y->ptr, xr->ptr, y->bytes, cudaMemcpyDeviceToDevice, st));
+        return 0;
+      };
+      return 0;
+    });
+    P.touch(src, s);
+  }
+
+  // arena
+  const int nsteps = (int)m->steps.size();
+  int rc = plan_arena(m, nsteps, budget);
+  if (rc) return rc;
+  if (m->arena_bytes) SPINN_CUDA_TRY(cudaMalloc(&m->arena, m->arena_bytes));
+  for (auto& b : m->bufs) {
+    if (b.alias >= 0) continue;
+    if (b.external) {
+      if (b.bytes) SPINN_CUDA_TRY(cudaMalloc(&b.ptr, align_up(b.bytes, 256)));
+    } else if (b.offset >= 0) {
+      b.ptr = reinterpret_cast<float*>(m->arena + b.offset);
+    }
+  }
+  for (auto& b : m->bufs) {
+    if (b.alias < 0) continue;
+    int r = b.alias;
+    while (m->bufs[r].alias >= 0) r = m->bufs[r].alias;
+    b.ptr = m->bufs[r].ptr;
+  }
+  // weights
+  m->wbytes = m->whost.size() * 4;
+  if (m->wbytes) {
+    SPINN_CUDA_TRY(cudaMalloc(&m->wdev, m->wbytes));
+    SPINN_CUDA_TRY(cudaMemcpy(m->wdev, m->whost.data(), m->wbytes, cudaMemcpyHostToDevice));
+  }
+  std::vector<float>().swap(m->whost);
+  // closures
+  m->kernels = 0;
+  for (int i = 0; i < nsteps; ++i) {
+    rc = builders[i](m->steps[i]);
+    if (rc) return rc;
+    if (m->steps[i].kind != 0) ++m->kernels;
+  }
+  return 0;
+}
+
+static int run_steps(SpinnCudaModel* m, cudaStream_t st) {
+  const bool prof = (m->flags & SPINN_CUDA_PLAN_PROFILE) != 0;
+  for (size_t i = 0; i < m->steps.size(); ++i) {
+    if (prof) cudaEventRecord(m->events[i], st);
+    int rc = m->steps[i].run(st);
+    if (rc) return rc;
+  }
+  if (prof) cudaEventRecord(m->events[m->steps.size()], st);
+  return 0;
+}
+
+static void release_model(SpinnCudaModel* m) {
+  if (!m) return;
+  if (m->device >= 0) cudaSetDevice(m->device);
+  if (m->gexec) cudaGraphExecDestroy(m->gexec);
+  if (m->graph) cudaGraphDestroy(m->graph);
+  for (auto e : m->events) cudaEventDestroy(e);
+  for (auto& b : m->bufs)
+    if (b.external && b.ptr && b.alias < 0) cudaFree(b.ptr);
+  if (m->arena) cudaFree(m->arena);
+  if (m->wdev) cudaFree(m->wdev);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+// ------------------------------------------------------------------ C ABI (model level)
+extern "C" {
+
+__attribute__((visibility("default"))) SpinnCudaModel* spinn_cuda_load_buffer(const void* data, size_t size) {
+  if (!data || size < sizeof(EnnfHeader)) {
+    set_error("spinn_cuda_load_buffer: empty image");
+    return nullptr;
+  }
+  auto* m = new SpinnCudaModel();
+  m->image.assign((const uint8_t*)data, (const uint8_t*)data + size);
+  if (parse_image(m)) {
+    delete m;
+    return nullptr;
+  }
+  return m;
+}
+
+__attribute__((visibility("default"))) SpinnCudaModel* spinn_cuda_load(const char* path) {
+  FILE* f = path ? fopen(path, "rb") : nullptr;
+  if (!f) {
+    set_error("spinn_cuda_load: cannot open %s", path ? path : "(null)");
+    return nullptr;
+  }
+  fseek(f, 0, SEEK_END);
+  const long sz = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  std::vector<uint8_t> buf(sz > 0 ? sz : 0);
+  const size_t rd = sz > 0 ? fread(buf.data(), 1, sz, f) : 0;
+  fclose(f);
+  if ((long)rd != sz) {
+    set_error("spinn_cuda_load: short read on %s", path);
+    return nullptr;
+  }
+  return spinn_cuda_load_buffer(buf.data(), buf.size());
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_plan(SpinnCudaModel* m, int device, uint64_t max_arena_bytes,
+                                                           int flags) {
+  if (!m) {
+    set_error("spinn_cuda_plan: null model");
+    return SPINN_CUDA_EINVAL;
+  }
+  if (m->planned) {
+    set_error("spinn_cuda_plan: model already planned");
+    return SPINN_CUDA_ESTATE;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(device));
+  m->device = device;
+  m->flags = flags;
+  SPINN_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  int rc = compile_model(m, max_arena_bytes);
+  if (rc) return rc;
+  if (flags & SPINN_CUDA_PLAN_PROFILE) {
+    m->events.resize(m->steps.size() + 1);
+    for (auto& e : m->events) SPINN_CUDA_TRY(cudaEventCreate(&e));
+  }
+  // one eager pass validates every launch; then the step list is captured as a graph
+  rc = run_steps(m, m->stream);
+  if (rc) return rc;
+  SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  rc = check_device_error_flag(device, m->stream);
+  if (rc) return rc;
+  if (!(flags & (SPINN_CUDA_PLAN_NO_GRAPH | SPINN_CUDA_PLAN_PROFILE))) {
+    SPINN_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    rc = run_steps(m, m->stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    SPINN_CUDA_TRY(e);
+    m->graph = g;
+    SPINN_CUDA_TRY(cudaGraphInstantiate(&m->gexec, g, 0));
+  }
+  m->planned = true;
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_run_device(SpinnCudaModel* m, void* stream) {
+  if (!m || !m->planned) {
+    set_error("spinn_cuda_run_device: model not planned");
+    return SPINN_CUDA_ESTATE;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(m->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+  if (m->gexec) {
+    SPINN_CUDA_TRY(cudaGraphLaunch(m->gexec, st));
+    return 0;
+  }
+  int rc = run_steps(m, st);
+  if (rc) return rc;
+  if (m->flags & SPINN_CUDA_PLAN_PROFILE) {
+    SPINN_CUDA_TRY(cudaStreamSynchronize(st));
+    m->step_ms.assign(m->steps.size(), 0.0f);
+    for (size_t i = 0; i < m->steps.size(); ++i) cudaEventElapsedTime(&m->step_ms[i], m->events[i], m->events[i + 1]);
+  }
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_run(SpinnCudaModel* m, const void* input, void* output) {
+  if (!m || !m->planned) {
+    set_error("spinn_cuda_run: model not planned");
+    return SPINN_CUDA_ESTATE;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(m->device));
+  if (input && !m->in_buf.empty()) {
+    const Buf& b = m->bufs[m->in_buf[0]];
+    SPINN_CUDA_TRY(cudaMemcpyAsync(b.ptr, input, b.bytes, cudaMemcpyHostToDevice, m->stream));
+  }
+  int rc = spinn_cuda_run_device(m, nullptr);
+  if (rc) return rc;
+  if (output && !m->out_buf.empty()) {
+    const Buf& b = m->bufs[m->out_buf[0]];
+    SPINN_CUDA_TRY(cudaMemcpyAsync(output, b.ptr, b.bytes, cudaMemcpyDeviceToHost, m->stream));
+  }
+  SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return check_device_error_flag(m->device, m->stream);
+}
+
+__attribute__((visibility("default"))) void* spinn_cuda_io_ptr(SpinnCudaModel* m, int is_output, int index,
+                                                               size_t* bytes) {
+  if (!m || !m->planned) return nullptr;
+  const auto& v = is_output ? m->out_buf : m->in_buf;
+  if (index < 0 || index >= (int)v.size()) return nullptr;
+  const Buf& b = m->bufs[v[index]];
+  if (bytes) *bytes = b.bytes;
+  return b.ptr;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_io_count(SpinnCudaModel* m, int is_output) {
+  if (!m) return SPINN_CUDA_EINVAL;
+  return (int)(is_output ? m->outputs.size() : m->inputs.size());
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_io_dims(SpinnCudaModel* m, int is_output, int index,
+                                                              uint32_t* dims) {
+  if (!m) return SPINN_CUDA_EINVAL;
+  const auto& v = is_output ? m->outputs : m->inputs;
+  if (index < 0 || index >= (int)v.size()) return SPINN_CUDA_EINVAL;
+  const TensorRec& t = m->tensors[v[index]];
+  if (dims) std::memcpy(dims, t.dims, sizeof(t.dims));
+  return t.ndim;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_plan_info(SpinnCudaModel* m, uint64_t* arena_bytes,
+                                                                uint64_t* weight_bytes, int* num_steps,
+                                                                int* num_kernels) {
+  if (!m || !m->planned) return SPINN_CUDA_ESTATE;
+  if (arena_bytes) *arena_bytes = m->arena_bytes;
+  if (weight_bytes) *weight_bytes = m->wbytes;
+  if (num_steps) *num_steps = (int)m->steps.size();
+  if (num_kernels) *num_kernels = m->kernels;
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_profile(SpinnCudaModel* m, int* op_types, float* ms,
+                                                              double* flops, int cap) {
+  if (!m || !m->planned) return SPINN_CUDA_ESTATE;
+  const int n = std::min<int>(cap, (int)m->step_ms.size());
+  for (int i = 0; i < n; ++i) {
+    if (op_types) op_types[i] = m->steps[i].op;
+    if (ms) ms[i] = m->step_ms[i];
+    if (flops) flops[i] = m->steps[i].flops;
+  }
+  return n;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_step_kind(SpinnCudaModel* m, int i) {
+  if (!m || i < 0 || i >= (int)m->steps.size()) return -1;
+  return m->steps[i].kind;
+}
+
+__attribute__((visibility("default"))) void spinn_cuda_free(SpinnCudaModel* m) { release_model(m); }
+
+}  // extern "C"
+}  // namespace spinn

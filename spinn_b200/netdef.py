@@ -1,0 +1,290 @@
+"""Network definitions in ONNX/ENNF terms, with seeded synthetic weights.
+
+A :class:`Graph` is an ordered ONNX-style graph (named tensors, initializers, nodes with
+attributes, full static shapes for every intermediate).  It is the single source for the
+two serialisations this project needs:
+
+* ``spinn_b200.ennf.convert`` -- the fused ``.ennf`` file that SPINN's converter
+  (``SPINN/onnx2ennf.c`` + ``SPINN/graph_opt.c``) would write for the same graph;
+* ``oracle/onnx_writer.py`` -- an ONNX protobuf, fed to the reference converter itself
+  (test infrastructure) to pin the former byte for byte.
+
+Node order follows a PyTorch ``torch.onnx`` export (conv, bn, relu, ...), because the
+reference fusion passes are order sensitive (``SPINN/graph_opt.c:350-374``).
+
+Synthetic data follows the benchmark configurations: conv weights He-normal
+``N(0, sqrt(2/fan_in))``, BatchNorm ``gamma~U(0.5,1.5)``, ``beta,mean~N(0,0.1)``,
+``var~U(0.5,1.5)``, ``eps=1e-5``; all parameters drawn from one
+``numpy.random.default_rng(seed)`` in node order (conv weight, then gamma, beta, mean,
+var); the FC layer ``W,b ~ U(-1/sqrt(fan_in), 1/sqrt(fan_in))``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+Shape = Tuple[int, ...]
+
+
+@dataclass
+class Node:
+    op_type: str
+    inputs: List[str]
+    outputs: List[str]
+    attrs: Dict[str, object] = field(default_factory=dict)
+    name: str = ""
+
+
+@dataclass
+class Graph:
+    name: str = "spinn_b200"
+    nodes: List[Node] = field(default_factory=list)
+    initializers: Dict[str, np.ndarray] = field(default_factory=dict)
+    inputs: List[Tuple[str, Shape]] = field(default_factory=list)
+    outputs: List[Tuple[str, Shape]] = field(default_factory=list)
+    value_info: Dict[str, Shape] = field(default_factory=dict)
+    opset: int = 13
+
+    # ------------------------------------------------------------------ helpers
+    def shape(self, name: str) -> Shape:
+        if name in self.initializers:
+            return tuple(self.initializers[name].shape)
+        for n, s in self.inputs:
+            if n == name:
+                return s
+        return self.value_info[name]
+
+    def add_input(self, name: str, shape: Sequence[int]) -> str:
+        self.inputs.append((name, tuple(int(d) for d in shape)))
+        return name
+
+    def add_init(self, name: str, arr: np.ndarray) -> str:
+        self.initializers[name] = np.ascontiguousarray(arr, dtype=np.float32)
+        return name
+
+    def add_node(self, op: str, inputs: Sequence[str], outputs: Sequence[str],
+                 out_shapes: Sequence[Shape], **attrs) -> List[str]:
+        for o, s in zip(outputs, out_shapes):
+            self.value_info[o] = tuple(int(d) for d in s)
+        self.nodes.append(Node(op, list(inputs), list(outputs), dict(attrs),
+                               name=f"{op}_{len(self.nodes)}"))
+        return list(outputs)
+
+    def mark_output(self, name: str) -> None:
+        self.outputs.append((name, self.value_info[name]))
+        # graph outputs are described by graph.output, not value_info (ONNX convention)
+        del self.value_info[name]
+
+    def copy(self) -> "Graph":
+        g = Graph(self.name, [Node(n.op_type, list(n.inputs), list(n.outputs), dict(n.attrs), n.name)
+                              for n in self.nodes],
+                  {k: v.copy() for k, v in self.initializers.items()},
+                  list(self.inputs), list(self.outputs), dict(self.value_info), self.opset)
+        return g
+
+    def flops(self) -> int:
+        """Algorithmic multiply-add FLOPs (2 per MAC) of the Conv/Gemm/MatMul nodes."""
+        total = 0
+        for n in self.nodes:
+            if n.op_type == "Conv":
+                w = self.shape(n.inputs[1])
+                y = self._out_shape(n)
+                total += 2 * int(np.prod(y)) * w[1] * w[2] * w[3]
+            elif n.op_type == "Gemm":
+                a = self.shape(n.inputs[0])
+                y = self._out_shape(n)
+                k = a[0] if n.attrs.get("transA", 0) else a[1]
+                total += 2 * y[0] * y[1] * k
+            elif n.op_type == "MatMul":
+                a = self.shape(n.inputs[0])
+                y = self._out_shape(n)
+                total += 2 * int(np.prod(y)) * a[-1]
+        return total
+
+    def _out_shape(self, n: Node) -> Shape:
+        o = n.outputs[0]
+        for name, s in self.outputs:
+            if name == o:
+                return s
+        return self.value_info[o]
+
+
+def conv_out_hw(h: int, w: int, k: int, s: int, p: int) -> Tuple[int, int]:
+    return (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+
+
+class _Builder:
+    """Small helper that names tensors and draws weights in node order."""
+
+    def __init__(self, g: Graph, rng: np.random.Generator):
+        self.g = g
+        self.rng = rng
+        self.k = 0
+
+    def _id(self, prefix: str) -> str:
+        self.k += 1
+        return f"{prefix}_{self.k}"
+
+    def conv(self, x: str, oc: int, k: int, s: int, p: int, group: int = 1,
+             bias: bool = False, dilation: int = 1) -> str:
+        n, c, h, w = self.g.shape(x)
+        fan_in = (c // group) * k * k
+        wname = self.g.add_init(self._id("conv_w"),
+                                self.rng.normal(0.0, np.sqrt(2.0 / fan_in), (oc, c // group, k, k)))
+        ins = [x, wname]
+        if bias:
+            ins.append(self.g.add_init(self._id("conv_b"), self.rng.normal(0.0, 0.1, (oc,))))
+        oh, ow = conv_out_hw(h, w, (k - 1) * dilation + 1, s, p)
+        return self.g.add_node("Conv", ins, [self._id("conv")], [(n, oc, oh, ow)],
+                               kernel_shape=[k, k], strides=[s, s], pads=[p, p, p, p],
+                               dilations=[dilation, dilation], group=group)[0]
+
+    def bn(self, x: str, eps: float = 1e-5) -> str:
+        c = self.g.shape(x)[1]
+        gamma = self.g.add_init(self._id("bn_gamma"), self.rng.uniform(0.5, 1.5, (c,)))
+        beta = self.g.add_init(self._id("bn_beta"), self.rng.normal(0.0, 0.1, (c,)))
+        mean = self.g.add_init(self._id("bn_mean"), self.rng.normal(0.0, 0.1, (c,)))
+        var = self.g.add_init(self._id("bn_var"), self.rng.uniform(0.5, 1.5, (c,)))
+        return self.g.add_node("BatchNormalization", [x, gamma, beta, mean, var], [self._id("bn")],
+                               [self.g.shape(x)], epsilon=float(eps), momentum=0.9)[0]
+
+    def unary(self, op: str, x: str) -> str:
+        return self.g.add_node(op, [x], [self._id(op.lower())], [self.g.shape(x)])[0]
+
+    def add(self, a: str, b: str) -> str:
+        return self.g.add_node("Add", [a, b], [self._id("add")], [self.g.shape(a)])[0]
+
+    def mul(self, a: str, b: str) -> str:
+        return self.g.add_node("Mul", [a, b], [self._id("mul")], [self.g.shape(a)])[0]
+
+    def silu(self, x: str) -> str:
+        s = self.unary("Sigmoid", x)
+        return self.mul(x, s)
+
+    def maxpool(self, x: str, k: int, s: int, p: int) -> str:
+        n, c, h, w = self.g.shape(x)
+        oh, ow = conv_out_hw(h, w, k, s, p)
+        return self.g.add_node("MaxPool", [x], [self._id("maxpool")], [(n, c, oh, ow)],
+                               kernel_shape=[k, k], strides=[s, s], pads=[p, p, p, p])[0]
+
+    def gap(self, x: str) -> str:
+        n, c, _, _ = self.g.shape(x)
+        return self.g.add_node("GlobalAveragePool", [x], [self._id("gap")], [(n, c, 1, 1)])[0]
+
+    def flatten(self, x: str) -> str:
+        s = self.g.shape(x)
+        return self.g.add_node("Flatten", [x], [self._id("flatten")],
+                               [(s[0], int(np.prod(s[1:])))], axis=1)[0]
+
+    def gemm(self, x: str, n_out: int, trans_b: int = 1) -> str:
+        m, k = self.g.shape(x)
+        bound = 1.0 / np.sqrt(k)
+        wshape = (n_out, k) if trans_b else (k, n_out)
+        w = self.g.add_init(self._id("fc_w"), self.rng.uniform(-bound, bound, wshape))
+        b = self.g.add_init(self._id("fc_b"), self.rng.uniform(-bound, bound, (n_out,)))
+        return self.g.add_node("Gemm", [x, w, b], [self._id("gemm")], [(m, n_out)],
+                               alpha=1.0, beta=1.0, transA=0, transB=int(trans_b))[0]
+
+
+# ---------------------------------------------------------------------- models
+def conv_bn_relu(batch: int = 1, c: int = 64, hw: int = 56, oc: int = 64, k: int = 3,
+                 stride: int = 1, pad: int = 1, seed: int = 0, act: str = "Relu"
+                 ) -> Tuple[Graph, np.ndarray]:
+    """Single Conv+BatchNorm(+act) layer (the benchmark's first configuration).
+
+    Draw order from ``default_rng(seed)``: input X~U(-1,1), W~N(0,sqrt(2/fan_in)),
+    gamma, beta, mean, var.  Returns the graph and the input tensor.
+    """
+    rng = np.random.default_rng(seed)
+    x_val = rng.uniform(-1.0, 1.0, (batch, c, hw, hw)).astype(np.float32)
+    g = Graph("conv_bn_relu")
+    b = _Builder(g, rng)
+    x = g.add_input("input", (batch, c, hw, hw))
+    y = b.bn(b.conv(x, oc, k, stride, pad))
+    if act == "Relu":
+        y = b.unary("Relu", y)
+    elif act == "SiLU":
+        y = b.silu(y)
+    g.mark_output(y)
+    return g, x_val
+
+
+def conv_bn_add_relu(batch: int = 1, c: int = 64, hw: int = 56, seed: int = 0
+                     ) -> Tuple[Graph, np.ndarray]:
+    """Conv+BN whose output is added to the block input and ReLU'd (residual fusion)."""
+    rng = np.random.default_rng(seed)
+    x_val = rng.uniform(-1.0, 1.0, (batch, c, hw, hw)).astype(np.float32)
+    g = Graph("conv_bn_add_relu")
+    b = _Builder(g, rng)
+    x = g.add_input("input", (batch, c, hw, hw))
+    r = b.unary("Relu", x)
+    y = b.unary("Relu", b.add(b.bn(b.conv(r, c, 3, 1, 1)), r))
+    g.mark_output(y)
+    return g, x_val
+
+
+RESNET_DEPTHS = {18: None, 50: [3, 4, 6, 3], 101: [3, 4, 23, 3], 152: [3, 8, 36, 3]}
+
+
+def resnet(depth: int = 50, batch: int = 1, image: int = 224, num_classes: int = 1000,
+           seed: int = 2, width: int = 64) -> Graph:
+    """Bottleneck ResNet (v1.5: stride on the 3x3 conv), torchvision export order."""
+    blocks = RESNET_DEPTHS[depth]
+    if blocks is None:
+        raise ValueError("only bottleneck depths (50/101/152) are defined")
+    rng = np.random.default_rng(seed)
+    g = Graph(f"resnet{depth}")
+    b = _Builder(g, rng)
+    x = g.add_input("input", (batch, 3, image, image))
+    y = b.unary("Relu", b.bn(b.conv(x, width, 7, 2, 3)))
+    y = b.maxpool(y, 3, 2, 1)
+    in_c = width
+    for stage, nblk in enumerate(blocks):
+        mid = width * (2 ** stage)
+        out_c = mid * 4
+        for i in range(nblk):
+            stride = 2 if (i == 0 and stage > 0) else 1
+            idn = y
+            t = b.unary("Relu", b.bn(b.conv(y, mid, 1, 1, 0)))
+            t = b.unary("Relu", b.bn(b.conv(t, mid, 3, stride, 1)))
+            t = b.bn(b.conv(t, out_c, 1, 1, 0))
+            if i == 0:
+                idn = b.bn(b.conv(y, out_c, 1, stride, 0))
+            y = b.unary("Relu", b.add(t, idn))
+            in_c = out_c
+    y = b.flatten(b.gap(y))
+    y = b.gemm(y, num_classes, trans_b=1)
+    g.mark_output(y)
+    return g
+
+
+def resnet_input(batch: int, image: int = 224, seed: int = 2) -> np.ndarray:
+    """N(0,1) NCHW input, drawn from ``default_rng(seed + 1)``."""
+    return np.random.default_rng(seed + 1).standard_normal((batch, 3, image, image),
+                                                           dtype=np.float32)
+
+
+def gemm_case(m: int, n: int, k: int, trans_a: int = 0, trans_b: int = 0, alpha: float = 1.0,
+              beta: float = 1.0, c_shape: Optional[str] = "vector", seed: int = 1
+              ) -> Tuple[Graph, np.ndarray]:
+    """Standalone Gemm ``Y = alpha*A*B + beta*C`` with A, B, C ~ U(-1,1) from ``default_rng(seed)``.
+
+    ``c_shape`` is ``"vector"`` ([N]), ``"full"`` ([M,N]) or ``None`` (no C input).
+    B and C are initializers (weights); A is the graph input.
+    """
+    rng = np.random.default_rng(seed)
+    a_val = rng.uniform(-1, 1, (k, m) if trans_a else (m, k)).astype(np.float32)
+    g = Graph("gemm")
+    a = g.add_input("A", a_val.shape)
+    bw = g.add_init("B", rng.uniform(-1, 1, (n, k) if trans_b else (k, n)))
+    ins = [a, bw]
+    if c_shape == "vector":
+        ins.append(g.add_init("C", rng.uniform(-1, 1, (n,))))
+    elif c_shape == "full":
+        ins.append(g.add_init("C", rng.uniform(-1, 1, (m, n))))
+    g.add_node("Gemm", ins, ["Y"], [(m, n)], alpha=float(alpha), beta=float(beta),
+               transA=int(trans_a), transB=int(trans_b))
+    g.mark_output("Y")
+    return g, a_val

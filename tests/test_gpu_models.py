@@ -1,0 +1,61 @@
+"""Model-level parity on the GPU: .ennf models through the device runtime (spinn_cuda_load /
+plan / run) against the reference runtime (oracle/_ref: spinn_load / spinn_plan / spinn_run,
+O-fix) on identical seeded inputs.
+
+Tolerances (benchmark statement): per-layer relative L2 <= 2e-3; end to end, max abs error
+<= 1e-2 and identical argmax.
+"""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref_outputs(ref_oracle, image: bytes, x, tmp_path):
+    p = tmp_path / "m.ennf"
+    p.write_bytes(image)
+    return ref_oracle.run_model(str(p), x)
+
+
+@pytest.mark.parametrize("act", ["Relu", "SiLU"])
+def test_cfg0_conv_bn_act(cuda_lib, ref_oracle, tmp_path, act):
+    from spinn_b200 import ennf, netdef, runtime
+    g, x = netdef.conv_bn_relu(act=act)
+    img = ennf.convert(g)
+    ref = list(_ref_outputs(ref_oracle, img, x, tmp_path).values())[0]
+    m = runtime.Model(img)
+    y = m.run(x).ravel()
+    assert rel_l2(y, ref) <= 2e-3, rel_l2(y, ref)
+
+
+def test_cfg0_batch(cuda_lib, ref_oracle, tmp_path):
+    from spinn_b200 import ennf, netdef, runtime
+    g, x = netdef.conv_bn_relu(batch=8)
+    img = ennf.convert(g)
+    ref = list(_ref_outputs(ref_oracle, img, x, tmp_path).values())[0]
+    y = runtime.Model(img).run(x).ravel()
+    assert rel_l2(y, ref) <= 2e-3
+
+
+def test_residual_block(cuda_lib, ref_oracle, tmp_path):
+    from spinn_b200 import ennf, netdef, runtime
+    g, x = netdef.conv_bn_add_relu(batch=2, c=64, hw=28)
+    img = ennf.convert(g)
+    ref = list(_ref_outputs(ref_oracle, img, x, tmp_path).values())[0]
+    y = runtime.Model(img).run(x).ravel()
+    assert rel_l2(y, ref) <= 2e-3
+
+
+def test_resnet50_end_to_end(cuda_lib, ref_oracle, tmp_path):
+    from spinn_b200 import ennf, netdef, runtime
+    g = netdef.resnet(50, batch=2, seed=2)
+    x = netdef.resnet_input(2, seed=2)
+    img = ennf.convert(g)
+    ref = list(_ref_outputs(ref_oracle, img, x, tmp_path).values())[0].reshape(2, -1)
+    y = runtime.Model(img).run(x).reshape(2, -1)
+    err = float(np.abs(y - ref).max())
+    assert rel_l2(y, ref) <= 2e-3, rel_l2(y, ref)
+    assert err <= 1e-2, err
+    assert (y.argmax(1) == ref.argmax(1)).all()
