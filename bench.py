@@ -1,0 +1,348 @@
+"""Benchmark: ResNet-101 (bottleneck [3,4,23,3]) inference at batch 256, 3x224x224, fp32
+storage with tf32 tensor-core math, on 1..8 B200s of one node (benchmark configuration 3).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+The global batch of 256 images is split evenly over the N ranks (strong scaling; no
+collectives on the data path -- each rank runs its own weight replica).  A step is one
+forward pass of every rank's shard.  Rank 0 prints one JSON line:
+
+* value     images/s of the whole job from device time: the sum of per-step CUDA-event
+            times on the launching stream (L2 flushed with a 256 MiB write between steps,
+            outside the events), max over ranks.
+* e2e       the same metric through the C ABI call a user makes (spinn_cuda_run): pinned
+            host input -> device, run, logits -> host, every step, wall clock, max over ranks.
+* roofline  the tcgen05 convolution kernel: algorithmic conv FLOPs / its device time, both
+            taken from one profiled replay (CUDA events between the graph's kernels).
+* cpu_baseline  the reference's own CPU runtime (oracle/_ref, built unmodified from the
+            reference sources, epilogue fixed) on a bounded sample, rank 0 at N=1 only.
+
+``--impl reference`` times that reference CPU runtime alone (rank 0; other ranks exit 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+GLOBAL_BATCH = 256
+IMAGE = 224
+DEPTH = 101
+SEED = 3
+METRIC = "resnet101_images_per_sec"
+UNIT = "images/s"
+CPU_SAMPLE_BATCH = 2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global batch")
+    ap.add_argument("--depth", type=int, default=DEPTH)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons, sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for i, n in enumerate(names):
+                if r[5 + i].strip() == "Active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def build_model_image(batch: int, depth: int):
+    from spinn_b200 import ennf, netdef
+    g = netdef.resnet(depth, batch=batch, image=IMAGE, seed=SEED)
+    return ennf.convert(g), g.flops()
+
+
+def cpu_reference_rate(depth: int, seconds: float, warmup: int = 1, min_runs: int = 2):
+    """Reference CPU runtime (oracle/_ref, O-fix) on ResNet-`depth` batch CPU_SAMPLE_BATCH."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    if not oracle.ref_available():
+        return None
+    img, _ = build_model_image(CPU_SAMPLE_BATCH, depth)
+    from spinn_b200 import netdef
+    x = netdef.resnet_input(CPU_SAMPLE_BATCH, IMAGE, seed=SEED)
+    ref = oracle.RefOracle(fix=True)
+    threads = os.cpu_count() or 1
+    ref.set_threads(threads)
+    with tempfile.NamedTemporaryFile(suffix=".ennf", delete=False) as f:
+        f.write(img)
+        path = f.name
+    try:
+        ts = ref.time_model(path, x, steps=1, warmup=warmup)
+        n = max(min_runs, int(seconds / max(ts[0], 1e-3)))
+        ts += ref.time_model(path, x, steps=n - 1, warmup=0)
+    finally:
+        os.unlink(path)
+    per = statistics.median(ts)
+    return {"value": CPU_SAMPLE_BATCH / per, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"ResNet-{depth} batch {CPU_SAMPLE_BATCH} 3x224x224, {len(ts)} spinn_run calls after {warmup} "
+                      f"warm-up, median {per * 1e3:.1f} ms/call, OMP threads={threads}"}
+
+
+def run_reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    t0 = time.time()
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libspinn_ref.so was not built"}))
+        return 0
+    from spinn_b200 import netdef
+    img, _ = build_model_image(CPU_SAMPLE_BATCH, args.depth)
+    x = netdef.resnet_input(CPU_SAMPLE_BATCH, IMAGE, seed=SEED)
+    ref = oracle.RefOracle(fix=True)
+    threads = os.cpu_count() or 1
+    ref.set_threads(threads)
+    with tempfile.NamedTemporaryFile(suffix=".ennf", delete=False) as f:
+        f.write(img)
+        path = f.name
+    try:
+        ts = ref.time_model(path, x, steps=args.steps, warmup=args.warmup)
+    finally:
+        os.unlink(path)
+    total = sum(ts)
+    value = CPU_SAMPLE_BATCH * args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (He-init weights, N(0,1) input)",
+        "config": {"workload": f"ResNet-{args.depth} 3x224x224 (benchmark configuration 3); each step a "
+                               f"bounded sample of {CPU_SAMPLE_BATCH} images", "global_batch": args.batch,
+                   "image": IMAGE, "sample_batch": CPU_SAMPLE_BATCH},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} spinn_run calls of batch {CPU_SAMPLE_BATCH} after "
+                                   f"{args.warmup} warm-up, O-fix build, OMP threads={threads}"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": time.time() - t0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+    from spinn_b200 import lib, runtime
+
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        pg = dist
+    if args.batch % world:
+        raise SystemExit(f"global batch {args.batch} not divisible by {world} ranks")
+    shard = args.batch // world
+
+    t_build = time.time()
+    img, flops_per_step = build_model_image(shard, args.depth)
+    model = runtime.Model(img, device=local, flags=lib.PLAN_PROFILE)
+    info = model.plan_info()
+    kinds = model.step_kinds()
+    build_s = time.time() - t_build
+
+    g = torch.Generator().manual_seed(SEED * 1000 + rank)
+    x = torch.randn((shard, 3, IMAGE, IMAGE), generator=g, dtype=torch.float32)
+    x_pin = x.pin_memory()
+    in_ptr, in_bytes = model.io_ptr(False, 0)
+    out_ptr, out_bytes = model.io_ptr(True, 0)
+    out_pin = torch.empty(out_bytes // 4, dtype=torch.float32).pin_memory()
+    # a dedicated stream: the legacy default stream (handle 0) would mean "the model's own
+    # stream" to spinn_cuda_run_device, and events on it would not order with that stream
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    # one call through the C ABI leaves this shard's input resident in the model's device
+    # input buffer; the device-timed loop then reuses it
+    model.run_ptr(x_pin.data_ptr(), out_pin.data_ptr())
+    torch.cuda.synchronize()
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=f"cuda:{local}")
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    sid = stream.cuda_stream
+    for _ in range(args.warmup):
+        model.run_device(sid)
+        flush.zero_()
+    barrier()
+
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    w0 = time.perf_counter()
+    for i in range(args.steps):
+        starts[i].record(stream)
+        model.run_device(sid)
+        ends[i].record(stream)
+        flush.zero_()
+    barrier()
+    wall = time.perf_counter() - w0
+    clocks = sampler.stop() if sampler else None
+    dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([dev_ms], dtype=torch.float64, device=f"cuda:{local}")
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    dev_ms_max = float(t.item())
+    value = args.batch * args.steps / (dev_ms_max / 1e3)
+
+    # profiled replay: per-kernel device times for the roofline
+    model.run_profiled(sid)
+    prof = model.profile()
+    conv_ms = sum(ms for (op, ms, fl), k in zip(prof, kinds) if k == 1)
+    conv_fl = sum(fl for (op, ms, fl), k in zip(prof, kinds) if k == 1)
+    conv_launches = sum(1 for k in kinds if k == 1)
+    by_kind = {}
+    for (op, ms, fl), k in zip(prof, kinds):
+        by_kind[k] = by_kind.get(k, 0.0) + ms
+    kind_names = {0: "alias", 1: "tc_conv", 2: "tc_gemm", 3: "depthwise", 4: "direct", 5: "pool", 6: "eltwise",
+                  7: "layout", 8: "winograd"}
+    breakdown = {kind_names.get(k, str(k)): round(v, 4) for k, v in sorted(by_kind.items())}
+
+    # end to end through the C ABI with pinned host buffers
+    barrier()
+    e0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.run_ptr(x_pin.data_ptr(), out_pin.data_ptr())
+    barrier()
+    e2e_s = time.perf_counter() - e0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local}")
+    if pg is not None:
+        pg.all_reduce(te, op=pg.ReduceOp.MAX)
+    e2e_value = args.batch * args.steps / float(te.item())
+
+    peaks, peak_src = measured_peaks()
+    tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    achieved = conv_fl / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_reference_rate(args.depth, args.cpu_seconds)
+        except Exception as e:  # reported, not fatal
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference", "sample": f"failed: {e}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "tf32",
+            "data": "synthetic (He-init fp32 weights, BN stats as configuration 0, N(0,1) input)",
+            "config": {"workload": f"ResNet-{args.depth} batch {args.batch} 3x224x224 (benchmark configuration 3)",
+                       "global_batch": args.batch, "per_gpu_batch": shard, "image": IMAGE,
+                       "parallelism": f"batch sharded over {world} GPU(s), weight replica per GPU, no collectives",
+                       "l2": "flushed between timed steps (256 MiB write, outside the events)",
+                       "graph": "CUDA graph of the planned step list"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+                         "frac": achieved / tf32_peak if tf32_peak else None, "traffic": None,
+                         "kernel": "tc_gemm_kernel (implicit-GEMM conv, tcgen05 kind::tf32)",
+                         "peak_source": f"{peak_src}: bf16_tflops_sustained / 2 (dense tf32)",
+                         "launches_per_step": conv_launches,
+                         "flops_per_launch_avg": conv_fl / max(conv_launches, 1),
+                         "ms_per_launch_avg": conv_ms / max(conv_launches, 1)},
+            "model_tflops": flops_per_step * world / (dev_ms_max / args.steps / 1e3) / 1e12,
+            "breakdown_ms_per_step": breakdown,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(in_bytes) * world,
+                    "d2h_bytes_per_step": int(out_bytes) * world},
+            "gpu_launches": info["kernels"] * args.steps * world,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "plan": {"arena_bytes": info["arena_bytes"], "weight_bytes": info["weight_bytes"],
+                     "steps": info["steps"], "build_s": round(build_s, 1)},
+            "wall_s_timed_region": wall,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

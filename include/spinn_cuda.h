@@ -118,7 +118,8 @@ SpinnCudaModel *spinn_cuda_load_buffer(const void *data, size_t size);
 /* Stage 2: plan and allocate on `device`: one device arena (64-bit offsets; budget
  * max_arena_bytes, 0 = unlimited), weights uploaded and pre-transformed, kernels chosen.
  * Mirrors spinn_plan (spinn_runtime.h:114-123; SPINN_MEM_ERR_NOMEM -> SPINN_CUDA_ENOMEM).
- * flags: bit 0 = do not capture a CUDA graph; bit 1 = profile per node (CUDA events);
+ * flags: bit 0 = do not capture a CUDA graph; bit 1 = also prepare a profiled variant
+ *        (spinn_cuda_run_profiled);
  *        bit 2 = keep activations fp32 on store (no tf32 rounding of conv outputs). */
 #define SPINN_CUDA_PLAN_NO_GRAPH 1
 #define SPINN_CUDA_PLAN_PROFILE 2
@@ -135,6 +136,10 @@ int spinn_cuda_run(SpinnCudaModel *m, const void *input, void *output);
  * not waited for. */
 int spinn_cuda_run_device(SpinnCudaModel *m, void *stream);
 
+/* Profiled run (plan flag PROFILE): the step list with a CUDA event between steps, replayed
+ * from its own captured graph; synchronous.  Per-step device times via spinn_cuda_profile. */
+int spinn_cuda_run_profiled(SpinnCudaModel *m, void *stream);
+
 /* Device buffer of graph input (is_output=0) or output (is_output=1) number `index`,
  * NCHW fp32 as the .ennf declares it, and its size in bytes. */
 void *spinn_cuda_io_ptr(SpinnCudaModel *m, int is_output, int index, size_t *bytes);
@@ -147,7 +152,7 @@ int spinn_cuda_io_dims(SpinnCudaModel *m, int is_output, int index, uint32_t *di
 int spinn_cuda_plan_info(SpinnCudaModel *m, uint64_t *arena_bytes, uint64_t *weight_bytes,
                          int *num_steps, int *num_kernels);
 
-/* Per-node device times of the last run (plan flag PROFILE): fills up to `cap` entries of
+/* Per-step device times of the last profiled run: fills up to `cap` entries of
  * op_type / milliseconds / algorithmic FLOPs; returns the number of entries. */
 int spinn_cuda_profile(SpinnCudaModel *m, int *op_types, float *ms, double *flops, int cap);
 

@@ -141,6 +141,8 @@ struct SpinnCudaModel {
   std::vector<StepRec> steps;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t gexec = nullptr;
+  cudaGraph_t pgraph = nullptr;      // same steps with an event between each (profiling)
+  cudaGraphExec_t pgexec = nullptr;
   std::vector<cudaEvent_t> events;
   std::vector<float> step_ms;
   int kernels = 0;
@@ -1007,14 +1009,15 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
   return 0;
 }
 
-static int run_steps(SpinnCudaModel* m, cudaStream_t st) {
-  const bool prof = (m->flags & SPINN_CUDA_PLAN_PROFILE) != 0;
+static int run_steps(SpinnCudaModel* m, cudaStream_t st, bool prof) {
+  // External records become real event nodes when captured into a graph (a plain record
+  // inside a capture is only an intra-graph dependency marker and is never timestamped).
   for (size_t i = 0; i < m->steps.size(); ++i) {
-    if (prof) cudaEventRecord(m->events[i], st);
+    if (prof) SPINN_CUDA_TRY(cudaEventRecordWithFlags(m->events[i], st, cudaEventRecordExternal));
     int rc = m->steps[i].run(st);
     if (rc) return rc;
   }
-  if (prof) cudaEventRecord(m->events[m->steps.size()], st);
+  if (prof) SPINN_CUDA_TRY(cudaEventRecordWithFlags(m->events[m->steps.size()], st, cudaEventRecordExternal));
   return 0;
 }
 
@@ -1023,6 +1026,8 @@ static void release_model(SpinnCudaModel* m) {
   if (m->device >= 0) cudaSetDevice(m->device);
   if (m->gexec) cudaGraphExecDestroy(m->gexec);
   if (m->graph) cudaGraphDestroy(m->graph);
+  if (m->pgexec) cudaGraphExecDestroy(m->pgexec);
+  if (m->pgraph) cudaGraphDestroy(m->pgraph);
   for (auto e : m->events) cudaEventDestroy(e);
   for (auto& b : m->bufs)
     if (b.external && b.ptr && b.alias < 0) cudaFree(b.ptr);
@@ -1089,26 +1094,57 @@ __attribute__((visibility("default"))) int spinn_cuda_plan(SpinnCudaModel* m, in
     for (auto& e : m->events) SPINN_CUDA_TRY(cudaEventCreate(&e));
   }
   // one eager pass validates every launch; then the step list is captured as a graph
-  rc = run_steps(m, m->stream);
+  rc = run_steps(m, m->stream, false);
   if (rc) return rc;
   SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
   rc = check_device_error_flag(device, m->stream);
   if (rc) return rc;
-  if (!(flags & (SPINN_CUDA_PLAN_NO_GRAPH | SPINN_CUDA_PLAN_PROFILE))) {
-    SPINN_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-    rc = run_steps(m, m->stream);
-    cudaGraph_t g = nullptr;
-    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
-    if (rc) {
-      if (g) cudaGraphDestroy(g);
-      return rc;
+  if (!(flags & SPINN_CUDA_PLAN_NO_GRAPH)) {
+    for (int pass = 0; pass < ((flags & SPINN_CUDA_PLAN_PROFILE) ? 2 : 1); ++pass) {
+      SPINN_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+      rc = run_steps(m, m->stream, pass == 1);
+      cudaGraph_t g = nullptr;
+      cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+      if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      SPINN_CUDA_TRY(e);
+      cudaGraphExec_t ge = nullptr;
+      SPINN_CUDA_TRY(cudaGraphInstantiate(&ge, g, 0));
+      if (pass == 0) {
+        m->graph = g;
+        m->gexec = ge;
+      } else {
+        m->pgraph = g;
+        m->pgexec = ge;
+      }
     }
-    SPINN_CUDA_TRY(e);
-    m->graph = g;
-    SPINN_CUDA_TRY(cudaGraphInstantiate(&m->gexec, g, 0));
   }
   m->planned = true;
   return 0;
+}
+
+// Runs the step list with an event between steps (the event-annotated graph when one was
+// captured) and records every step's device time.
+extern "C" __attribute__((visibility("default"))) int spinn_cuda_run_profiled(SpinnCudaModel* m, void* stream) {
+  if (!m || !m->planned || m->events.empty()) {
+    set_error("spinn_cuda_run_profiled: plan with SPINN_CUDA_PLAN_PROFILE first");
+    return SPINN_CUDA_ESTATE;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(m->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+  if (m->pgexec) {
+    SPINN_CUDA_TRY(cudaGraphLaunch(m->pgexec, st));
+  } else {
+    int rc = run_steps(m, st, true);
+    if (rc) return rc;
+  }
+  SPINN_CUDA_TRY(cudaStreamSynchronize(st));
+  m->step_ms.assign(m->steps.size(), 0.0f);
+  for (size_t i = 0; i < m->steps.size(); ++i)
+    SPINN_CUDA_TRY(cudaEventElapsedTime(&m->step_ms[i], m->events[i], m->events[i + 1]));
+  return check_device_error_flag(m->device, st);
 }
 
 __attribute__((visibility("default"))) int spinn_cuda_run_device(SpinnCudaModel* m, void* stream) {
@@ -1122,14 +1158,7 @@ __attribute__((visibility("default"))) int spinn_cuda_run_device(SpinnCudaModel*
     SPINN_CUDA_TRY(cudaGraphLaunch(m->gexec, st));
     return 0;
   }
-  int rc = run_steps(m, st);
-  if (rc) return rc;
-  if (m->flags & SPINN_CUDA_PLAN_PROFILE) {
-    SPINN_CUDA_TRY(cudaStreamSynchronize(st));
-    m->step_ms.assign(m->steps.size(), 0.0f);
-    for (size_t i = 0; i < m->steps.size(); ++i) cudaEventElapsedTime(&m->step_ms[i], m->events[i], m->events[i + 1]);
-  }
-  return 0;
+  return run_steps(m, st, false);
 }
 
 __attribute__((visibility("default"))) int spinn_cuda_run(SpinnCudaModel* m, const void* input, void* output) {

@@ -173,6 +173,10 @@ class Model:
     def run_device(self, stream: int = 0) -> None:
         check(lib().spinn_cuda_run_device(self._h, stream or None), "spinn_cuda_run_device")
 
+    def run_profiled(self, stream: int = 0) -> None:
+        """One run with per-step device timing (plan with PLAN_PROFILE); synchronous."""
+        check(lib().spinn_cuda_run_profiled(self._h, stream or None), "spinn_cuda_run_profiled")
+
     def plan_info(self) -> dict:
         a, w = ctypes.c_uint64(0), ctypes.c_uint64(0)
         s, k = ctypes.c_int(0), ctypes.c_int(0)
