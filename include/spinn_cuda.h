@@ -106,6 +106,19 @@ int spinn_cuda_gemm(SpinnTensor **in, int n_in, void *params, uint16_t params_si
 int spinn_cuda_matmul(SpinnTensor **in, int n_in, void *params, uint16_t params_size,
                       SpinnTensor **out, int n_out);
 
+/* Convolution that allocates nothing (no counterpart in the reference).  For hosts that must
+ * not allocate device memory while running -- SPINN's own deployment model plans all memory
+ * up front -- this variant of spinn_cuda_conv2d keeps every temporary in one fixed 32 MiB
+ * device array that each GPU loading the library holds until exit.  Arguments are device
+ * pointers (NCHW fp32 x, OIHW w, optional bias[oc], residual like y when fused_act is 4/5)
+ * and the geometry; group 1.  Larger problems return SPINN_CUDA_EINVAL.  The first call on a
+ * device resolves the array's address (make it before any stream capture); calls overlapping
+ * on the GPU share the array and race; the call waits for `stream` before returning. */
+int spinn_cuda_conv2d_noalloc(const float *x, const float *w, const float *bias, const float *residual,
+                              float *y, int n, int c, int h, int w_, int oc, int kh, int kw,
+                              int stride_h, int stride_w, int pad_h, int pad_w, int fused_act,
+                              void *stream);
+
 /* ------------------------------------------------------------------ model level */
 
 typedef struct SpinnCudaModel SpinnCudaModel;

@@ -77,6 +77,7 @@ struct TcGemmArgs {
   int act = 0;
   int round_out = 0;
   int bn = 0;  // 0 = choose
+  int* err = nullptr;  // device error word; nullptr = the per-device flag
 };
 // Checks whether the tcgen05 path accepts the problem (alignment, corner ranges ...).
 bool tc_gemm_supported(const TcGemmArgs& a, std::string* why);

@@ -509,7 +509,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   p.round_out = a.round_out;
   p.alpha = a.alpha;
   p.bias = a.bias;
-  p.err = device_error_flag(dev);
+  p.err = a.err ? a.err : device_error_flag(dev);
   const int grid = (int)std::min<long>(tiles, sms);
   if (a.a_mode == 0) return dispatch_bn_cb<kIm2col>(bn, cb, ma, mb, my, mr, p, grid, stream);
   return dispatch_bn_cb<kTiled>(bn, cb, ma, mb, my, mr, p, grid, stream);

@@ -61,6 +61,7 @@ _SIGS = {
                                        ctypes.c_void_p, ctypes.c_int]),
     "spinn_cuda_matmul": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_uint16,
                                          ctypes.c_void_p, ctypes.c_int]),
+    "spinn_cuda_conv2d_noalloc": (ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 12 + [ctypes.c_void_p]),
     "spinn_cuda_load": (ctypes.c_void_p, [ctypes.c_char_p]),
     "spinn_cuda_load_buffer": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_size_t]),
     "spinn_cuda_plan": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_int]),
