@@ -59,6 +59,24 @@ def parse():
     return ap.parse_args()
 
 
+def shard_bounds(global_batch: int, rank: int, world: int):
+    """[start, stop) of the images rank `rank` processes (even split, no remainder)."""
+    if global_batch % world:
+        raise ValueError(f"global batch {global_batch} not divisible by {world} ranks")
+    per = global_batch // world
+    return rank * per, (rank + 1) * per
+
+
+def reduce_max(value: float, pg, device=None) -> float:
+    """Max of `value` over ranks (identity without a process group)."""
+    if pg is None:
+        return float(value)
+    import torch
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -210,9 +228,8 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         pg = dist
-    if args.batch % world:
-        raise SystemExit(f"global batch {args.batch} not divisible by {world} ranks")
-    shard = args.batch // world
+    start, stop = shard_bounds(args.batch, rank, world)
+    shard = stop - start
 
     t_build = time.time()
     img, flops_per_step = build_model_image(shard, args.depth)
@@ -221,8 +238,8 @@ def main():
     kinds = model.step_kinds()
     build_s = time.time() - t_build
 
-    g = torch.Generator().manual_seed(SEED * 1000 + rank)
-    x = torch.randn((shard, 3, IMAGE, IMAGE), generator=g, dtype=torch.float32)
+    from spinn_b200 import netdef
+    x = torch.from_numpy(netdef.image_batch(start, shard, IMAGE, seed=SEED))
     x_pin = x.pin_memory()
     in_ptr, in_bytes = model.io_ptr(False, 0)
     out_ptr, out_bytes = model.io_ptr(True, 0)
@@ -265,10 +282,7 @@ def main():
     wall = time.perf_counter() - w0
     clocks = sampler.stop() if sampler else None
     dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    t = torch.tensor([dev_ms], dtype=torch.float64, device=f"cuda:{local}")
-    if pg is not None:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    dev_ms_max = float(t.item())
+    dev_ms_max = reduce_max(dev_ms, pg, f"cuda:{local}")
     value = args.batch * args.steps / (dev_ms_max / 1e3)
 
     # profiled replay: per-kernel device times for the roofline
@@ -290,11 +304,8 @@ def main():
     for _ in range(args.steps):
         model.run_ptr(x_pin.data_ptr(), out_pin.data_ptr())
     barrier()
-    e2e_s = time.perf_counter() - e0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local}")
-    if pg is not None:
-        pg.all_reduce(te, op=pg.ReduceOp.MAX)
-    e2e_value = args.batch * args.steps / float(te.item())
+    e2e_s = reduce_max(time.perf_counter() - e0, pg, f"cuda:{local}")
+    e2e_value = args.batch * args.steps / e2e_s
 
     peaks, peak_src = measured_peaks()
     tf32_peak = peaks["bf16_tflops_sustained"] / 2.0

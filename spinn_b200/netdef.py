@@ -260,6 +260,15 @@ def resnet(depth: int = 50, batch: int = 1, image: int = 224, num_classes: int =
     return g
 
 
+def image_batch(start: int, count: int, image: int = 224, seed: int = 3) -> np.ndarray:
+    """Images ``start .. start+count-1`` of a global N(0,1) batch, image i drawn from
+    ``default_rng([seed, i])``: a rank's shard equals the slice of the global batch."""
+    out = np.empty((count, 3, image, image), np.float32)
+    for j in range(count):
+        out[j] = np.random.default_rng([seed, start + j]).standard_normal((3, image, image), dtype=np.float32)
+    return out
+
+
 def resnet_input(batch: int, image: int = 224, seed: int = 2) -> np.ndarray:
     """N(0,1) NCHW input, drawn from ``default_rng(seed + 1)``."""
     return np.random.default_rng(seed + 1).standard_normal((batch, 3, image, image),
