@@ -62,6 +62,28 @@ __global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, float* __restri
   }
 }
 
+// One thread per output pixel (b, i, j): 16 channels = 4 phases (dy, dx) x 4 input channels.
+__global__ void space_to_depth2_kernel(const float* __restrict__ x, float4* __restrict__ y, int n, int c, int h,
+                                       int w, int h2, int w2, int ph, int pw) {
+  const long total = (long)n * h2 * w2;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int j = (int)(i % w2);
+    long t = i / w2;
+    const int r = (int)(t % h2);
+    const int b = (int)(t / h2);
+#pragma unroll
+    for (int ph4 = 0; ph4 < 4; ++ph4) {
+      const int iy = 2 * r + (ph4 >> 1) - ph, ix = 2 * j + (ph4 & 1) - pw;
+      const bool in = iy >= 0 && iy < h && ix >= 0 && ix < w;
+      float v[4];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch)
+        v[ch] = (in && ch < c) ? x[(((size_t)b * c + ch) * h + iy) * w + ix] : 0.0f;
+      y[i * 4 + ph4] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  }
+}
+
 // MaxPool (SPINN/run_time/ops/pool/maxpool.c:5-49): -1e30 start, padded taps skipped.
 __global__ void maxpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
                                     int c4, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw) {
@@ -309,6 +331,15 @@ int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, in
   const int hw = h * w;
   dim3 grid((hw + 31) / 32, (cpad + 31) / 32, n), block(32, 8);
   nchw_to_nhwc_kernel<<<grid, block, 0, s>>>(x, y, c, hw, cpad);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_space_to_depth2(const float* x, float* y, int n, int c, int h, int w, int h2, int w2, int ph, int pw,
+                           cudaStream_t s) {
+  SPINN_CHECK_ARG(c >= 1 && c <= 4, "space_to_depth2: %d channels (at most 4)", c);
+  const long work = (long)n * h2 * w2;
+  space_to_depth2_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(x, reinterpret_cast<float4*>(y), n, c, h,
+                                                                             w, h2, w2, ph, pw);
   SPINN_LAUNCH_CHECK();
 }
 

@@ -87,6 +87,10 @@ inline int tc_num_kb(int K) { return (K + 31) / 32; }
 
 // ------------------------------------------------------------------ glue kernels (glue.cu)
 int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s);
+// NCHW x[n][c][h][w] (c <= 4) -> space-to-depth-2 NHWC y[n][h2][w2][16] with
+// y[..][(dy*2+dx)*4 + ch] = x[n][ch][2i+dy-ph][2j+dx-pw] (zero outside / for ch >= c).
+int launch_space_to_depth2(const float* x, float* y, int n, int c, int h, int w, int h2, int w2, int ph, int pw,
+                           cudaStream_t s);
 int launch_nhwc_to_nchw(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s);
 int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh,
                         int kw, int sh, int sw, int ph, int pw, cudaStream_t s);

@@ -390,7 +390,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     return step++;
   };
 
-  // graph inputs: NCHW staging (external); 4-D inputs get an NHWC arena copy
+  // graph inputs: NCHW staging buffers outside the arena; the tensor aliases its staging and
+  // consumers convert on demand (ensure_nhwc, or the space-to-depth stem below)
   for (size_t i = 0; i < m->inputs.size(); ++i) {
     const int id = m->inputs[i];
     const TensorRec& t = m->tensors[id];
@@ -400,29 +401,21 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     st.external = 1;
     const int sb = P.new_buf(st);
     m->in_buf.push_back(sb);
-    if (t.ndim == 4) {
-      set_nhwc(m->bufs[id], t);
-      const int s = add_step(-1, 0, 7, 0, [m, sb, id](StepRec& r) {
-        const Buf& x = m->bufs[sb];
-        const Buf& y = m->bufs[id];
-        r.run = [&x, &y](cudaStream_t st) { return launch_nchw_to_nhwc(x.ptr, y.ptr, y.n, y.c, y.h, y.w, y.cpad, st); };
-        return 0;
-      });
-      P.touch(id, s);
-    } else {
-      m->bufs[id] = m->bufs[sb];
-      m->bufs[id].external = 0;
-      m->bufs[id].alias = sb;
-    }
+    m->bufs[id] = m->bufs[sb];
+    m->bufs[id].external = 0;
+    m->bufs[id].alias = sb;
     produced[id] = 1;
   }
 
+  std::map<int, int> nhwc_of;  // row-major 4-D tensor id -> its NHWC copy
   auto ensure_nhwc = [&](int id, int node) -> int {
     // returns a buffer index holding tensor `id` in NHWC layout
     Buf& b = m->bufs[id];
     if (b.lay == LAY_NHWC) return id;
     const TensorRec& t = m->tensors[id];
     if (t.ndim != 4) return -1;
+    auto it = nhwc_of.find(id);
+    if (it != nhwc_of.end()) return it->second;
     Buf nb;
     set_nhwc(nb, t);
     const int tb = P.new_buf(nb);
@@ -434,6 +427,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     });
     P.touch(id, s);
     P.touch(tb, s);
+    nhwc_of[id] = tb;
     return tb;
   };
   auto ensure_row = [&](int id, int node) -> int {
@@ -508,7 +502,49 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           set_error("plan: Conv node %d shape mismatch", ni);
           return SPINN_CUDA_EFORMAT;
         }
-        const int xb = ensure_nhwc(nd.in[0], ni);
+        // Space-to-depth stem: a stride-2 convolution over a graph input with <= 4 channels is
+        // run as a stride-1, pad-0 convolution over
+        //   X'[n][i][j][(dy*2+dx)*4 + c] = x[n][c][2i+dy-PH][2j+dx-PW]     (16 channels)
+        // with ceil(KH/2) x ceil(KW/2) taps and W'[o][ky][kx][dy][dx][c] = W[o][c][2ky+dy][2kx+dx].
+        // Same sums; the tensor-core tile then takes 16 channels per tap instead of 4.
+        bool is_input = false;
+        for (auto id : m->inputs) is_input |= (id == nd.in[0]);
+        const bool s2d = G == 1 && SH == 2 && SW == 2 && DH == 1 && DW == 1 && C <= 4 && KH >= 2 && KW >= 2 &&
+                         is_input && m->bufs[nd.in[0]].lay == LAY_ROW;
+        int xb;
+        int Hc = H, Wc = Wd, Cc = round4(C), KHc = KH, KWc = KW, SHc = SH, SWc = SW, PHc = PH, PWc = PW, DHc = DH,
+            DWc = DW;
+        if (s2d) {
+          KHc = (KH + 1) / 2;
+          KWc = (KW + 1) / 2;
+          Hc = OH + KHc - 1;
+          Wc = OW + KWc - 1;
+          Cc = 16;
+          SHc = SWc = 1;
+          PHc = PWc = 0;
+          Buf sb;
+          sb.lay = LAY_NHWC;
+          sb.n = N;
+          sb.c = Cc;
+          sb.cpad = Cc;
+          sb.h = Hc;
+          sb.w = Wc;
+          sb.bytes = (uint64_t)N * Hc * Wc * Cc * 4;
+          xb = P.new_buf(sb);
+          const int src = nd.in[0];
+          const int s = add_step(ni, 0, 7, 0, [=](StepRec& r) {
+            const Buf* x = &m->bufs[src];
+            const Buf* y = &m->bufs[xb];
+            r.run = [=](cudaStream_t st) {
+              return launch_space_to_depth2(x->ptr, y->ptr, N, C, H, Wd, Hc, Wc, PH, PW, st);
+            };
+            return 0;
+          });
+          P.touch(src, s);
+          P.touch(xb, s);
+        } else {
+          xb = ensure_nhwc(nd.in[0], ni);
+        }
         int rb = -1;
         if (has_res) {
           rb = ensure_nhwc(nd.in.back(), ni);
@@ -524,16 +560,19 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         const double fl = conv_flops(W, Y);
         const int rnd = P.round_out;
         if (G == 1) {
-          // tcgen05 implicit GEMM: weights [ocpad][kpad], k = (r*KW + s)*cpad + c
-          const int K = KH * KW * cpad;
+          // tcgen05 implicit GEMM: weights [ocpad][kpad], k = (r*KWc + s)*Cc + c
+          const int K = KHc * KWc * Cc;
           const int kpad = tc_num_kb(K) * 32;
           const uint64_t woff = P.wreserve((uint64_t)ocpad * kpad);
           for (int o = 0; o < OC; ++o)
             for (int c = 0; c < C; ++c)
               for (int r = 0; r < KH; ++r)
-                for (int s = 0; s < KW; ++s)
-                  m->whost[woff + (uint64_t)o * kpad + (r * KW + s) * cpad + c] =
-                      host_round_tf32(W.host[(((uint64_t)o * C + c) * KH + r) * KW + s]);
+                for (int s = 0; s < KW; ++s) {
+                  const float v = host_round_tf32(W.host[(((uint64_t)o * C + c) * KH + r) * KW + s]);
+                  const uint64_t k = s2d ? (uint64_t)((r / 2) * KWc + s / 2) * Cc + ((r % 2) * 2 + s % 2) * 4 + c
+                                         : (uint64_t)(r * KW + s) * cpad + c;
+                  m->whost[woff + (uint64_t)o * kpad + k] = v;
+                }
           uint64_t boff = ~0ull;
           if (B) {
             boff = P.wreserve(ocpad);
@@ -543,21 +582,21 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             TcGemmArgs a;
             a.a_mode = 0;
             a.n = N;
-            a.h = H;
-            a.w = Wd;
-            a.cpad = cpad;
-            a.kh = KH;
-            a.kw = KW;
-            a.sh = SH;
-            a.sw = SW;
-            a.ph = PH;
-            a.pw = PW;
-            a.dh = DH;
-            a.dw = DW;
+            a.h = Hc;
+            a.w = Wc;
+            a.cpad = Cc;
+            a.kh = KHc;
+            a.kw = KWc;
+            a.sh = SHc;
+            a.sw = SWc;
+            a.ph = PHc;
+            a.pw = PWc;
+            a.dh = DHc;
+            a.dw = DWc;
             a.oh = OH;
             a.ow = OW;
             a.M = N * OH * OW;
-            a.K = KH * KW * cpad;
+            a.K = KHc * KWc * Cc;
             a.kpad = kpad;
             a.N = ocpad;
             a.ldy = ocpad;

@@ -52,7 +52,7 @@ struct TcParams {
   int* err;
 };
 
-template <int BN, int CB>
+template <int BN, int CB, bool RES>
 struct Cfg {
   static constexpr int NSUB = kBK / CB;
   static constexpr uint32_t A_SUB = kBM * CB * 4;
@@ -60,8 +60,14 @@ struct Cfg {
   static constexpr uint32_t A_STAGE = kBM * kBK * 4;
   static constexpr uint32_t B_STAGE = BN * kBK * 4;
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
-  static constexpr uint32_t EPI = 4 * 4096 * 2;  // per epilogue warp: 32x32 output + residual staging
-  static constexpr int STAGES = ((kSmemBudget - (int)EPI) / (int)STAGE) > 8 ? 8 : ((kSmemBudget - (int)EPI) / (int)STAGE);
+  // epilogue: two 32x32 fp32 staging blocks per epilogue warp (double-buffered TMA stores)
+  static constexpr uint32_t OUT_BYTES = 2 * 4 * 4096;
+  // residual ring: 128 rows x 32 columns per slot, filled by the residual producer warp
+  static constexpr int RES_SLOTS = RES ? 3 : 0;
+  static constexpr uint32_t RES_SLOT = kBM * 32 * 4;
+  static constexpr uint32_t EPI = OUT_BYTES + RES_SLOTS * RES_SLOT;
+  static constexpr int STAGES_FIT = (kSmemBudget - (int)EPI) / (int)STAGE;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // BN in {64,128,256} -> 128/256/512, powers of two
   static constexpr uint32_t SMEM = STAGES * STAGE + EPI + 256 + 1024;
   static_assert(STAGES >= 2, "pipeline needs two stages");
@@ -84,25 +90,27 @@ __device__ __forceinline__ uint64_t stage_desc(uint32_t stage_addr, int j, uint3
   }
 }
 
-template <int BN, int CB, int MODE>
+template <int BN, int CB, int MODE, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapY, const __grid_constant__ CUtensorMap mapR,
                    const TcParams p) {
-  using C = Cfg<BN, CB>;
+  using C = Cfg<BN, CB, RES>;
   constexpr int STAGES = C::STAGES;
+  constexpr int NRS = C::RES_SLOTS > 0 ? C::RES_SLOTS : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * C::A_STAGE;
-  uint8_t* sOut = sB + STAGES * C::B_STAGE;  // 4 x 4 KiB, 1024-aligned
-  uint8_t* sRes = sOut + 4 * 4096;           // 4 x 4 KiB
-  uint64_t* full = reinterpret_cast<uint64_t*>(sRes + 4 * 4096);
+  uint8_t* sOut = sB + STAGES * C::B_STAGE;  // [2][4 warps][4 KiB], 1024-aligned
+  uint8_t* sRes = sOut + C::OUT_BYTES;       // [RES_SLOTS][16 KiB]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sRes + C::RES_SLOTS * C::RES_SLOT);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* rbar = tempty + 2;
-  uint64_t* drain = rbar + 4;
+  uint64_t* rfull = tempty + 2;
+  uint64_t* rempty = rfull + NRS;
+  uint64_t* drain = rempty + NRS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -117,7 +125,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);
     }
-    for (int w = 0; w < 4; ++w) mbar_init(&rbar[w], 1);
+    for (int r = 0; r < NRS; ++r) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], 4);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -126,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&mapA);
     prefetch_tmap(&mapB);
     prefetch_tmap(&mapY);
-    if (p.has_res) prefetch_tmap(&mapR);
+    if constexpr (RES) prefetch_tmap(&mapR);
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -138,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (A, W)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
@@ -233,12 +244,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(drain, 0, &dummy, kDrainNs);
       }
     }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ residual producer
+    // Streams the residual, 128 rows x 32 columns per slot, ahead of the epilogue so the
+    // loads overlap the main loop instead of sitting on the epilogue's critical path.
+    if constexpr (RES) {
+      if (lane == 0) {
+        int slot = 0;
+        uint32_t ph = 0;
+        uint32_t armed = 0, armed_ph = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+          const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+          const int m0 = tm * kBM, n0 = tn * BN;
+          bool ok = true;
+          for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
+            if (!mbar_wait(&rempty[slot], ph ^ 1, abort_flag, kTimeoutNs)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&rfull[slot], C::RES_SLOT);
+            armed |= 1u << slot;
+            armed_ph = (armed_ph & ~(1u << slot)) | (ph << slot);
+            tma_load_2d(&mapR, &rfull[slot], sRes + slot * C::RES_SLOT, n0 + c * 32, m0);
+            if (++slot == C::RES_SLOTS) {
+              slot = 0;
+              ph ^= 1;
+            }
+          }
+          if (!ok) break;
+        }
+        if (*abort_flag) {
+          volatile int dummy = 0;
+          for (int r = 0; r < C::RES_SLOTS; ++r)
+            if (armed & (1u << r)) mbar_wait(&rfull[r], (armed_ph >> r) & 1, &dummy, kDrainNs);
+        }
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int wq = warp & 3;  // TMEM lane quarter this warp may access
-    float* st_out = reinterpret_cast<float*>(sOut + wq * 4096);
-    float* st_res = reinterpret_cast<float*>(sRes + wq * 4096);
+    int rslot = 0;
     uint32_t rph = 0;
+    uint32_t chunk_no = 0;  // selects the output staging buffer
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
@@ -250,34 +297,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort_flag) break;
       tc_fence_after();
       const int row0 = m0 + wq * 32;
-      if (row0 < p.M) {
-        for (int c = 0; c < BN / 32; ++c) {
-          const int col0 = n0 + c * 32;
-          if (col0 >= p.N) break;
-          if (p.has_res) {
-            if (lane == 0) {
-              fence_proxy_async_smem();
-              mbar_arrive_expect_tx(&rbar[wq], 4096);
-              tma_load_2d(&mapR, &rbar[wq], st_res, col0, row0);
-            }
-            mbar_wait(&rbar[wq], rph, abort_flag, kTimeoutNs);
-            rph ^= 1;
-          }
-          uint32_t r[32];
+      const bool rows_live = row0 < p.M;
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = n0 + c * 32;
+        if (col0 >= p.N) break;
+        const float* res_row = nullptr;
+        if constexpr (RES) {
+          mbar_wait(&rfull[rslot], rph, abort_flag, kTimeoutNs);
           __syncwarp();
+          if (*abort_flag) break;
+          res_row = reinterpret_cast<const float*>(sRes + rslot * C::RES_SLOT) + (wq * 32 + lane) * 32;
+        }
+        if (rows_live) {
+          uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + b * BN + c * 32 + ((uint32_t)(wq * 32) << 16), r);
           tmem_ld_wait();
+          const float bias_lane = (p.bias && col0 + lane < p.N) ? __ldg(p.bias + col0 + lane) : 0.0f;
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = col0 + i;
-            const float bias = (p.bias && col < p.N) ? __ldg(p.bias + col) : 0.0f;
-            v[i] = p.alpha * __uint_as_float(r[i]) + bias;
-          }
-          if (p.has_res) {
+          for (int i = 0; i < 32; ++i) v[i] = p.alpha * __uint_as_float(r[i]) + __shfl_sync(0xffffffffu, bias_lane, i);
+          if constexpr (RES) {
+            const int rr = wq * 32 + lane;  // row inside the 128-row residual slot
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const float4 x = *reinterpret_cast<const float4*>(st_res + lane * 32 + ((j ^ (lane & 7)) * 4));
+              const float4 x = *reinterpret_cast<const float4*>(res_row + ((j ^ (rr & 7)) * 4));
               v[4 * j + 0] += x.x;
               v[4 * j + 1] += x.y;
               v[4 * j + 2] += x.z;
@@ -295,7 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = to_tf32_rna(v[i]);
           }
-          if (lane == 0) tma_store_wait_read0();
+          float* st_out = reinterpret_cast<float*>(sOut + ((chunk_no & 1) * 4 + wq) * 4096);
+          if (lane == 0) tma_store_wait_read<1>();  // the store that used this buffer has read it
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -307,6 +351,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) {
             tma_store_2d(&mapY, st_out, col0, row0);
             tma_store_commit();
+          }
+          ++chunk_no;
+        }
+        if constexpr (RES) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&rempty[rslot]);
+          if (++rslot == C::RES_SLOTS) {
+            rslot = 0;
+            rph ^= 1;
           }
         }
       }
@@ -326,11 +379,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && *abort_flag && p.err) atomicExch(p.err, 1);
 }
 
-template <int BN, int CB, int MODE>
+template <int BN, int CB, int MODE, bool RES>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr,
                    const TcParams& p, int grid, cudaStream_t stream) {
-  using C = Cfg<BN, CB>;
-  auto kern = tc_gemm_kernel<BN, CB, MODE>;
+  using C = Cfg<BN, CB, RES>;
+  auto kern = tc_gemm_kernel<BN, CB, MODE, RES>;
   // The opt-in shared-memory size is a per-device function attribute: set it once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -345,11 +398,11 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return 0;
 }
 
-template <int MODE>
+template <int MODE, bool RES>
 int dispatch_bn_cb(int bn, int cb, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
                    const CUtensorMap& mr, const TcParams& p, int grid, cudaStream_t s) {
 #define SPINN_TC_CASE(BNV, CBV) \
-  if (bn == BNV && cb == CBV) return launch_variant<BNV, CBV, MODE>(ma, mb, my, mr, p, grid, s);
+  if (bn == BNV && cb == CBV) return launch_variant<BNV, CBV, MODE, RES>(ma, mb, my, mr, p, grid, s);
   SPINN_TC_CASE(256, 32) SPINN_TC_CASE(128, 32) SPINN_TC_CASE(64, 32)
   if constexpr (MODE == kIm2col) {
     SPINN_TC_CASE(256, 16) SPINN_TC_CASE(128, 16) SPINN_TC_CASE(64, 16)
@@ -491,7 +544,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (a.res) {
-    rc = encode_tiled_2d(&mr, a.res, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.ldr * 4, 32, 32,
+    rc = encode_tiled_2d(&mr, a.res, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.ldr * 4, 32, kBM,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
@@ -511,8 +564,11 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   p.bias = a.bias;
   p.err = a.err ? a.err : device_error_flag(dev);
   const int grid = (int)std::min<long>(tiles, sms);
-  if (a.a_mode == 0) return dispatch_bn_cb<kIm2col>(bn, cb, ma, mb, my, mr, p, grid, stream);
-  return dispatch_bn_cb<kTiled>(bn, cb, ma, mb, my, mr, p, grid, stream);
+  if (a.a_mode == 0)
+    return a.res ? dispatch_bn_cb<kIm2col, true>(bn, cb, ma, mb, my, mr, p, grid, stream)
+                 : dispatch_bn_cb<kIm2col, false>(bn, cb, ma, mb, my, mr, p, grid, stream);
+  return a.res ? dispatch_bn_cb<kTiled, true>(bn, cb, ma, mb, my, mr, p, grid, stream)
+               : dispatch_bn_cb<kTiled, false>(bn, cb, ma, mb, my, mr, p, grid, stream);
 }
 
 }  // namespace spinn

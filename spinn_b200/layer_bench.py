@@ -1,0 +1,65 @@
+"""Times one fused convolution layer (Conv+BN+ReLU, optionally +residual) through the device
+runtime -- a unit for tuning and for profiling a single kernel.
+
+    python -m spinn_b200.layer_bench --batch 512 --c 256 --hw 14 --oc 256 --k 3 [--residual]
+
+Prints one JSON line: device ms per run (CUDA events around the planned step list, inputs
+resident), algorithmic TFLOP/s of the layer and algorithmic GB/s (input + output
+[+ residual] + weights, each touched once).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--c", type=int, default=256)
+    ap.add_argument("--hw", type=int, default=14)
+    ap.add_argument("--oc", type=int, default=256)
+    ap.add_argument("--k", type=int, default=3)
+    ap.add_argument("--stride", type=int, default=1)
+    ap.add_argument("--residual", action="store_true", help="conv+BN+Add+ReLU (needs c == oc, stride 1)")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+
+    import numpy as np
+    import torch
+
+    from spinn_b200 import ennf, netdef, runtime
+
+    pad = a.k // 2
+    if a.residual:
+        g, x = netdef.conv_bn_add_relu(batch=a.batch, c=a.c, hw=a.hw)
+    else:
+        g, x = netdef.conv_bn_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k, stride=a.stride, pad=pad)
+    model = runtime.Model(ennf.convert(g))
+    model.run(x)  # stages the input on the device
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    for _ in range(a.warmup):
+        model.run_device(stream.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.iters):
+        model.run_device(stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.iters
+    oc = a.c if a.residual else a.oc
+    oh = (a.hw + 2 * pad - a.k) // a.stride + 1
+    flops = 2.0 * a.batch * oc * oh * oh * a.c * a.k * a.k
+    cpad = (a.c + 3) // 4 * 4
+    byts = 4.0 * (a.batch * a.hw * a.hw * cpad + a.batch * oh * oh * oc * (2 if a.residual else 1)
+                  + oc * a.c * a.k * a.k)
+    print(json.dumps({"layer": vars(a), "ms_per_run": ms, "tflops": flops / ms / 1e9, "gbs": byts / ms / 1e6,
+                      "steps": model.plan_info()["steps"]}))
+    model.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
