@@ -312,7 +312,7 @@ __attribute__((visibility("default"))) int spinn_cuda_conv2d(SpinnTensor** in, i
   rc = to_device(in[0], xb, &x);
   if (rc) return rc;
   float* xn = scratch_take(xnb);
-  rc = launch_nchw_to_nhwc(x, xn, g.N, g.C, g.H, g.W, cpad, st);
+  rc = launch_nchw_to_nhwc(x, xn, g.N, g.C, g.H, g.W, cpad, st, /*round_tf32=*/g.G == 1);
   if (rc) return rc;
   float* rn = nullptr;
   if (R) {
@@ -471,6 +471,10 @@ __attribute__((visibility("default"))) int spinn_cuda_gemm(SpinnTensor** in, int
   float* a_use = const_cast<float*>(a_rm);
   if (Kp != K) {
     rc = repitch(a_rm, M, K, Kp, &a_use, st);
+    if (rc) return rc;
+  }
+  if (a_use != A->data) {  // a private copy: round the MMA operand to nearest tf32
+    rc = launch_round_tf32(a_use, (long)M * Kp, st);
     if (rc) return rc;
   }
   // B -> K-major [Np][kpad], tf32-rounded; cached when B is a weight

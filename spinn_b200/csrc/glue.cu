@@ -28,7 +28,8 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 }
 
 // [n][c][hw] -> [n][hw][cpad] through a 32x33 shared tile; channels >= c are written as 0.
-__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int c, int hw, int cpad) {
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int c, int hw, int cpad,
+                                    int round_tf32) {
   __shared__ float tile[32][33];
   const int n = blockIdx.z;
   const int hw0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
@@ -41,7 +42,10 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restri
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int p = hw0 + i, cc = c0 + threadIdx.x;
-    if (p < hw && cc < cpad) yn[(size_t)p * cpad + cc] = tile[threadIdx.x][i];
+    if (p < hw && cc < cpad) {
+      const float v = tile[threadIdx.x][i];
+      yn[(size_t)p * cpad + cc] = round_tf32 ? to_tf32_rna(v) : v;
+    }
   }
 }
 
@@ -64,7 +68,7 @@ __global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, float* __restri
 
 // One thread per output pixel (b, i, j): 16 channels = 4 phases (dy, dx) x 4 input channels.
 __global__ void space_to_depth2_kernel(const float* __restrict__ x, float4* __restrict__ y, int n, int c, int h,
-                                       int w, int h2, int w2, int ph, int pw) {
+                                       int w, int h2, int w2, int ph, int pw, int round_tf32) {
   const long total = (long)n * h2 * w2;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int j = (int)(i % w2);
@@ -79,6 +83,10 @@ __global__ void space_to_depth2_kernel(const float* __restrict__ x, float4* __re
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch)
         v[ch] = (in && ch < c) ? x[(((size_t)b * c + ch) * h + iy) * w + ix] : 0.0f;
+      if (round_tf32) {
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) v[ch] = to_tf32_rna(v[ch]);
+      }
       y[i * 4 + ph4] = make_float4(v[0], v[1], v[2], v[3]);
     }
   }
@@ -148,7 +156,8 @@ __global__ void avgpool_nhwc_kernel(const float4* __restrict__ x, float4* __rest
 
 // GlobalAveragePool (SPINN/run_time/ops/pool/global_avg_pool.c:4-28): sequential fp32 sum
 // over the spatial positions in order, then one division -- the reference's exact order.
-__global__ void gap_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int n, int hw, int cpad) {
+__global__ void gap_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int n, int hw, int cpad,
+                                int round_tf32) {
   const long total = (long)n * cpad;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int c = (int)(i % cpad);
@@ -156,7 +165,8 @@ __global__ void gap_nhwc_kernel(const float* __restrict__ x, float* __restrict__
     const float* p = x + (size_t)b * hw * cpad + c;
     float s = 0.0f;
     for (int k = 0; k < hw; ++k) s += p[(size_t)k * cpad];
-    y[i] = s / (float)hw;
+    const float v = s / (float)hw;
+    y[i] = round_tf32 ? to_tf32_rna(v) : v;
   }
 }
 
@@ -327,19 +337,20 @@ __global__ void round_tf32_kernel(float* x, long n) {
     return 0;                                                                       \
   } while (0)
 
-int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s) {
+int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s,
+                        int round_tf32) {
   const int hw = h * w;
   dim3 grid((hw + 31) / 32, (cpad + 31) / 32, n), block(32, 8);
-  nchw_to_nhwc_kernel<<<grid, block, 0, s>>>(x, y, c, hw, cpad);
+  nchw_to_nhwc_kernel<<<grid, block, 0, s>>>(x, y, c, hw, cpad, round_tf32);
   SPINN_LAUNCH_CHECK();
 }
 
 int launch_space_to_depth2(const float* x, float* y, int n, int c, int h, int w, int h2, int w2, int ph, int pw,
-                           cudaStream_t s) {
+                           cudaStream_t s, int round_tf32) {
   SPINN_CHECK_ARG(c >= 1 && c <= 4, "space_to_depth2: %d channels (at most 4)", c);
   const long work = (long)n * h2 * w2;
   space_to_depth2_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(x, reinterpret_cast<float4*>(y), n, c, h,
-                                                                             w, h2, w2, ph, pw);
+                                                                             w, h2, w2, ph, pw, round_tf32);
   SPINN_LAUNCH_CHECK();
 }
 
@@ -369,9 +380,9 @@ int launch_avgpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad,
   SPINN_LAUNCH_CHECK();
 }
 
-int launch_gap_nhwc(const float* x, float* y, int n, int hw, int cpad, cudaStream_t s) {
+int launch_gap_nhwc(const float* x, float* y, int n, int hw, int cpad, cudaStream_t s, int round_tf32) {
   const long work = (long)n * cpad;
-  gap_nhwc_kernel<<<grid_for(work, 128), 128, 0, s>>>(x, y, n, hw, cpad);
+  gap_nhwc_kernel<<<grid_for(work, 128), 128, 0, s>>>(x, y, n, hw, cpad, round_tf32);
   SPINN_LAUNCH_CHECK();
 }
 

@@ -86,17 +86,20 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);
 inline int tc_num_kb(int K) { return (K + 31) / 32; }
 
 // ------------------------------------------------------------------ glue kernels (glue.cu)
-int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s);
+// round_tf32: round values to tf32 (nearest, ties away) on the way, for tensors that feed an
+// MMA operand (the tensor core would otherwise truncate them, a bias that compounds over layers).
+int launch_nchw_to_nhwc(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s,
+                        int round_tf32 = 0);
 // NCHW x[n][c][h][w] (c <= 4) -> space-to-depth-2 NHWC y[n][h2][w2][16] with
 // y[..][(dy*2+dx)*4 + ch] = x[n][ch][2i+dy-ph][2j+dx-pw] (zero outside / for ch >= c).
 int launch_space_to_depth2(const float* x, float* y, int n, int c, int h, int w, int h2, int w2, int ph, int pw,
-                           cudaStream_t s);
+                           cudaStream_t s, int round_tf32 = 0);
 int launch_nhwc_to_nchw(const float* x, float* y, int n, int c, int h, int w, int cpad, cudaStream_t s);
 int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh,
                         int kw, int sh, int sw, int ph, int pw, cudaStream_t s);
 int launch_avgpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh,
                         int kw, int sh, int sw, int ph, int pw, int count_include_pad, cudaStream_t s);
-int launch_gap_nhwc(const float* x, float* y, int n, int hw, int cpad, cudaStream_t s);
+int launch_gap_nhwc(const float* x, float* y, int n, int hw, int cpad, cudaStream_t s, int round_tf32 = 0);
 // y = op(a, b) elementwise with modulo broadcast (SPINN/run_time/ops/math/add.c:4-22).
 enum EltOp { ELT_ADD = 0, ELT_MUL = 1, ELT_SUB = 2, ELT_DIV = 3 };
 int launch_binary(const float* a, long na, const float* b, long nb, float* y, long n, int op, int act,

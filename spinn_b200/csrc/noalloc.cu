@@ -116,7 +116,7 @@ extern "C" __attribute__((visibility("default"))) int spinn_cuda_conv2d_noalloc(
   float* rs = has_res ? reinterpret_cast<float*>(base + kErrSlot + xb + wb + bb + yb) : nullptr;
 
   SPINN_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
-  rc = launch_nchw_to_nhwc(x, xs, n, c, h, wd, cpad, st);
+  rc = launch_nchw_to_nhwc(x, xs, n, c, h, wd, cpad, st, /*round_tf32=*/1);
   if (rc) return rc;
   const long wtotal = (long)ocpad * kpad;
   weight_km_kernel<<<(int)std::min<long>((wtotal + 255) / 256, 148 * 8), 256, 0, st>>>(w, ws, oc, c, kh, kw, cpad,

@@ -419,10 +419,13 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     Buf nb;
     set_nhwc(nb, t);
     const int tb = P.new_buf(nb);
-    const int s = add_step(node, 0, 7, 0, [m, id, tb](StepRec& r) {
+    const int rnd = P.round_out;
+    const int s = add_step(node, 0, 7, 0, [m, id, tb, rnd](StepRec& r) {
       const Buf& x = m->bufs[id];
       const Buf& y = m->bufs[tb];
-      r.run = [&x, &y](cudaStream_t st) { return launch_nchw_to_nhwc(x.ptr, y.ptr, y.n, y.c, y.h, y.w, y.cpad, st); };
+      r.run = [&x, &y, rnd](cudaStream_t st) {
+        return launch_nchw_to_nhwc(x.ptr, y.ptr, y.n, y.c, y.h, y.w, y.cpad, st, rnd);
+      };
       return 0;
     });
     P.touch(id, s);
@@ -532,11 +535,12 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           sb.bytes = (uint64_t)N * Hc * Wc * Cc * 4;
           xb = P.new_buf(sb);
           const int src = nd.in[0];
+          const int rnd_in = P.round_out;
           const int s = add_step(ni, 0, 7, 0, [=](StepRec& r) {
             const Buf* x = &m->bufs[src];
             const Buf* y = &m->bufs[xb];
             r.run = [=](cudaStream_t st) {
-              return launch_space_to_depth2(x->ptr, y->ptr, N, C, H, Wd, Hc, Wc, PH, PW, st);
+              return launch_space_to_depth2(x->ptr, y->ptr, N, C, H, Wd, Hc, Wc, PH, PW, st, rnd_in);
             };
             return 0;
           });
@@ -713,10 +717,13 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         }
         const int yb = nd.out[0];
         set_nhwc(m->bufs[yb], Y);  // [N, C, 1, 1] -> NHWC == [N][cpad]
+        const int rnd = P.round_out;
         const int s = add_step(ni, nd.op, 5, 0, [=](StepRec& r) {
           const Buf* x = &m->bufs[xb];
           const Buf* y = &m->bufs[yb];
-          r.run = [=](cudaStream_t st) { return launch_gap_nhwc(x->ptr, y->ptr, x->n, x->h * x->w, x->cpad, st); };
+          r.run = [=](cudaStream_t st) {
+            return launch_gap_nhwc(x->ptr, y->ptr, x->n, x->h * x->w, x->cpad, st, rnd);
+          };
           return 0;
         });
         P.touch(xb, s);

@@ -64,3 +64,26 @@ def test_resnet50_end_to_end(cuda_lib, ref_oracle, tmp_path):
     assert rel_l2(y, ref) <= 2e-3, rel_l2(y, ref)
     assert err <= 1e-2 * scale, (err, scale)
     assert (y.argmax(1) == ref.argmax(1)).all()
+
+
+def test_reference_runtime_dispatches_to_cuda_operators(cuda_lib, ref_oracle, tmp_path):
+    """Drop-in check: the reference's own spinn_load/spinn_plan/spinn_run (oracle/_ref, host
+    arena) with Conv, Gemm and MatMul registered to libspinn_cuda's SpinnOpKernel entry points
+    through spinn_cuda_register, against the same runtime on its CPU operators."""
+    import ctypes
+
+    from spinn_b200 import ennf, lib, netdef
+    g = netdef.resnet(50, batch=1, seed=2)
+    x = netdef.resnet_input(1, seed=2)
+    cpu = list(_ref_outputs(ref_oracle, ennf.convert(g), x, tmp_path).values())[0]
+    L = lib.lib()
+    assert L.spinn_cuda_register(ctypes.c_void_p(ref_oracle.register_op_fn())) == 3
+    try:
+        gpu = list(_ref_outputs(ref_oracle, ennf.convert(g), x, tmp_path).values())[0]
+    finally:
+        ref_oracle.clear_overrides()
+    assert L.spinn_cuda_sync() == 0
+    scale = float(np.abs(cpu).max())
+    assert rel_l2(gpu, cpu) <= 2e-3, rel_l2(gpu, cpu)
+    assert float(np.abs(gpu - cpu).max()) <= 1e-2 * scale
+    assert gpu.argmax() == cpu.argmax()
