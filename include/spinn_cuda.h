@@ -133,10 +133,12 @@ SpinnCudaModel *spinn_cuda_load_buffer(const void *data, size_t size);
  * Mirrors spinn_plan (spinn_runtime.h:114-123; SPINN_MEM_ERR_NOMEM -> SPINN_CUDA_ENOMEM).
  * flags: bit 0 = do not capture a CUDA graph; bit 1 = also prepare a profiled variant
  *        (spinn_cuda_run_profiled);
- *        bit 2 = keep activations fp32 on store (no tf32 rounding of conv outputs). */
+ *        bit 2 = keep activations fp32 on store (no tf32 rounding of conv outputs);
+ *        bit 3 = Winograd F(4x4,3x3) for 3x3 stride-1 group-1 convolutions. */
 #define SPINN_CUDA_PLAN_NO_GRAPH 1
 #define SPINN_CUDA_PLAN_PROFILE 2
 #define SPINN_CUDA_PLAN_NO_ROUND 4
+#define SPINN_CUDA_PLAN_WINOGRAD 8 /* run 3x3 stride-1 convolutions with Winograd F(4x4,3x3) */
 int spinn_cuda_plan(SpinnCudaModel *m, int device, uint64_t max_arena_bytes, int flags);
 
 /* Stage 3: run one inference.  Copies input 0 (NCHW fp32, host memory) to the device, runs

@@ -85,6 +85,27 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);
 // Number of K blocks (32 wide) and padded K the weight matrix must have.
 inline int tc_num_kb(int K) { return (K + 31) / 32; }
 
+// ------------------------------------------------------------------ Winograd F(4x4,3x3) (winograd.cu)
+// 3x3 stride-1 convolution of NHWC x[n][h][w][cpad] into y[n][oh][ow][ocpad] through the
+// transform buffers v [36][tiles][3*cpad] and m [36][tiles][ocpad]
+// (tiles = n*ceil(oh/4)*ceil(ow/4)) and transformed weights u [36][ocpad][kpad],
+// kpad = 32-multiple >= 3*cpad (winograd_f43_weights; split-tf32 products).
+struct WinogradArgs {
+  const float* x = nullptr;
+  int n = 0, h = 0, w = 0, cpad = 0, oh = 0, ow = 0, ph = 1, pw = 1;
+  const float* u = nullptr;
+  int ocpad = 0, kpad = 0;
+  float* v = nullptr;
+  float* m = nullptr;
+  const float* bias = nullptr;
+  const float* res = nullptr;
+  float* y = nullptr;
+  int act = 0, round_out = 0;
+};
+inline long winograd_tiles(int n, int oh, int ow) { return (long)n * ((oh + 3) / 4) * ((ow + 3) / 4); }
+void winograd_f43_weights(const float* w, int oc, int c, int cpad, int ocpad, int kpad, float* u);
+int winograd_f43_run(const WinogradArgs& a, cudaStream_t s);
+
 // ------------------------------------------------------------------ glue kernels (glue.cu)
 // round_tf32: round values to tf32 (nearest, ties away) on the way, for tensors that feed an
 // MMA operand (the tensor core would otherwise truncate them, a bias that compounds over layers).

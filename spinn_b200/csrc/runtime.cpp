@@ -563,7 +563,61 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         const TensorRec* B = (n_real > 2 && m->tensors[nd.in[2]].host) ? &m->tensors[nd.in[2]] : nullptr;
         const double fl = conv_flops(W, Y);
         const int rnd = P.round_out;
-        if (G == 1) {
+        const bool wino = (m->flags & SPINN_CUDA_PLAN_WINOGRAD) && G == 1 && !s2d && KH == 3 && KW == 3 && SH == 1 &&
+                          SW == 1 && DH == 1 && DW == 1;
+        if (wino) {
+          // Winograd F(4x4,3x3): transforms in HBM, 36 tcgen05 GEMMs (winograd.cu)
+          const int kpad = tc_num_kb(3 * cpad) * 32;
+          const uint64_t woff = P.wreserve((uint64_t)36 * ocpad * kpad);
+          winograd_f43_weights(W.host, OC, C, cpad, ocpad, kpad, &m->whost[woff]);
+          uint64_t boff = ~0ull;
+          if (B) {
+            boff = P.wreserve(ocpad);
+            for (int o = 0; o < OC; ++o) m->whost[boff + o] = B->host[o];
+          }
+          const long tiles = winograd_tiles(N, OH, OW);
+          Buf vb, mb;
+          vb.lay = mb.lay = LAY_ROW;
+          vb.bytes = (uint64_t)36 * tiles * 3 * cpad * 4;
+          mb.bytes = (uint64_t)36 * tiles * ocpad * 4;
+          const int vbi = P.new_buf(vb), mbi = P.new_buf(mb);
+          const int s = add_step(ni, OP_CONV, 8, fl, [=](StepRec& r) {
+            const Buf* xbp = &m->bufs[xb];
+            const Buf* ybp = &m->bufs[yb];
+            const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
+            const Buf* vp = &m->bufs[vbi];
+            const Buf* mp = &m->bufs[mbi];
+            r.run = [=](cudaStream_t st) {
+              WinogradArgs a;
+              a.x = xbp->ptr;
+              a.n = N;
+              a.h = H;
+              a.w = Wd;
+              a.cpad = cpad;
+              a.oh = OH;
+              a.ow = OW;
+              a.ph = PH;
+              a.pw = PW;
+              a.u = m->wdev + woff;
+              a.ocpad = ocpad;
+              a.kpad = kpad;
+              a.v = vp->ptr;
+              a.m = mp->ptr;
+              a.bias = boff != ~0ull ? m->wdev + boff : nullptr;
+              a.res = rbp ? rbp->ptr : nullptr;
+              a.y = ybp->ptr;
+              a.act = act;
+              a.round_out = rnd;
+              return winograd_f43_run(a, st);
+            };
+            return 0;
+          });
+          P.touch(xb, s);
+          P.touch(yb, s);
+          P.touch(vbi, s);
+          P.touch(mbi, s);
+          if (rb >= 0) P.touch(rb, s);
+        } else if (G == 1) {
           // tcgen05 implicit GEMM: weights [ocpad][kpad], k = (r*KWc + s)*Cc + c
           const int K = KHc * KWc * Cc;
           const int kpad = tc_num_kb(K) * 32;

@@ -22,6 +22,7 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=3)
     ap.add_argument("--stride", type=int, default=1)
     ap.add_argument("--residual", action="store_true", help="conv+BN+Add+ReLU (needs c == oc, stride 1)")
+    ap.add_argument("--winograd", action="store_true", help="plan with Winograd F(4x4,3x3)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
@@ -36,7 +37,8 @@ def main(argv=None):
         g, x = netdef.conv_bn_add_relu(batch=a.batch, c=a.c, hw=a.hw)
     else:
         g, x = netdef.conv_bn_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k, stride=a.stride, pad=pad)
-    model = runtime.Model(ennf.convert(g))
+    from spinn_b200 import lib
+    model = runtime.Model(ennf.convert(g), flags=lib.PLAN_WINOGRAD if a.winograd else 0)
     model.run(x)  # stages the input on the device
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)

@@ -87,3 +87,34 @@ def test_reference_runtime_dispatches_to_cuda_operators(cuda_lib, ref_oracle, tm
     assert rel_l2(gpu, cpu) <= 2e-3, rel_l2(gpu, cpu)
     assert float(np.abs(gpu - cpu).max()) <= 1e-2 * scale
     assert gpu.argmax() == cpu.argmax()
+
+
+@pytest.mark.parametrize("case", [(1, 64, 56, 64, "Relu"), (2, 32, 15, 48, "Relu"), (2, 16, 9, 16, "SiLU")])
+def test_winograd_f43_conv_vs_reference(cuda_lib, ref_oracle, tmp_path, case):
+    """3x3 stride-1 convolutions through Winograd F(4x4,3x3) (plan flag WINOGRAD), including
+    output sizes that are not multiples of the 4x4 tile."""
+    from spinn_b200 import ennf, lib, netdef, runtime
+    n, c, hw, oc, act = case
+    g, x = netdef.conv_bn_relu(batch=n, c=c, hw=hw, oc=oc, act=act)
+    img = ennf.convert(g)
+    ref = list(_ref_outputs(ref_oracle, img, x, tmp_path).values())[0]
+    m = runtime.Model(img, flags=lib.PLAN_WINOGRAD)
+    assert 8 in m.step_kinds()
+    y = m.run(x).ravel()
+    assert rel_l2(y, ref) <= 2e-3, rel_l2(y, ref)
+
+
+def test_winograd_residual_and_resnet50(cuda_lib, ref_oracle, tmp_path):
+    from spinn_b200 import ennf, lib, netdef, runtime
+    g, x = netdef.conv_bn_add_relu(batch=2, c=64, hw=28)
+    img = ennf.convert(g)
+    ref = list(_ref_outputs(ref_oracle, img, x, tmp_path).values())[0]
+    y = runtime.Model(img, flags=lib.PLAN_WINOGRAD).run(x).ravel()
+    assert rel_l2(y, ref) <= 2e-3, rel_l2(y, ref)
+    g = netdef.resnet(50, batch=2, seed=2)
+    x = netdef.resnet_input(2, seed=2)
+    img = ennf.convert(g)
+    ref = list(_ref_outputs(ref_oracle, img, x, tmp_path).values())[0].reshape(2, -1)
+    y = runtime.Model(img, flags=lib.PLAN_WINOGRAD).run(x).reshape(2, -1)
+    assert rel_l2(y, ref) <= 2e-3, rel_l2(y, ref)
+    assert (y.argmax(1) == ref.argmax(1)).all()
