@@ -21,6 +21,7 @@ import numpy as np
 # AttributeProto.AttributeType
 _ATTR_FLOAT, _ATTR_INT, _ATTR_STRING, _ATTR_INTS = 1, 2, 3, 7
 _FLOAT32 = 1
+_INT64 = 7
 
 
 def _varint(v: int) -> bytes:
@@ -77,9 +78,10 @@ def _attribute(name: str, value) -> bytes:
 
 
 def _tensor(name: str, arr: np.ndarray) -> bytes:
-    arr = np.ascontiguousarray(arr, dtype=np.float32)
+    is_int = np.asarray(arr).dtype.kind in "iu"
+    arr = np.ascontiguousarray(arr, dtype=np.int64 if is_int else np.float32)
     msg = _f_packed_varints(1, arr.shape) if arr.ndim else b""
-    msg += _f_varint(2, _FLOAT32) + _f_str(8, name) + _f_bytes(9, arr.tobytes())
+    msg += _f_varint(2, _INT64 if is_int else _FLOAT32) + _f_str(8, name) + _f_bytes(9, arr.tobytes())
     return msg
 
 

@@ -27,6 +27,7 @@ struct DevWeight {
   float* w = nullptr;
   float* b = nullptr;
   int kpad = 0;
+  uint64_t sig = 0;  // content signature of the source tensor(s) when prepared
 };
 
 struct Session {
@@ -102,16 +103,56 @@ int to_device(const SpinnTensor* t, size_t bytes, const float** dptr) {
 
 enum WKind { W_TC = 0, W_DW = 1, W_GROUPED = 2, W_GEMM_B = 3 };
 
+// Signature of a tensor's contents from up to 257 evenly spaced elements (FNV-1a over the
+// bit patterns and the element count).  Cached weights are keyed by data pointer, like the
+// reference's per-tensor packed copy (SpinnTensor.packed_data); a host buffer freed and reused
+// at the same address by another model would otherwise be served stale, so each lookup
+// re-checks the signature and re-prepares on a mismatch.
+uint64_t content_sig(const SpinnTensor* t) {
+  const uint64_t n = t->elem_count;
+  if (!t->data || n == 0) return 0;
+  const uint64_t stride = n > 256 ? n / 256 : 1;
+  const uint64_t cnt = (n - 1) / stride + 1;
+  std::vector<uint32_t> v(cnt);
+  if (is_device_ptr(t->data)) {
+    if (cudaMemcpy2D(v.data(), 4, t->data, stride * 4, 4, cnt, cudaMemcpyDeviceToHost) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+  } else {
+    const uint32_t* p = static_cast<const uint32_t*>(t->data);
+    for (uint64_t i = 0; i < cnt; ++i) v[i] = p[i * stride];
+  }
+  uint64_t h = 1469598103934665603ull ^ n;
+  for (uint32_t x : v) {
+    h ^= x;
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+void release(DevWeight& d) {
+  if (d.w) cudaFree(d.w);
+  if (d.b) cudaFree(d.b);
+  d = DevWeight();
+}
+
 // Conv weights for the chosen kernel, cached.
 int conv_weights(const SpinnTensor* W, const SpinnTensor* B, int kind, int C, int cpad, int OC, int KH, int KW, int G,
                  DevWeight** out) {
   Session& S = g_sess;
   auto key = std::make_tuple((const void*)W->data, (uint64_t)W->elem_count * 1000003ull + (B ? (uint64_t)(uintptr_t)B->data : 0),
                              kind, cpad);
+  const uint64_t sig = content_sig(W) * 31 + (B ? content_sig(B) : 0);
   auto it = S.wcache.find(key);
   if (it != S.wcache.end()) {
-    *out = &it->second;
-    return 0;
+    if (it->second.sig == sig) {
+      *out = &it->second;
+      return 0;
+    }
+    SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));  // queued work may still read the old copy
+    release(it->second);
+    S.wcache.erase(it);
   }
   std::vector<float> w, b;
   int rc = fetch_host(W, &w);
@@ -151,6 +192,7 @@ int conv_weights(const SpinnTensor* W, const SpinnTensor* B, int kind, int C, in
   for (int o = 0; o < OC && B; ++o) hb[o] = b[o];
   SPINN_CUDA_TRY(cudaMalloc(&dw.b, hb.size() * 4));
   SPINN_CUDA_TRY(cudaMemcpy(dw.b, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice));
+  dw.sig = sig;
   auto ins = S.wcache.emplace(key, dw);
   *out = &ins.first->second;
   return 0;
@@ -255,10 +297,7 @@ __attribute__((visibility("default"))) void spinn_cuda_shutdown(void) {
   if (!S.ready) return;
   cudaSetDevice(S.device);
   cudaStreamSynchronize(S.stream);
-  for (auto& kv : S.wcache) {
-    cudaFree(kv.second.w);
-    cudaFree(kv.second.b);
-  }
+  for (auto& kv : S.wcache) release(kv.second);
   S.wcache.clear();
   if (S.scratch) cudaFree(S.scratch);
   S.scratch = nullptr;
@@ -482,7 +521,14 @@ __attribute__((visibility("default"))) int spinn_cuda_gemm(SpinnTensor** in, int
   if (Bt->is_weight) {
     Session& S = g_sess;
     auto key = std::make_tuple((const void*)Bt->data, (uint64_t)Bt->elem_count, (int)W_GEMM_B, transB);
+    const uint64_t sig = content_sig(Bt);
     auto it = S.wcache.find(key);
+    if (it != S.wcache.end() && it->second.sig != sig) {
+      SPINN_CUDA_TRY(cudaStreamSynchronize(st));
+      release(it->second);
+      S.wcache.erase(it);
+      it = S.wcache.end();
+    }
     if (it == S.wcache.end()) {
       std::vector<float> hb;
       rc = fetch_host(Bt, &hb);
@@ -493,6 +539,7 @@ __attribute__((visibility("default"))) int spinn_cuda_gemm(SpinnTensor** in, int
           w[(size_t)n * kpad + k] = host_round_tf32(transB ? hb[(size_t)n * K + k] : hb[(size_t)k * N + n]);
       DevWeight dw;
       dw.kpad = kpad;
+      dw.sig = sig;
       SPINN_CUDA_TRY(cudaMalloc(&dw.w, w.size() * 4));
       SPINN_CUDA_TRY(cudaMemcpy(dw.w, w.data(), w.size() * 4, cudaMemcpyHostToDevice));
       it = S.wcache.emplace(key, dw).first;

@@ -305,6 +305,60 @@ __global__ void grouped_kernel(const float* __restrict__ x, const float* __restr
   }
 }
 
+__global__ void resize_nearest_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
+                                      int c4, int oh, int ow) {
+  const long total = (long)n * oh * ow * c4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int cq = (int)(i % c4);
+    long t = i / c4;
+    const int ox = (int)(t % ow);
+    t /= ow;
+    const int oy = (int)(t % oh);
+    const int b = (int)(t / oh);
+    const int iy = (int)((long)oy * h / oh), ix = (int)((long)ox * w / ow);
+    y[i] = x[(((size_t)b * h + iy) * w + ix) * c4 + cq];
+  }
+}
+
+struct PermuteArgs {
+  int ndim;
+  long out_dims[8];
+  long in_stride_of_out[8];  // input element stride for a step along each output dimension
+};
+
+__global__ void permute_kernel(const float* __restrict__ x, float* __restrict__ y, long total, PermuteArgs a) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    long rem = i, src = 0;
+    for (int d = a.ndim - 1; d >= 0; --d) {
+      const long c = rem % a.out_dims[d];
+      rem /= a.out_dims[d];
+      src += c * a.in_stride_of_out[d];
+    }
+    y[i] = x[src];
+  }
+}
+
+// One warp per (outer, inner) row: max, sum of exp, normalise (three passes over dim).
+__global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ y, long outer, int dim, long inner) {
+  const long rows = outer * inner;
+  const int lane = threadIdx.x & 31;
+  const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  for (long r = warp; r < rows; r += nwarps) {
+    const long o = r / inner, in = r - o * inner;
+    const float* xr = x + o * dim * inner + in;
+    float* yr = y + o * dim * inner + in;
+    float m = -INFINITY;
+    for (int j = lane; j < dim; j += 32) m = fmaxf(m, xr[(long)j * inner]);
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float sum = 0.0f;
+    for (int j = lane; j < dim; j += 32) sum += expf(xr[(long)j * inner] - m);
+    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float inv = 1.0f / sum;
+    for (int j = lane; j < dim; j += 32) yr[(long)j * inner] = expf(xr[(long)j * inner] - m) * inv;
+  }
+}
+
 __global__ void transpose_kernel(const float* __restrict__ x, float* __restrict__ y, int rows, int cols) {
   __shared__ float tile[32][33];
   const size_t off = (size_t)blockIdx.z * rows * cols;
@@ -317,6 +371,21 @@ __global__ void transpose_kernel(const float* __restrict__ x, float* __restrict_
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int cc = c0 + i, r = r0 + threadIdx.x;
     if (cc < cols && r < rows) y[off + (size_t)cc * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+__global__ void split_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst, long rows, int cols,
+                                  int src_ld, int seg, int dst_ld, int o0, int o1, int o2) {
+  const long total = rows * cols;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / cols;
+    const int c = (int)(i - r * cols);
+    const float v = src[r * src_ld + c];
+    const float hi = to_tf32_rna(v), lo = to_tf32_rna(v - hi);
+    float* d = dst + r * (long)dst_ld + c;
+    d[0] = o0 ? lo : hi;
+    d[seg] = o1 ? lo : hi;
+    d[2 * (long)seg] = o2 ? lo : hi;
   }
 }
 
@@ -426,9 +495,50 @@ int launch_grouped_nhwc(const float* x, const float* w, const float* bias, const
   SPINN_LAUNCH_CHECK();
 }
 
+int launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow,
+                               cudaStream_t s) {
+  SPINN_CHECK_ARG(cpad % 4 == 0, "resize: channel stride %d not a multiple of 4", cpad);
+  const long work = (long)n * oh * ow * (cpad / 4);
+  resize_nearest_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_permute(const float* x, float* y, int ndim, const uint32_t* dims, const uint8_t* perm, cudaStream_t s) {
+  SPINN_CHECK_ARG(ndim >= 1 && ndim <= 8, "transpose: %d dimensions", ndim);
+  PermuteArgs a;
+  a.ndim = ndim;
+  long in_stride[8];
+  in_stride[ndim - 1] = 1;
+  for (int d = ndim - 2; d >= 0; --d) in_stride[d] = in_stride[d + 1] * dims[d + 1];
+  long total = 1;
+  for (int d = 0; d < ndim; ++d) {
+    SPINN_CHECK_ARG(perm[d] < ndim, "transpose: bad permutation");
+    a.out_dims[d] = dims[perm[d]];
+    a.in_stride_of_out[d] = in_stride[perm[d]];
+    total *= a.out_dims[d];
+  }
+  permute_kernel<<<grid_for(total, kEltThreads), kEltThreads, 0, s>>>(x, y, total, a);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_softmax(const float* x, float* y, long outer, int dim, long inner, cudaStream_t s) {
+  const long rows = outer * inner;
+  softmax_kernel<<<grid_for(rows * 32, kEltThreads), kEltThreads, 0, s>>>(x, y, outer, dim, inner);
+  SPINN_LAUNCH_CHECK();
+}
+
 int launch_transpose(const float* x, float* y, int batch, int rows, int cols, cudaStream_t s) {
   dim3 grid((cols + 31) / 32, (rows + 31) / 32, batch), block(32, 8);
   transpose_kernel<<<grid, block, 0, s>>>(x, y, rows, cols);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_split_tf32(const float* src, float* dst, long rows, int cols, int src_ld, int seg, int dst_ld, int o0,
+                      int o1, int o2, cudaStream_t s) {
+  SPINN_CHECK_ARG(seg >= cols && src_ld >= cols && dst_ld >= 3 * seg, "split_tf32: bad strides");
+  split_tf32_kernel<<<grid_for(rows * cols, kEltThreads), kEltThreads, 0, s>>>(src, dst, rows, cols, src_ld, seg,
+                                                                               dst_ld, o0, o1, o2);
   SPINN_LAUNCH_CHECK();
 }
 

@@ -139,8 +139,22 @@ int launch_grouped_nhwc(const float* x, const float* w, const float* bias, const
                         int n, int h, int wd, int c, int cpad, int oh, int ow, int oc, int ocpad, int kh,
                         int kw, int sh, int sw, int ph, int pw, int dh, int dw, int group, int act,
                         int round_out, cudaStream_t s);
+// Nearest resize, NHWC: y[b][oy][ox] = x[b][oy*h/oh][ox*w/ow] (integer mapping of
+// SPINN/run_time/ops/tensor/resize.c:21-30).
+int launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow,
+                               cudaStream_t s);
+// General row-major permutation (ONNX Transpose), up to 8 dimensions: y = x.transpose(perm).
+int launch_permute(const float* x, float* y, int ndim, const uint32_t* dims, const uint8_t* perm, cudaStream_t s);
+// Softmax over the middle axis of [outer][dim][inner] (SPINN/run_time/ops/activation/softmax.c).
+int launch_softmax(const float* x, float* y, long outer, int dim, long inner, cudaStream_t s);
 // Row-major transpose of `batch` matrices [rows][cols] -> [cols][rows].
 int launch_transpose(const float* x, float* y, int batch, int rows, int cols, cudaStream_t s);
+// Split-tf32 packing of a row-major [rows][cols] matrix (leading dimension src_ld) into
+// dst rows of dst_ld >= 3*seg floats (seg >= cols): segments in `order` (0 = hi, 1 = lo), hi = tf32(v),
+// lo = tf32(v - hi).  With A' = (hi, lo, hi) and B' = (hi, hi, lo), one GEMM over 3*seg gives
+// A_hi B_hi + A_lo B_hi + A_hi B_lo.  Only the first `cols` entries of each segment are written.
+int launch_split_tf32(const float* src, float* dst, long rows, int cols, int src_ld, int seg, int dst_ld, int o0,
+                      int o1, int o2, cudaStream_t s);
 // tf32 round-to-nearest-away in place (weights).
 int launch_round_tf32(float* x, long n, cudaStream_t s);
 

@@ -33,7 +33,8 @@ namespace spinn {
 enum : uint16_t {
   OP_ADD = 4, OP_DIV = 23, OP_MUL = 39, OP_SUB = 50, OP_CONV = 60, OP_AVGPOOL = 80, OP_GAP = 81, OP_MAXPOOL = 85,
   OP_BN = 100, OP_RELU = 130, OP_SIGMOID = 133, OP_GEMM = 160, OP_MATMUL = 161, OP_FLATTEN = 189,
-  OP_IDENTITY = 193, OP_RESHAPE = 197
+  OP_IDENTITY = 193, OP_RESHAPE = 197, OP_SOFTMAX = 134, OP_CONCAT = 183, OP_RESIZE = 198, OP_SPLIT = 206,
+  OP_TRANSPOSE = 211
 };
 constexpr uint32_t kMagic = 0x454E4E46;
 
@@ -1034,6 +1035,289 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         P.touch(xb, s);
         P.touch(yid, s);
         produced[yid] = 1;
+        break;
+      }
+      case OP_CONCAT:
+      case OP_SPLIT: {
+        // Concat (SPINN/run_time/ops/tensor/concat.c) / Split (tensor/split.c) as strided 2-D
+        // copies: along the channel axis of NHWC tensors, or along any axis of row-major ones.
+        const bool is_cat = nd.op == OP_CONCAT;
+        int axis = is_cat ? 1 : 0;
+        if (nd.params.size() >= 4) std::memcpy(&axis, nd.params.data(), 4);
+        const std::vector<uint16_t>& parts = is_cat ? nd.in : nd.out;
+        const int whole = is_cat ? nd.out[0] : nd.in[0];
+        const TensorRec& TW = m->tensors[whole];
+        if (axis < 0) axis += TW.ndim;
+        if (axis < 0 || axis >= TW.ndim) {
+          set_error("plan: %s node %d axis out of range", is_cat ? "Concat" : "Split", ni);
+          return SPINN_CUDA_EFORMAT;
+        }
+        for (auto id : parts)
+          if (m->tensors[id].is_weight) {
+            set_error("plan: Concat/Split node %d with constant operands", ni);
+            return SPINN_CUDA_EUNSUPPORTED;
+          }
+        const bool nhwc = TW.ndim == 4 && axis == 1;
+        std::vector<int> pb;  // buffers of the parts
+        int wb;
+        if (nhwc) {
+          if (is_cat) {
+            for (auto id : parts) pb.push_back(ensure_nhwc(id, ni));
+            wb = whole;
+            set_nhwc(m->bufs[wb], TW);
+          } else {
+            wb = ensure_nhwc(whole, ni);
+            for (auto id : parts) {
+              set_nhwc(m->bufs[id], m->tensors[id]);
+              pb.push_back(id);
+            }
+          }
+        } else {
+          if (is_cat) {
+            for (auto id : parts) pb.push_back(ensure_row(id, ni));
+            wb = whole;
+            set_row(m->bufs[wb], TW);
+          } else {
+            wb = ensure_row(whole, ni);
+            for (auto id : parts) {
+              set_row(m->bufs[id], m->tensors[id]);
+              pb.push_back(id);
+            }
+          }
+        }
+        long outer = 1, inner = 1;
+        for (int d = 0; d < axis; ++d) outer *= TW.dims[d];
+        for (int d = axis + 1; d < TW.ndim; ++d) inner *= TW.dims[d];
+        std::vector<int> sizes;
+        for (auto id : parts) sizes.push_back((int)m->tensors[id].dims[axis]);
+        const int s = add_step(ni, nd.op, 6, 0, [=](StepRec& r) {
+          std::vector<const Buf*> pp;
+          for (int b : pb) pp.push_back(&m->bufs[b]);
+          const Buf* w = &m->bufs[wb];
+          r.run = [=](cudaStream_t st) -> int {
+            size_t off = 0;
+            for (size_t i = 0; i < pp.size(); ++i) {
+              const Buf* p = pp[i];
+              size_t rows, width, wpitch, ppitch;
+              if (nhwc) {
+                rows = (size_t)w->n * w->h * w->w;
+                width = (size_t)sizes[i] * 4;
+                wpitch = (size_t)w->cpad * 4;
+                ppitch = (size_t)p->cpad * 4;
+              } else {
+                rows = outer;
+                width = (size_t)sizes[i] * inner * 4;
+                wpitch = (size_t)(w->bytes / 4 / outer) * 4;
+                ppitch = width;
+              }
+              char* wp = reinterpret_cast<char*>(w->ptr) + off;
+              if (is_cat) {
+                SPINN_CUDA_TRY(cudaMemcpy2DAsync(wp, wpitch, p->ptr, ppitch, width, rows, cudaMemcpyDeviceToDevice, st));
+              } else {
+                if (nhwc && p->cpad != sizes[i])
+                  SPINN_CUDA_TRY(cudaMemsetAsync(p->ptr, 0, p->bytes, st));
+                SPINN_CUDA_TRY(cudaMemcpy2DAsync(p->ptr, ppitch, wp, wpitch, width, rows, cudaMemcpyDeviceToDevice, st));
+              }
+              off += width;
+            }
+            if (is_cat && nhwc && off / 4 != (size_t)w->cpad) {  // zero the channel padding
+              const size_t rows = (size_t)w->n * w->h * w->w;
+              SPINN_CUDA_TRY(cudaMemset2DAsync(reinterpret_cast<char*>(w->ptr) + off, (size_t)w->cpad * 4, 0,
+                                               (size_t)w->cpad * 4 - off, rows, st));
+            }
+            return 0;
+          };
+          return 0;
+        });
+        P.touch(wb, s);
+        for (int b : pb) P.touch(b, s);
+        for (auto id : nd.out) produced[id] = 1;
+        break;
+      }
+      case OP_RESIZE: {
+        const TensorRec& X = m->tensors[nd.in[0]];
+        const TensorRec& Y = m->tensors[nd.out[0]];
+        if (X.ndim != 4 || Y.ndim != 4 || X.dims[0] != Y.dims[0] || X.dims[1] != Y.dims[1]) {
+          set_error("plan: Resize node %d: only 4-D spatial nearest resize is supported", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int xb = ensure_nhwc(nd.in[0], ni);
+        const int yb = nd.out[0];
+        set_nhwc(m->bufs[yb], Y);
+        const int s = add_step(ni, nd.op, 5, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[xb];
+          const Buf* y = &m->bufs[yb];
+          r.run = [=](cudaStream_t st) {
+            return launch_resize_nearest_nhwc(x->ptr, y->ptr, x->n, x->h, x->w, x->cpad, y->h, y->w, st);
+          };
+          return 0;
+        });
+        P.touch(xb, s);
+        P.touch(yb, s);
+        produced[yb] = 1;
+        break;
+      }
+      case OP_TRANSPOSE: {
+        const TensorRec& X = m->tensors[nd.in[0]];
+        uint8_t perm[8];
+        for (int d = 0; d < X.ndim; ++d) perm[d] = (uint8_t)(X.ndim - 1 - d);  // default: reverse
+        if (nd.params.size() >= 9 && nd.params[8] == X.ndim)
+          for (int d = 0; d < X.ndim; ++d) perm[d] = nd.params[d];
+        const int xb = ensure_row(nd.in[0], ni);
+        const int yb = nd.out[0];
+        set_row(m->bufs[yb], m->tensors[yb]);
+        std::vector<uint32_t> dims(X.dims, X.dims + 8);
+        std::vector<uint8_t> pv(perm, perm + 8);
+        const int ndim = X.ndim;
+        const int s = add_step(ni, nd.op, 7, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[xb];
+          const Buf* y = &m->bufs[yb];
+          r.run = [=](cudaStream_t st) { return launch_permute(x->ptr, y->ptr, ndim, dims.data(), pv.data(), st); };
+          return 0;
+        });
+        P.touch(xb, s);
+        P.touch(yb, s);
+        produced[yb] = 1;
+        break;
+      }
+      case OP_SOFTMAX: {
+        const TensorRec& X = m->tensors[nd.in[0]];
+        int axis = -1;
+        if (nd.params.size() >= 4) std::memcpy(&axis, nd.params.data(), 4);
+        if (axis < 0) axis += X.ndim;
+        if (axis < 0 || axis >= X.ndim) {
+          set_error("plan: Softmax node %d axis out of range", ni);
+          return SPINN_CUDA_EFORMAT;
+        }
+        long outer = 1, inner = 1;
+        for (int d = 0; d < axis; ++d) outer *= X.dims[d];
+        for (int d = axis + 1; d < X.ndim; ++d) inner *= X.dims[d];
+        const int dim = X.dims[axis];
+        const int xb = ensure_row(nd.in[0], ni);
+        const int yb = nd.out[0];
+        set_row(m->bufs[yb], m->tensors[yb]);
+        const int s = add_step(ni, nd.op, 6, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[xb];
+          const Buf* y = &m->bufs[yb];
+          r.run = [=](cudaStream_t st) { return launch_softmax(x->ptr, y->ptr, outer, dim, inner, st); };
+          return 0;
+        });
+        P.touch(xb, s);
+        P.touch(yb, s);
+        produced[yb] = 1;
+        break;
+      }
+      case OP_MATMUL: {
+        // MatMul (SPINN/run_time/ops/mm/matmul.c) with ONNX broadcasting of a 2-D B: per batch a
+        // tcgen05 GEMM in split-tf32 (A' = [A_hi|A_lo|A_hi], B' = [B_hi|B_hi|B_lo] along K), so
+        // activation x activation products (attention scores feeding a softmax) keep about
+        // fp32 accuracy; these GEMMs are small next to the convolutions.
+        const TensorRec& A = m->tensors[nd.in[0]];
+        const TensorRec& Bt = m->tensors[nd.in[1]];
+        const TensorRec& Y = m->tensors[nd.out[0]];
+        if (A.is_weight || A.ndim < 2 || Bt.ndim < 2) {
+          set_error("plan: MatMul node %d needs an activation A and 2-D+ operands", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int M = A.dims[A.ndim - 2], K = A.dims[A.ndim - 1];
+        const int K2 = Bt.dims[Bt.ndim - 2], N = Bt.dims[Bt.ndim - 1];
+        long batch = 1, batch_b = 1;
+        for (int d = 0; d < A.ndim - 2; ++d) batch *= A.dims[d];
+        for (int d = 0; d < Bt.ndim - 2; ++d) batch_b *= Bt.dims[d];
+        if (K != K2 || (batch_b != 1 && batch_b != batch)) {
+          set_error("plan: MatMul node %d shapes do not match", ni);
+          return SPINN_CUDA_EFORMAT;
+        }
+        const int seg = round4(K), Np = round4(N), kpad = tc_num_kb(3 * seg) * 32;
+        const int ab = ensure_row(nd.in[0], ni);
+        Buf t;
+        t.lay = LAY_ROW;
+        t.bytes = (uint64_t)batch * M * 3 * seg * 4;
+        const int at = P.new_buf(t);  // A' split-packed
+        uint64_t woff = ~0ull;
+        int bb = -1, btt = -1, bpt = -1;
+        if (Bt.is_weight) {
+          woff = P.wreserve((uint64_t)batch_b * Np * kpad);
+          for (long bi = 0; bi < batch_b; ++bi)
+            for (int n = 0; n < N; ++n)
+              for (int k = 0; k < K; ++k) {
+                const float v = Bt.host[((uint64_t)bi * K + k) * N + n];
+                const float hi = host_round_tf32(v), lo = host_round_tf32(v - hi);
+                float* row = &m->whost[woff + ((uint64_t)bi * Np + n) * kpad];
+                row[k] = hi;
+                row[seg + k] = hi;
+                row[2 * seg + k] = lo;
+              }
+        } else {
+          bb = ensure_row(nd.in[1], ni);
+          t.bytes = (uint64_t)batch_b * N * K * 4;
+          btt = P.new_buf(t);
+          t.bytes = (uint64_t)batch_b * Np * kpad * 4;
+          bpt = P.new_buf(t);
+        }
+        const int yb = nd.out[0];
+        set_row(m->bufs[yb], Y);
+        int yt = -1;
+        if (Np != N) {
+          t.bytes = (uint64_t)M * Np * 4;
+          yt = P.new_buf(t);
+        }
+        const int s = add_step(ni, nd.op, 2, 2.0 * batch * M * N * K, [=](StepRec& r) {
+          const Buf* a = &m->bufs[ab];
+          const Buf* ap = &m->bufs[at];
+          const Buf* b = bb >= 0 ? &m->bufs[bb] : nullptr;
+          const Buf* bt = btt >= 0 ? &m->bufs[btt] : nullptr;
+          const Buf* bp = bpt >= 0 ? &m->bufs[bpt] : nullptr;
+          const Buf* y = &m->bufs[yb];
+          const Buf* ytp = yt >= 0 ? &m->bufs[yt] : nullptr;
+          r.run = [=](cudaStream_t st) -> int {
+            if (seg != K) SPINN_CUDA_TRY(cudaMemsetAsync(ap->ptr, 0, ap->bytes, st));
+            int rc = launch_split_tf32(a->ptr, ap->ptr, batch * M, K, K, seg, 3 * seg, 0, 1, 0, st);
+            if (rc) return rc;
+            const float* wbase = woff != ~0ull ? m->wdev + woff : nullptr;
+            if (b) {
+              rc = launch_transpose(b->ptr, bt->ptr, (int)batch_b, K, N, st);  // -> [batch_b][N][K]
+              if (rc) return rc;
+              SPINN_CUDA_TRY(cudaMemsetAsync(bp->ptr, 0, bp->bytes, st));
+              for (long bi = 0; bi < batch_b; ++bi) {
+                rc = launch_split_tf32(bt->ptr + (size_t)bi * N * K, bp->ptr + (size_t)bi * Np * kpad, N, K, K, seg,
+                                       kpad, 0, 0, 1, st);
+                if (rc) return rc;
+              }
+              wbase = bp->ptr;
+            }
+            for (long i = 0; i < batch; ++i) {
+              TcGemmArgs g;
+              g.a_mode = 1;
+              g.x = ap->ptr + (size_t)i * M * 3 * seg;
+              g.M = M;
+              g.K = 3 * seg;
+              g.lda = 3 * seg;
+              g.wt = wbase + (size_t)(batch_b == 1 ? 0 : i) * Np * kpad;
+              g.kpad = kpad;
+              g.N = Np;
+              g.y = ytp ? ytp->ptr : y->ptr + (size_t)i * M * N;
+              g.ldy = Np;
+              rc = tc_gemm_launch(g, st);
+              if (rc) return rc;
+              if (ytp)
+                SPINN_CUDA_TRY(cudaMemcpy2DAsync(y->ptr + (size_t)i * M * N, (size_t)N * 4, ytp->ptr, (size_t)Np * 4,
+                                                 (size_t)N * 4, M, cudaMemcpyDeviceToDevice, st));
+            }
+            return 0;
+          };
+          return 0;
+        });
+        P.touch(ab, s);
+        P.touch(at, s);
+        if (bb >= 0) {
+          P.touch(bb, s);
+          P.touch(btt, s);
+          P.touch(bpt, s);
+        }
+        if (yt >= 0) P.touch(yt, s);
+        P.touch(yb, s);
+        produced[yb] = 1;
         break;
       }
       default:

@@ -138,7 +138,8 @@ def read(data: bytes) -> EnnfModel:
             continue
         _id, _r, off, size, _r2 = struct.unpack_from(WENTRY_FMT, data, entry_tab + 16 * tid)
         if size:
-            weights[tid] = np.frombuffer(data, np.float32, size // 4, wdata + off).reshape(t.dims)
+            dt = np.int64 if t.dtype == 7 else np.float32
+            weights[tid] = np.frombuffer(data, dt, size // np.dtype(dt).itemsize, wdata + off).reshape(t.dims)
     return EnnfModel(h, ins, outs, nodes, tensors, weights)
 
 
@@ -367,7 +368,21 @@ def _ints(v, n, fmt_len):
     return out
 
 
-def _params(node, op_code: int, fused_act: int) -> bytes:
+def _params(node, op_code: int, fused_act: int, pbuf: bytearray) -> bytes:
+    """ENNF parameter block of `node`.  `pbuf` is the converter's reused 1024-byte scratch
+    (params_buf, SPINN/onnx2ennf.c:307): most extractors clear their struct first, but Split
+    writes only `axis` and leaves `num_outputs` as whatever the previous node left there
+    (onnx2ennf_ops.c:275-280), which a byte-identical writer has to reproduce."""
+    a = node.attrs
+    if op_code == OP["Split"]:
+        struct.pack_into("<i", pbuf, 0, int(a.get("axis", 0)))
+        return bytes(pbuf[:8])
+    out = _params_fixed(node, op_code, fused_act)
+    pbuf[:len(out)] = out
+    return out
+
+
+def _params_fixed(node, op_code: int, fused_act: int) -> bytes:
     a = node.attrs
     if op_code == OP["Conv"]:
         return struct.pack(CONV_PARAMS_FMT, *_ints(a.get("kernel_shape", []), 4, 4),
@@ -390,6 +405,9 @@ def _params(node, op_code: int, fused_act: int) -> bytes:
         return struct.pack("<i", int(a.get("axis", 1)))
     if op_code == OP["Softmax"]:
         return struct.pack("<i", int(a.get("axis", -1)))
+    if op_code == OP["Transpose"]:
+        perm = list(a.get("perm", []))
+        return struct.pack("<8BB3x", *(perm + [0] * (8 - len(perm)))[:8], len(perm))
     return b""
 
 
@@ -440,12 +458,13 @@ def convert(graph, disable_add: bool = False, disable_silu: bool = False) -> byt
 
     node_blob = bytearray()
     n_eff = 0
+    pbuf = bytearray(1024)
     for i, n in enumerate(g.nodes):
         if fz.flags[i] & _SKIP:
             continue
         n_eff += 1
         code = OP[n.op_type]
-        p = _params(n, code, fz.act[i] if code == OP["Conv"] else 0)
+        p = _params(n, code, fz.act[i] if code == OP["Conv"] else 0, pbuf)
         flags = NODE_FLAG_FUSED if fz.flags[i] & _HAS_ACT else 0
         node_blob += struct.pack(NODEBASE_FMT, code, len(n.inputs), len(n.outputs), len(p), flags, 0)
         node_blob += b"".join(struct.pack("<H", ids[x]) for x in n.inputs)
@@ -456,7 +475,8 @@ def convert(graph, disable_add: bool = False, disable_silu: bool = False) -> byt
     for name in names:
         k = ids[name]
         if name in g.initializers:
-            dims, w, dt = g.initializers[name].shape, 1, 1
+            arr = g.initializers[name]
+            dims, w, dt = arr.shape, 1, (7 if arr.dtype == np.int64 else 1)
         else:
             dims, w = shapes.get(name, ()), 0
             dt = 1 if name in shapes else 0      # map_dtype(0) = UNDEFINED without value_info
@@ -475,7 +495,7 @@ def convert(graph, disable_add: bool = False, disable_silu: bool = False) -> byt
     for name in names:
         k = ids[name]
         if name in g.initializers:
-            raw = g.initializers[name].astype(np.float32).tobytes()
+            raw = np.ascontiguousarray(g.initializers[name]).tobytes()
             entries += struct.pack(WENTRY_FMT, k, 0, len(wblob), len(raw), 0)
             wblob += raw
         else:

@@ -61,7 +61,9 @@ class Graph:
         return name
 
     def add_init(self, name: str, arr: np.ndarray) -> str:
-        self.initializers[name] = np.ascontiguousarray(arr, dtype=np.float32)
+        arr = np.asarray(arr)
+        dt = np.int64 if arr.dtype.kind in "iu" else np.float32
+        self.initializers[name] = np.ascontiguousarray(arr, dtype=dt)
         return name
 
     def add_node(self, op: str, inputs: Sequence[str], outputs: Sequence[str],
@@ -118,10 +120,11 @@ def conv_out_hw(h: int, w: int, k: int, s: int, p: int) -> Tuple[int, int]:
 class _Builder:
     """Small helper that names tensors and draws weights in node order."""
 
-    def __init__(self, g: Graph, rng: np.random.Generator):
+    def __init__(self, g: Graph, rng: np.random.Generator, bn_spread: Optional[float] = None):
         self.g = g
         self.rng = rng
         self.k = 0
+        self.bn_spread = bn_spread
 
     def _id(self, prefix: str) -> str:
         self.k += 1
@@ -143,10 +146,21 @@ class _Builder:
 
     def bn(self, x: str, eps: float = 1e-5) -> str:
         c = self.g.shape(x)[1]
-        gamma = self.g.add_init(self._id("bn_gamma"), self.rng.uniform(0.5, 1.5, (c,)))
-        beta = self.g.add_init(self._id("bn_beta"), self.rng.normal(0.0, 0.1, (c,)))
-        mean = self.g.add_init(self._id("bn_mean"), self.rng.normal(0.0, 0.1, (c,)))
-        var = self.g.add_init(self._id("bn_var"), self.rng.uniform(0.5, 1.5, (c,)))
+        if self.bn_spread is None:   # the benchmark configurations' distribution
+            gamma = self.rng.uniform(0.5, 1.5, (c,))
+            beta = self.rng.normal(0.0, 0.1, (c,))
+            mean = self.rng.normal(0.0, 0.1, (c,))
+            var = self.rng.uniform(0.5, 1.5, (c,))
+        else:                        # statistics close to an identity normalisation
+            e = self.bn_spread
+            gamma = self.rng.uniform(1 - e, 1 + e, (c,))
+            beta = self.rng.normal(0.0, e, (c,))
+            mean = self.rng.normal(0.0, e, (c,))
+            var = self.rng.uniform(1 - e, 1 + e, (c,))
+        gamma = self.g.add_init(self._id("bn_gamma"), gamma)
+        beta = self.g.add_init(self._id("bn_beta"), beta)
+        mean = self.g.add_init(self._id("bn_mean"), mean)
+        var = self.g.add_init(self._id("bn_var"), var)
         return self.g.add_node("BatchNormalization", [x, gamma, beta, mean, var], [self._id("bn")],
                                [self.g.shape(x)], epsilon=float(eps), momentum=0.9)[0]
 
@@ -177,6 +191,51 @@ class _Builder:
         s = self.g.shape(x)
         return self.g.add_node("Flatten", [x], [self._id("flatten")],
                                [(s[0], int(np.prod(s[1:])))], axis=1)[0]
+
+    def conv_bn(self, x: str, oc: int, k: int, s: int, act: str = "SiLU", group: int = 1) -> str:
+        """Conv (no bias) + BatchNorm + activation ("SiLU", "Relu" or None)."""
+        y = self.bn(self.conv(x, oc, k, s, k // 2, group=group))
+        if act == "SiLU":
+            y = self.silu(y)
+        elif act == "Relu":
+            y = self.unary("Relu", y)
+        return y
+
+    def split2(self, x: str):
+        n, c, h, w = self.g.shape(x)
+        return self.g.add_node("Split", [x], [self._id("split"), self._id("split")],
+                               [(n, c // 2, h, w)] * 2, axis=1)
+
+    def concat(self, xs, axis: int = 1) -> str:
+        shp = list(self.g.shape(xs[0]))
+        shp[axis] = sum(self.g.shape(x)[axis] for x in xs)
+        return self.g.add_node("Concat", list(xs), [self._id("concat")], [tuple(shp)], axis=axis)[0]
+
+    def upsample2(self, x: str) -> str:
+        n, c, h, w = self.g.shape(x)
+        sc = self.g.add_init(self._id("scales"), np.array([1, 1, 2, 2], np.float32))
+        return self.g.add_node("Resize", [x, sc], [self._id("resize")], [(n, c, 2 * h, 2 * w)],
+                               mode="nearest")[0]
+
+    def reshape(self, x: str, shape) -> str:
+        shp = self.g.add_init(self._id("shape"), np.array(shape, np.int64))
+        return self.g.add_node("Reshape", [x, shp], [self._id("reshape")], [tuple(shape)])[0]
+
+    def transpose(self, x: str, perm) -> str:
+        s = self.g.shape(x)
+        return self.g.add_node("Transpose", [x], [self._id("transpose")], [tuple(s[p] for p in perm)],
+                               perm=list(perm))[0]
+
+    def matmul(self, a: str, b: str) -> str:
+        sa, sb = self.g.shape(a), self.g.shape(b)
+        return self.g.add_node("MatMul", [a, b], [self._id("matmul")], [tuple(sa[:-1]) + (sb[-1],)])[0]
+
+    def softmax(self, x: str) -> str:
+        return self.g.add_node("Softmax", [x], [self._id("softmax")], [self.g.shape(x)], axis=-1)[0]
+
+    def scale(self, x: str, v: float) -> str:
+        c = self.g.add_init(self._id("scale"), np.array([v], np.float32))
+        return self.g.add_node("Mul", [x, c], [self._id("mul")], [self.g.shape(x)])[0]
 
     def gemm(self, x: str, n_out: int, trans_b: int = 1) -> str:
         m, k = self.g.shape(x)
@@ -297,3 +356,137 @@ def gemm_case(m: int, n: int, k: int, trans_a: int = 0, trans_b: int = 0, alpha:
                transA=int(trans_a), transB=int(trans_b))
     g.mark_output("Y")
     return g, a_val
+
+
+# ------------------------------------------------------------------ YOLOv10n-shaped detector
+def _c2f(b: _Builder, x: str, c_out: int, n: int, shortcut: bool) -> str:
+    """CSP block: 1x1 conv to 2h channels, split in halves, n bottlenecks (two 3x3 convs,
+    optional identity shortcut) on the second half, concat of every stage, 1x1 conv."""
+    h = c_out // 2
+    a, y = b.split2(b.conv_bn(x, 2 * h, 1, 1))
+    outs = [a, y]
+    for _ in range(n):
+        t = b.conv_bn(b.conv_bn(y, h, 3, 1), h, 3, 1)
+        y = b.add(y, t) if shortcut else t
+        outs.append(y)
+    return b.conv_bn(b.concat(outs), c_out, 1, 1)
+
+
+def _down(b: _Builder, x: str, c_out: int) -> str:
+    """Pointwise conv then depthwise 3x3 stride 2 (BN, no activation)."""
+    y = b.conv_bn(x, c_out, 1, 1)
+    return b.conv_bn(y, c_out, 3, 2, act=None, group=c_out)
+
+
+def _sppf(b: _Builder, x: str) -> str:
+    c = b.g.shape(x)[1]
+    y = b.conv_bn(x, c // 2, 1, 1)
+    m1 = b.maxpool(y, 5, 1, 2)
+    m2 = b.maxpool(m1, 5, 1, 2)
+    m3 = b.maxpool(m2, 5, 1, 2)
+    return b.conv_bn(b.concat([y, m1, m2, m3]), c, 1, 1)
+
+
+def _psa(b: _Builder, x: str, heads: int = 2) -> str:
+    """Split-attention block: half of the channels pass through self-attention over the
+    spatial positions (q, k, v from one 1x1 conv; softmax(q^T k / sqrt(d)) applied to v;
+    1x1 projection, residual) and a two-layer 1x1 feed-forward (residual)."""
+    n, c, hh, ww = b.g.shape(x)
+    a, y = b.split2(b.conv_bn(x, c, 1, 1))
+    d = c // 2
+    hd = d // heads
+    qkv = b.conv_bn(y, 3 * d, 1, 1, act=None)
+    q, k, v = (b.reshape(t, (n, heads, hd, hh * ww)) for t in _split3(b, qkv))
+    attn = b.softmax(b.scale(b.matmul(b.transpose(q, (0, 1, 3, 2)), k), float(hd) ** -0.5))
+    o = b.matmul(v, b.transpose(attn, (0, 1, 3, 2)))
+    o = b.reshape(o, (n, d, hh, ww))
+    y = b.add(b.conv_bn(o, d, 1, 1, act=None), y)
+    y = b.add(b.conv_bn(b.conv_bn(y, 2 * d, 1, 1), d, 1, 1, act=None), y)
+    return b.conv_bn(b.concat([a, y]), c, 1, 1)
+
+
+def _split3(b: _Builder, x: str):
+    n, c, h, w = b.g.shape(x)
+    return b.g.add_node("Split", [x], [b._id("split") for _ in range(3)], [(n, c // 3, h, w)] * 3, axis=1)
+
+
+def _head(b: _Builder, x: str, reg: int = 64, nc: int = 80) -> str:
+    """Decoupled head: box branch (two 3x3 convs, 1x1 to reg) and class branch (depthwise
+    3x3 + pointwise twice, 1x1 to nc), concatenated and flattened to [N, reg+nc, H*W]."""
+    n, c, h, w = b.g.shape(x)
+    cb = max(16, c // 4, reg // 4)
+    bx = b.conv(b.conv_bn(b.conv_bn(x, cb, 3, 1), cb, 3, 1), reg, 1, 1, 0, bias=True)
+    cc = max(c, min(nc, 100))
+    cl = b.conv_bn(b.conv_bn(x, c, 3, 1, group=c), cc, 1, 1)
+    cl = b.conv_bn(b.conv_bn(cl, cc, 3, 1, group=cc), cc, 1, 1)
+    cl = b.conv(cl, nc, 1, 1, 0, bias=True)
+    return b.reshape(b.concat([bx, cl]), (n, reg + nc, h * w))
+
+
+YOLO_STAGES = ("stem", "p3", "p4", "c5", "sppf", "psa", "top", "s3", "s4", "s5", "heads")
+
+
+def yolo_shaped(batch: int = 1, image: int = 640, seed: int = 4, widths=(16, 32, 64, 128, 256),
+                depths=(1, 2, 2, 1), nc: int = 80, upto: Optional[str] = None,
+                bn_spread: Optional[float] = 0.1) -> Graph:
+    """A YOLOv10n-shaped detector: CSP/C2f backbone with pointwise + depthwise-3x3 stride-2
+    downsampling and SiLU activations, SPPF pooling, a split-attention (PSA) block, a
+    top-down/bottom-up feature pyramid with nearest upsampling and concatenation, and
+    decoupled heads at strides 8, 16 and 32, concatenated to [N, 64 + nc, anchors].
+    This is a synthetic network of that family (the original configuration is not part of
+    the reference); widths/depths follow the family's smallest ("n") scale.  ``upto`` ends
+    the graph after one of ``YOLO_STAGES`` (layer-wise parity checks)."""
+    if upto is not None and upto not in YOLO_STAGES:
+        raise ValueError(upto)
+    rng = np.random.default_rng(seed)
+    g = Graph(f"yolo_shaped_{image}")
+    b = _Builder(g, rng, bn_spread)
+    w0, w1, w2, w3, w4 = widths
+    x = g.add_input("images", (batch, 3, image, image))
+
+    def done(t: str) -> Graph:
+        g.mark_output(t)
+        return g
+
+    y = b.conv_bn(x, w0, 3, 2)                        # /2
+    y = b.conv_bn(y, w1, 3, 2)                        # /4
+    y = _c2f(b, y, w1, depths[0], True)
+    if upto == "stem":
+        return done(y)
+    y = b.conv_bn(y, w2, 3, 2)                        # /8
+    p3 = _c2f(b, y, w2, depths[1], True)
+    if upto == "p3":
+        return done(p3)
+    y = _down(b, p3, w3)                              # /16
+    p4 = _c2f(b, y, w3, depths[2], True)
+    if upto == "p4":
+        return done(p4)
+    y = _down(b, p4, w4)                              # /32
+    y = _c2f(b, y, w4, depths[3], True)
+    if upto == "c5":
+        return done(y)
+    y = _sppf(b, y)
+    if upto == "sppf":
+        return done(y)
+    p5 = _psa(b, y)
+    if upto == "psa":
+        return done(p5)
+    t = _c2f(b, b.concat([b.upsample2(p5), p4]), w3, 1, False)       # top-down /16
+    if upto == "top":
+        return done(t)
+    s3 = _c2f(b, b.concat([b.upsample2(t), p3]), w2, 1, False)       # /8 out
+    if upto == "s3":
+        return done(s3)
+    s4 = _c2f(b, b.concat([b.conv_bn(s3, w2, 3, 2), t]), w3, 1, False)   # /16 out
+    if upto == "s4":
+        return done(s4)
+    s5 = _c2f(b, b.concat([_down(b, s4, w3), p5]), w4, 1, True)          # /32 out
+    if upto == "s5":
+        return done(s5)
+    heads = [_head(b, s, nc=nc) for s in (s3, s4, s5)]
+    return done(b.concat(heads, axis=2))
+
+
+def yolo_input(batch: int, image: int = 640, seed: int = 4) -> np.ndarray:
+    """U(0,1) NCHW images from ``default_rng(seed + 1)``."""
+    return np.random.default_rng(seed + 1).uniform(0.0, 1.0, (batch, 3, image, image)).astype(np.float32)

@@ -23,6 +23,9 @@ def _graphs():
         "gemm_vec": netdef.gemm_case(8, 12, 16, trans_b=1)[0],
         "gemm_full": netdef.gemm_case(8, 12, 16, trans_a=1, c_shape="full")[0],
         "resnet50_64px": netdef.resnet(50, batch=1, image=64, num_classes=10, width=16),
+        # Split (stale num_outputs bytes), Concat, Resize, Reshape (int64 shape), Transpose,
+        # MatMul, Softmax, scalar Mul, depthwise convolutions
+        "yolo_shaped_128px": netdef.yolo_shaped(batch=1, image=128),
     }
 
 

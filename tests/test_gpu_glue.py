@@ -1,0 +1,75 @@
+"""Device glue operators of the YOLO-shaped graphs (Split, Concat, Resize, Reshape, Transpose,
+MatMul, Softmax, scalar Mul, Sigmoid, unfused Add) on small graphs, against the reference
+runtime (oracle/_ref) on identical inputs."""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_both(ref_oracle, tmp_path, g, x):
+    from spinn_b200 import ennf, runtime
+    img = ennf.convert(g)
+    p = tmp_path / "m.ennf"
+    p.write_bytes(img)
+    ref = list(ref_oracle.run_model(str(p), x).values())[0]
+    y = runtime.Model(img).run(x).ravel()
+    return y, ref
+
+
+def _builder(shape, seed=0):
+    from spinn_b200 import netdef
+    g = netdef.Graph("glue")
+    b = netdef._Builder(g, np.random.default_rng(seed))
+    x = g.add_input("x", shape)
+    xv = np.random.default_rng(seed + 1).uniform(-1, 1, shape).astype(np.float32)
+    return g, b, x, xv
+
+
+def test_split_concat_nhwc(cuda_lib, ref_oracle, tmp_path):
+    g, b, x, xv = _builder((2, 8, 10, 10))
+    y = b.conv_bn(x, 24, 3, 1)
+    a, c = b.split2(y)
+    y = b.concat([b.conv_bn(a, 12, 3, 1), c, b.conv_bn(c, 6, 1, 1)])   # 30 channels: pad lane zeroed
+    y = b.conv_bn(y, 16, 3, 1)
+    g.mark_output(y)
+    out, ref = _run_both(ref_oracle, tmp_path, g, xv)
+    assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
+
+
+def test_resize_and_unfused_add(cuda_lib, ref_oracle, tmp_path):
+    g, b, x, xv = _builder((1, 16, 7, 9))
+    y = b.conv_bn(x, 16, 3, 1)
+    y = b.upsample2(y)
+    z = b.conv_bn(y, 16, 3, 1)
+    y = b.add(z, y)                      # conv output has two consumers: Add stays a node
+    y = b.conv_bn(y, 8, 1, 1, act="Relu")
+    g.mark_output(y)
+    out, ref = _run_both(ref_oracle, tmp_path, g, xv)
+    assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
+
+
+def test_attention_reshape_transpose_matmul_softmax(cuda_lib, ref_oracle, tmp_path):
+    g, b, x, xv = _builder((2, 16, 6, 5))
+    n, c, h, w = 2, 16, 6, 5
+    qkv = b.conv_bn(x, 48, 1, 1, act=None)
+    from spinn_b200.netdef import _split3
+    q, k, v = (b.reshape(t, (n, 2, 8, h * w)) for t in _split3(b, qkv))
+    att = b.softmax(b.scale(b.matmul(b.transpose(q, (0, 1, 3, 2)), k), 8 ** -0.5))
+    o = b.reshape(b.matmul(v, b.transpose(att, (0, 1, 3, 2))), (n, 16, h, w))
+    y = b.conv_bn(o, 16, 1, 1)
+    g.mark_output(y)
+    out, ref = _run_both(ref_oracle, tmp_path, g, xv)
+    assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
+
+
+def test_row_concat_and_sigmoid(cuda_lib, ref_oracle, tmp_path):
+    g, b, x, xv = _builder((2, 8, 4, 4))
+    y1 = b.reshape(b.conv_bn(x, 12, 3, 1), (2, 12, 16))
+    y2 = b.reshape(b.conv_bn(x, 12, 1, 1), (2, 12, 16))
+    y = b.unary("Sigmoid", b.concat([y1, y2], axis=2))
+    g.mark_output(y)
+    out, ref = _run_both(ref_oracle, tmp_path, g, xv)
+    assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)

@@ -106,3 +106,26 @@ def test_matmul(cuda_lib, port_oracle, shape):
     runtime.matmul(a, b, y)
     ref = port_oracle.matmul(a, b)
     assert rel_l2(y, ref) <= TOL
+
+
+def test_weight_cache_follows_content_at_a_reused_address(cuda_lib, port_oracle):
+    """Cached device weights are keyed by host pointer; rewriting the same buffer with new
+    weights (as when a freed model's memory is reused) must not serve the stale copy."""
+    from spinn_b200 import runtime
+    rng = np.random.default_rng(21)
+    a = rng.uniform(-1, 1, (64, 96)).astype(np.float32)
+    b = rng.uniform(-1, 1, (80, 96)).astype(np.float32)
+    y = np.zeros((64, 80), np.float32)
+    runtime.gemm(a, b, y, None, runtime.gemm_params(1.0, 1.0, 0, 1))
+    assert rel_l2(y, port_oracle.gemm(a, b, None, 64, 80, 96, 0, 1)) <= TOL
+    b[...] = rng.uniform(-1, 1, b.shape)          # same address, new contents
+    runtime.gemm(a, b, y, None, runtime.gemm_params(1.0, 1.0, 0, 1))
+    assert rel_l2(y, port_oracle.gemm(a, b, None, 64, 80, 96, 0, 1)) <= TOL
+    x = rng.uniform(-1, 1, (1, 16, 8, 8)).astype(np.float32)
+    w = rng.normal(0, 0.3, (16, 16, 3, 3)).astype(np.float32)
+    yc = np.zeros((1, 16, 8, 8), np.float32)
+    params = runtime.conv_params((3, 3), (1, 1), (1, 1, 1, 1), (1, 1), 1, 0, 0)
+    runtime.conv2d(x, w, yc, None, None, params)
+    w[...] = rng.normal(0, 0.3, w.shape)
+    runtime.conv2d(x, w, yc, None, None, params)
+    assert rel_l2(yc, port_oracle.conv2d(x, w, None, None, (1, 1), (1, 1))) <= TOL
