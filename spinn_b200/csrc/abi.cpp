@@ -37,6 +37,8 @@ struct Session {
   uint8_t* scratch = nullptr;
   size_t scratch_cap = 0;
   size_t scratch_used = 0;
+  float* ws = nullptr;  // split-K workspace of the tcgen05 launches
+  size_t ws_cap = 0;
   std::map<std::tuple<const void*, uint64_t, int, int>, DevWeight> wcache;
 };
 
@@ -68,6 +70,23 @@ float* scratch_take(size_t bytes) {
   return reinterpret_cast<float*>(S.scratch + off);
 }
 size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// Launches a tcgen05 GEMM with the split-K workspace its shape wants (grown on demand).
+int tc_launch_ws(TcGemmArgs a, cudaStream_t st) {
+  Session& S = g_sess;
+  const size_t need = tc_gemm_workspace_bytes(a);
+  if (need > S.ws_cap) {
+    SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));
+    if (S.ws) cudaFree(S.ws);
+    S.ws = nullptr;
+    S.ws_cap = 0;
+    SPINN_CUDA_TRY(cudaMalloc(&S.ws, need));
+    S.ws_cap = need;
+  }
+  a.ws = S.ws;
+  a.ws_bytes = need;
+  return tc_gemm_launch(a, st);
+}
 
 bool is_device_ptr(const void* p) {
   cudaPointerAttributes a;
@@ -302,6 +321,9 @@ __attribute__((visibility("default"))) void spinn_cuda_shutdown(void) {
   if (S.scratch) cudaFree(S.scratch);
   S.scratch = nullptr;
   S.scratch_cap = 0;
+  if (S.ws) cudaFree(S.ws);
+  S.ws = nullptr;
+  S.ws_cap = 0;
   cudaStreamDestroy(S.stream);
   S.stream = nullptr;
   S.ready = false;
@@ -395,7 +417,7 @@ __attribute__((visibility("default"))) int spinn_cuda_conv2d(SpinnTensor** in, i
     a.y = yn;
     a.ldy = ocpad;
     a.act = g.act;
-    rc = tc_gemm_launch(a, st);
+    rc = tc_launch_ws(a, st);
   } else if (g.G == g.C && g.G == g.OC) {
     rc = conv_weights(in[1], B, W_DW, g.C, cpad, g.OC, g.KH, g.KW, g.G, &dw);
     if (rc) return rc;
@@ -444,7 +466,7 @@ static int gemm_core(const float* A, int lda, const float* Bt, int kpad, int M, 
   g.y = yt;
   g.ldy = Np;
   g.alpha = alpha;
-  int rc = tc_gemm_launch(g, st);
+  int rc = tc_launch_ws(g, st);
   if (rc) return rc;
   if (yt != Y)
     SPINN_CUDA_TRY(cudaMemcpy2DAsync(Y, (size_t)N * 4, yt, (size_t)Np * 4, (size_t)N * 4, M, cudaMemcpyDeviceToDevice, st));

@@ -40,6 +40,9 @@ const char* get_error();
 int encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                     uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                     CUtensorMapSwizzle swizzle);
+// 3-D tiled map of `planes` row-major [outer][inner] matrices stored back to back.
+int encode_tiled_3d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t planes,
+                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
 int encode_im2col_4d(CUtensorMap* map, const void* base, int n, int h, int w, int c,
                      int lower_w, int lower_h, int upper_w, int upper_h, int channels_per_pixel,
                      int pixels_per_column, int stride_w, int stride_h, CUtensorMapSwizzle swizzle);
@@ -78,7 +81,14 @@ struct TcGemmArgs {
   int round_out = 0;
   int bn = 0;  // 0 = choose
   int* err = nullptr;  // device error word; nullptr = the per-device flag
+  // Split-K workspace (optional).  With one, problems that leave SMs idle are split along K
+  // into raw fp32 partials (ksplit x M x N floats) reduced in a fixed order by a finish kernel
+  // that applies the epilogue; results stay deterministic.
+  float* ws = nullptr;
+  size_t ws_bytes = 0;
 };
+// Workspace a launch of `a` would use (0 when it would not split), for planners.
+size_t tc_gemm_workspace_bytes(const TcGemmArgs& a);
 // Checks whether the tcgen05 path accepts the problem (alignment, corner ranges ...).
 bool tc_gemm_supported(const TcGemmArgs& a, std::string* why);
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);

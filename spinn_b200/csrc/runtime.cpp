@@ -138,6 +138,8 @@ struct SpinnCudaModel {
   uint64_t arena_bytes = 0;
   float* wdev = nullptr;
   uint64_t wbytes = 0;
+  float* splitk_ws = nullptr;      // split-K partial sums, shared by all steps (one stream)
+  size_t splitk_bytes = 0;
   std::vector<float> whost;        // pre-transformed weights before upload
   std::vector<StepRec> steps;
   cudaGraph_t graph = nullptr;
@@ -153,6 +155,9 @@ namespace spinn {
 namespace {
 
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+// Records the split-K workspace a tcgen05 launch of this shape will want.
+void note_ws(SpinnCudaModel* m, const TcGemmArgs& a) { m->splitk_bytes = std::max(m->splitk_bytes, tc_gemm_workspace_bytes(a)); }
 int round4(int c) { return (c + 3) & ~3; }
 
 // ------------------------------------------------------------------ load
@@ -665,7 +670,10 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             const Buf* xbp = &m->bufs[xb];
             const Buf* ybp = &m->bufs[yb];
             const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
+            note_ws(m, a);
             r.run = [m, a, xbp, ybp, rbp, woff, boff](cudaStream_t st) mutable {
+              a.ws = m->splitk_ws;
+              a.ws_bytes = m->splitk_bytes;
               a.x = xbp->ptr;
               a.y = ybp->ptr;
               a.res = rbp ? rbp->ptr : nullptr;
@@ -869,6 +877,15 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           const Buf* atp = at >= 0 ? &m->bufs[at] : nullptr;
           const Buf* y = &m->bufs[yb];
           const Buf* ytp = yt >= 0 ? &m->bufs[yt] : nullptr;
+          TcGemmArgs q;
+          q.a_mode = 1;
+          q.M = M;
+          q.K = K;
+          q.lda = Kp;
+          q.kpad = kpad;
+          q.N = Np;
+          q.ldy = Np;
+          note_ws(m, q);
           r.run = [=](cudaStream_t st) {
             const float* A_ = a->ptr;
             if (atp) {
@@ -896,6 +913,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             g.y = ytp ? ytp->ptr : y->ptr;
             g.ldy = Np;
             g.alpha = alpha;
+            g.ws = m->splitk_ws;
+            g.ws_bytes = m->splitk_bytes;
             int rc = tc_gemm_launch(g, st);
             if (rc) return rc;
             if (ytp)
@@ -1270,6 +1289,15 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           const Buf* bp = bpt >= 0 ? &m->bufs[bpt] : nullptr;
           const Buf* y = &m->bufs[yb];
           const Buf* ytp = yt >= 0 ? &m->bufs[yt] : nullptr;
+          TcGemmArgs q;
+          q.a_mode = 1;
+          q.M = M;
+          q.K = 3 * seg;
+          q.lda = 3 * seg;
+          q.kpad = kpad;
+          q.N = Np;
+          q.ldy = Np;
+          note_ws(m, q);
           r.run = [=](cudaStream_t st) -> int {
             if (seg != K) SPINN_CUDA_TRY(cudaMemsetAsync(ap->ptr, 0, ap->bytes, st));
             int rc = launch_split_tf32(a->ptr, ap->ptr, batch * M, K, K, seg, 3 * seg, 0, 1, 0, st);
@@ -1298,6 +1326,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
               g.N = Np;
               g.y = ytp ? ytp->ptr : y->ptr + (size_t)i * M * N;
               g.ldy = Np;
+              g.ws = m->splitk_ws;
+              g.ws_bytes = m->splitk_bytes;
               rc = tc_gemm_launch(g, st);
               if (rc) return rc;
               if (ytp)
@@ -1390,6 +1420,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     if (rc) return rc;
     if (m->steps[i].kind != 0) ++m->kernels;
   }
+  if (m->splitk_bytes) SPINN_CUDA_TRY(cudaMalloc(&m->splitk_ws, m->splitk_bytes));
   return 0;
 }
 
@@ -1417,6 +1448,7 @@ static void release_model(SpinnCudaModel* m) {
     if (b.external && b.ptr && b.alias < 0) cudaFree(b.ptr);
   if (m->arena) cudaFree(m->arena);
   if (m->wdev) cudaFree(m->wdev);
+  if (m->splitk_ws) cudaFree(m->splitk_ws);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }

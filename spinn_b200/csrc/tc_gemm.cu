@@ -19,10 +19,18 @@
 // together share the activation tile in L2.  Two TMEM accumulators let the epilogue of one
 // tile overlap the main loop of the next.
 //
+// Problems with fewer tiles than SMs (small batches, the last stages of a ResNet, the FC
+// layer) are split along K when the caller supplies a workspace: each (tile, K slice) unit
+// stores raw fp32 partials into its own plane of the workspace and splitk_finish_kernel sums
+// the planes in a fixed order and applies the epilogue, so results are deterministic.
+//
 // Every wait on an mbarrier is bounded (ptx.cuh mbar_wait); on expiry the CTA drains what it
 // issued, frees TMEM and returns with the device error flag set.
 #include <algorithm>
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -32,7 +40,6 @@ namespace spinn {
 namespace {
 
 constexpr int kBM = 128;       // tile rows (output pixels) = TMEM lanes
-constexpr int kBK = 32;        // K elements per pipeline stage (128 bytes of fp32/tf32)
 constexpr int kThreads = 256;
 constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s per wait; a stage takes microseconds
 constexpr uint64_t kDrainNs = 200000000ull;
@@ -46,19 +53,28 @@ struct TcParams {
   int cpad, taps, kw, dil_h, dil_w;
   int ohw, ow, stride_h, stride_w, pad_h, pad_w;
   int tiles_n, num_tiles;
+  int ksplit, kb_per, num_units;  // work unit u: tile u % num_tiles, K slice u / num_tiles
+  int nstages;                    // ring stages in use (<= the variant's STAGES)
   int has_res, act, round_out;
   float alpha;
   const float* bias;
   int* err;
 };
 
-template <int BN, int CB, bool RES>
+// BK: K depth of one pipeline stage, 32 or 64.  Deeper stages halve the barrier handoffs per
+// K (each handoff costs a few hundred cycles of single-thread latency); CTA pairs use 64 (one
+// handoff feeds 1024 MMA cycles per SM), 256-wide single-CTA tiles keep 32 so that four
+// stages fit beside the W tile.
+template <int BN, int CB, bool RES, int PAIR, int BK_>
 struct Cfg {
-  static constexpr int NSUB = kBK / CB;
+  static constexpr int BK = BK_;
+  static constexpr int BNC = BN / PAIR;  // B rows (output channels) held by each CTA
+  static constexpr int NSUB = BK / CB;   // TMA boxes per operand per stage
+  static constexpr int KSTEPS = BK / 8;  // MMAs per stage
   static constexpr uint32_t A_SUB = kBM * CB * 4;
-  static constexpr uint32_t B_SUB = BN * CB * 4;
-  static constexpr uint32_t A_STAGE = kBM * kBK * 4;
-  static constexpr uint32_t B_STAGE = BN * kBK * 4;
+  static constexpr uint32_t B_SUB = BNC * CB * 4;
+  static constexpr uint32_t A_STAGE = kBM * BK * 4;
+  static constexpr uint32_t B_STAGE = BNC * BK * 4;
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
   // epilogue: two 32x32 fp32 staging blocks per epilogue warp (double-buffered TMA stores)
   static constexpr uint32_t OUT_BYTES = 2 * 4 * 4096;
@@ -71,33 +87,57 @@ struct Cfg {
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // BN in {64,128,256} -> 128/256/512, powers of two
   static constexpr uint32_t SMEM = STAGES * STAGE + EPI + 256 + 1024;
   static_assert(STAGES >= 2, "pipeline needs two stages");
+  static_assert(PAIR == 1 || BNC >= 64, "pair tiles split BN into halves of at least 64 rows");
 };
 
-// Descriptor of the j-th 8-wide K slice of a stage whose rows are `rows` long in the MMA's
-// M or N dimension.
+// Start-address offset (bytes) of the j-th 8-wide K slice of a stage, and the descriptor
+// template (offset 0) for operand tiles with `sub_bytes` per channel block.
 template <int CB>
-__device__ __forceinline__ uint64_t stage_desc(uint32_t stage_addr, int j, uint32_t sub_bytes) {
+__device__ __forceinline__ uint32_t kslice_offset(int j, uint32_t sub_bytes) {
   if constexpr (CB == 4) {
-    // no swizzle: core matrices of 8 rows x 16 B; the two 16-B K halves of one MMA live in
-    // consecutive sub-tiles (LBO = sub-tile size), 8-row groups are 128 B apart (SBO).
-    return make_smem_desc(stage_addr + (2 * j) * sub_bytes, sub_bytes, 128, kSwNone);
+    return (2 * j) * sub_bytes;  // no swizzle: the two 16-B K halves of one MMA are consecutive sub-tiles
   } else {
-    constexpr uint32_t row_bytes = CB * 4;
-    const uint32_t sub = (8 * j) / CB;
-    const uint32_t off = ((8 * j) % CB) * 4;
+    return ((8 * j) / CB) * sub_bytes + ((8 * j) % CB) * 4;
+  }
+}
+template <int CB>
+__device__ __forceinline__ uint64_t stage_desc0(uint32_t addr, uint32_t sub_bytes) {
+  if constexpr (CB == 4) {
+    // core matrices of 8 rows x 16 B; K halves sub_bytes apart (LBO), 8-row groups 128 B (SBO)
+    return make_smem_desc(addr, sub_bytes, 128, kSwNone);
+  } else {
     constexpr uint32_t layout = CB == 32 ? kSw128 : CB == 16 ? kSw64 : kSw32;
-    return make_smem_desc(stage_addr + sub * sub_bytes + off, 16, 8 * row_bytes, layout);
+    return make_smem_desc(addr, 16, 8 * CB * 4, layout);
   }
 }
 
-template <int BN, int CB, int MODE, bool RES>
+// All lanes wait; the warp proceeds only if every lane saw the phase complete.  Warp-wide
+// loops take every exit decision through these so that the lanes never diverge on a flag
+// that another warp raises.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t ns) {
+  const bool ok = mbar_wait(bar, parity, abort, ns);
+  return __all_sync(0xffffffffu, ok);
+}
+__device__ __forceinline__ bool warp_aborted(volatile int* abort) { return __any_sync(0xffffffffu, *abort != 0); }
+
+// PAIR = 1: one CTA per 128 x BN tile.  PAIR = 2: a cluster of two CTAs per 256 x BN tile
+// with one cta_group::2 MMA stream issued by the leader (rank 0); each CTA loads its own 128
+// rows of A and BN/2 rows of W.  Barrier roles in pair mode: `full` of the leader counts the
+// bytes of both CTAs; the leader's MMA thread signals `empty` and `tfull` in both CTAs; both
+// CTAs' epilogue warps arrive on the leader's `tempty` (8 arrivals).
+//
+// The producer and MMA warps run their loops with all 32 lanes (lane 0 issues): a single
+// diverged lane spends about half again as long per barrier handoff.
+template <int BN, int CB, int MODE, bool RES, int PAIR, int BK_>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapY, const __grid_constant__ CUtensorMap mapR,
                    const TcParams p) {
-  using C = Cfg<BN, CB, RES>;
+  using C = Cfg<BN, CB, RES, PAIR, BK_>;
   constexpr int STAGES = C::STAGES;
+  constexpr int BK = C::BK;
   constexpr int NRS = C::RES_SLOTS > 0 ? C::RES_SLOTS : 1;
+  constexpr int TM = kBM * PAIR;  // rows of one work unit
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -115,6 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR == 2 ? cluster_ctarank() : 0;
+  const int unit0 = blockIdx.x / PAIR, unit_step = gridDim.x / PAIR;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -123,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], 4 * PAIR);
     }
     for (int r = 0; r < NRS; ++r) {
       mbar_init(&rfull[r], 1);
@@ -140,109 +182,178 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (RES) prefetch_tmap(&mapR);
   }
   if (warp == 2) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR == 2) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR == 2) cluster_sync();  // the peer's barriers are initialised before use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (A, W)
-    if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0;
-      uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
-      for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
-        const int m0 = tm * kBM, n0 = tn * BN;
-        int w0 = 0, h0 = 0, img = 0;
-        if constexpr (MODE == kIm2col) {
-          img = m0 / p.ohw;
-          const int rem = m0 - img * p.ohw;
-          const int oh = rem / p.ow, ow = rem - oh * p.ow;
-          w0 = ow * p.stride_w - p.pad_w;
-          h0 = oh * p.stride_h - p.pad_h;
-        }
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs)) break;
-          mbar_arrive_expect_tx(&full[s], C::STAGE);
-          armed |= 1u << s;
-          armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
+    int s = 0;
+    uint32_t ph = 0;
+    uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
+    for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step) {
+      const int ks = u / p.num_tiles, tile = u - ks * p.num_tiles;
+      const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+      int m0 = tm * TM + (int)rank * kBM;
+      if (m0 >= p.M) m0 = tm * TM;  // a pair's second half past the end: load valid rows, store none
+      const int nb0 = tn * BN + (int)rank * C::BNC;
+      const int kb0 = ks * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
+      int w0 = 0, h0 = 0, img = 0;
+      // im2col walk state for the next box: channel offset c0 inside tap (r, q)
+      int c0 = 0, r = 0, q = 0, tap = 0;
+      if constexpr (MODE == kIm2col) {
+        img = m0 / p.ohw;
+        const int rem = m0 - img * p.ohw;
+        const int oh = rem / p.ow, ow = rem - oh * p.ow;
+        w0 = ow * p.stride_w - p.pad_w;
+        h0 = oh * p.stride_h - p.pad_h;
+        const int k0 = kb0 * BK;
+        tap = k0 / p.cpad;
+        c0 = k0 - tap * p.cpad;
+        r = tap / p.kw;
+        q = tap - r * p.kw;
+      }
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!warp_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs)) break;
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], C::STAGE * PAIR);
           uint8_t* a_dst = sA + s * C::A_STAGE;
           uint8_t* b_dst = sB + s * C::B_STAGE;
+          const uint32_t bar_leader = PAIR == 2 ? mapa_shared(smem_u32(&full[s]), 0) : 0;
 #pragma unroll
           for (int j = 0; j < C::NSUB; ++j) {
-            const int k = kb * kBK + j * CB;
+            const int k = kb * BK + j * CB;
             if constexpr (MODE == kIm2col) {
-              int tap = k / p.cpad;
-              const int c0 = k - tap * p.cpad;
-              if (tap >= p.taps) tap = p.taps - 1;  // K padding: any real tap, its weights are zero
-              const int r = tap / p.kw, q = tap - r * p.kw;
-              tma_load_im2col_4d(&mapA, &full[s], a_dst + j * C::A_SUB, c0, w0, h0, img,
-                                 (uint16_t)(q * p.dil_w), (uint16_t)(r * p.dil_h));
+              // K padding past the last tap: re-read the last tap, its weights are zero
+              const int rr = tap < p.taps ? r : (p.taps - 1) / p.kw;
+              const int qq = tap < p.taps ? q : (p.taps - 1) - ((p.taps - 1) / p.kw) * p.kw;
+              const int cc = tap < p.taps ? c0 : p.cpad - CB;
+              if constexpr (PAIR == 2)
+                tma_load_im2col_4d_pair(&mapA, bar_leader, a_dst + j * C::A_SUB, cc, w0, h0, img,
+                                        (uint16_t)(qq * p.dil_w), (uint16_t)(rr * p.dil_h));
+              else
+                tma_load_im2col_4d(&mapA, &full[s], a_dst + j * C::A_SUB, cc, w0, h0, img, (uint16_t)(qq * p.dil_w),
+                                   (uint16_t)(rr * p.dil_h));
+              c0 += CB;
+              if (c0 == p.cpad) {
+                c0 = 0;
+                ++tap;
+                if (++q == p.kw) {
+                  q = 0;
+                  ++r;
+                }
+              }
             } else {
-              tma_load_2d(&mapA, &full[s], a_dst + j * C::A_SUB, k, m0);
+              if constexpr (PAIR == 2)
+                tma_load_2d_pair(&mapA, bar_leader, a_dst + j * C::A_SUB, k, m0);
+              else
+                tma_load_2d(&mapA, &full[s], a_dst + j * C::A_SUB, k, m0);
             }
-            tma_load_2d(&mapB, &full[s], b_dst + j * C::B_SUB, k, n0);
+            if constexpr (PAIR == 2)
+              tma_load_2d_pair(&mapB, bar_leader, b_dst + j * C::B_SUB, k, nb0);
+            else
+              tma_load_2d(&mapB, &full[s], b_dst + j * C::B_SUB, k, nb0);
           }
-          if (++s == STAGES) {
-            s = 0;
-            ph ^= 1;
+          if (rank == 0) {
+            armed |= 1u << s;
+            armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
           }
         }
-      }
-      if (*abort_flag) {
-        // Let every copy this thread issued land before the CTA's shared memory goes away.
-        volatile int dummy = 0;
-        for (int st = 0; st < STAGES; ++st)
-          if (armed & (1u << st)) mbar_wait(&full[st], (armed_ph >> st) & 1, &dummy, kDrainNs);
+        __syncwarp();
+        if (++s == p.nstages) {
+          s = 0;
+          ph ^= 1;
+        }
       }
     }
+    if (warp_aborted(abort_flag) && lane == 0) {
+      // Let every copy this thread issued land before the CTA's shared memory goes away
+      // (in a pair the leader's `full` also counts the peer's copies).
+      volatile int dummy = 0;
+      for (int st = 0; st < STAGES; ++st)
+        if (armed & (1u << st)) mbar_wait(&full[st], (armed_ph >> st) & 1, &dummy, kDrainNs);
+    }
+    __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_tf32(kBM, BN);
+    // ------------------------------------------------------------ MMA issuer (pair leader)
+    if (rank == 0) {
+      constexpr uint32_t idesc = make_idesc_tf32(TM, BN);
+      const uint64_t adesc0 = stage_desc0<CB>(smem_u32(sA), C::A_SUB);
+      const uint64_t bdesc0 = stage_desc0<CB>(smem_u32(sB), C::B_SUB);
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
       bool issued = false;
-      for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++it) {
+      for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step, ++it) {
         const int b = it & 1;
         const uint32_t aph = (it >> 1) & 1;
-        if (!mbar_wait(&tempty[b], aph ^ 1, abort_flag, kTimeoutNs)) break;
+        const int kb0 = (u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
+        if (!warp_wait(&tempty[b], aph ^ 1, abort_flag, kTimeoutNs)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + b * BN;
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag, kTimeoutNs)) {
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!warp_wait(&full[s], ph, abort_flag, kTimeoutNs)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * C::A_STAGE);
-          const uint32_t b0 = smem_u32(sB + s * C::B_STAGE);
+          if (lane == 0) {
+            const uint64_t as = adesc0 + ((s * C::A_STAGE) >> 4), bs = bdesc0 + ((s * C::B_STAGE) >> 4);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            umma_tf32(d, stage_desc<CB>(a0, j, C::A_SUB), stage_desc<CB>(b0, j, C::B_SUB), idesc,
-                      (kb | j) != 0 ? 1u : 0u);
+            for (int j = 0; j < C::KSTEPS; ++j) {
+              const uint64_t ad = as + (kslice_offset<CB>(j, C::A_SUB) >> 4);
+              const uint64_t bd = bs + (kslice_offset<CB>(j, C::B_SUB) >> 4);
+              const uint32_t acc = (kb != kb0 || j != 0) ? 1u : 0u;
+              if constexpr (PAIR == 2)
+                umma_tf32_pair(d, ad, bd, idesc, acc);
+              else
+                umma_tf32(d, ad, bd, idesc, acc);
+            }
+            if constexpr (PAIR == 2) {
+              umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
+              umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+            } else {
+              umma_commit(&empty[s]);
+            }
           }
+          __syncwarp();
           issued = true;
-          umma_commit(&empty[s]);
-          if (++s == STAGES) {
+          if (++s == p.nstages) {
             s = 0;
             ph ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[b]);
+        if (lane == 0) {
+          if constexpr (PAIR == 2) {
+            umma_commit_pair(mapa_shared(smem_u32(&tfull[b]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&tfull[b]), 1));
+          } else {
+            umma_commit(&tfull[b]);
+          }
+        }
+        __syncwarp();
       }
-      if (*abort_flag && issued) {
+      if (warp_aborted(abort_flag) && issued && lane == 0) {
         volatile int dummy = 0;
-        umma_commit(drain);
+        if constexpr (PAIR == 2)
+          umma_commit_pair(mapa_shared(smem_u32(drain), 0));
+        else
+          umma_commit(drain);
         mbar_wait(drain, 0, &dummy, kDrainNs);
       }
+      __syncwarp();
     }
   } else if (warp == 3) {
     // ------------------------------------------------------------ residual producer
@@ -253,9 +364,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int slot = 0;
         uint32_t ph = 0;
         uint32_t armed = 0, armed_ph = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+        for (int tile = unit0; tile < p.num_tiles && !*abort_flag; tile += unit_step) {  // ksplit == 1
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
-          const int m0 = tm * kBM, n0 = tn * BN;
+          const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
           bool ok = true;
           for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
             if (!mbar_wait(&rempty[slot], ph ^ 1, abort_flag, kTimeoutNs)) {
@@ -287,14 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t rph = 0;
     uint32_t chunk_no = 0;  // selects the output staging buffer
     int it = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+    // A split launch (ksplit > 1) stores raw partial sums into plane `ks` of the workspace;
+    // the finish kernel applies the epilogue after reducing the planes.
+    const bool partial = p.ksplit > 1;
+    const bool unit_alpha = p.alpha == 1.0f;
+    for (int u = unit0; u < p.num_units; u += unit_step, ++it) {
+      const int ks = u / p.num_tiles, tile = u - ks * p.num_tiles;
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
-      const int m0 = tm * kBM, n0 = tn * BN;
+      const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
       const int b = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      mbar_wait(&tfull[b], aph, abort_flag, kTimeoutNs);
-      __syncwarp();
-      if (*abort_flag) break;
+      if (!warp_wait(&tfull[b], aph, abort_flag, kTimeoutNs)) break;
       tc_fence_after();
       const int row0 = m0 + wq * 32;
       const bool rows_live = row0 < p.M;
@@ -303,40 +417,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (col0 >= p.N) break;
         const float* res_row = nullptr;
         if constexpr (RES) {
-          mbar_wait(&rfull[rslot], rph, abort_flag, kTimeoutNs);
-          __syncwarp();
-          if (*abort_flag) break;
+          if (!warp_wait(&rfull[rslot], rph, abort_flag, kTimeoutNs)) break;
           res_row = reinterpret_cast<const float*>(sRes + rslot * C::RES_SLOT) + (wq * 32 + lane) * 32;
         }
         if (rows_live) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + b * BN + c * 32 + ((uint32_t)(wq * 32) << 16), r);
           tmem_ld_wait();
-          const float bias_lane = (p.bias && col0 + lane < p.N) ? __ldg(p.bias + col0 + lane) : 0.0f;
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = p.alpha * __uint_as_float(r[i]) + __shfl_sync(0xffffffffu, bias_lane, i);
-          if constexpr (RES) {
-            const int rr = wq * 32 + lane;  // row inside the 128-row residual slot
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          if (!partial) {
+            if (!unit_alpha) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 x = *reinterpret_cast<const float4*>(res_row + ((j ^ (rr & 7)) * 4));
-              v[4 * j + 0] += x.x;
-              v[4 * j + 1] += x.y;
-              v[4 * j + 2] += x.z;
-              v[4 * j + 3] += x.w;
+              for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
             }
-          }
-          if (p.act == 1 || p.act == 5) {
+            if (p.bias) {
+              if (col0 + 32 <= p.N) {
+                // same address in every lane: one broadcast transaction per float4
+                const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = v[i] < 0.0f ? 0.0f : v[i];
-          } else if (p.act == 3) {
+                for (int j = 0; j < 8; ++j) {
+                  const float4 bb = __ldg(b4 + j);
+                  v[4 * j + 0] += bb.x;
+                  v[4 * j + 1] += bb.y;
+                  v[4 * j + 2] += bb.z;
+                  v[4 * j + 3] += bb.w;
+                }
+              } else {
+                const float bias_lane = col0 + lane < p.N ? __ldg(p.bias + col0 + lane) : 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = v[i] / (1.0f + expf(-v[i]));
-          }
-          if (p.round_out) {
+                for (int i = 0; i < 32; ++i) v[i] += __shfl_sync(0xffffffffu, bias_lane, i);
+              }
+            }
+            if constexpr (RES) {
+              const int rr = wq * 32 + lane;  // row inside the 128-row residual slot
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = to_tf32_rna(v[i]);
+              for (int j = 0; j < 8; ++j) {
+                const float4 x = *reinterpret_cast<const float4*>(res_row + ((j ^ (rr & 7)) * 4));
+                v[4 * j + 0] += x.x;
+                v[4 * j + 1] += x.y;
+                v[4 * j + 2] += x.z;
+                v[4 * j + 3] += x.w;
+              }
+            }
+            if (p.act == 1 || p.act == 5) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = v[i] < 0.0f ? 0.0f : v[i];
+            } else if (p.act == 3) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = v[i] / (1.0f + expf(-v[i]));
+            }
+            if (p.round_out) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = to_tf32_rna(v[i]);
+            }
           }
           float* st_out = reinterpret_cast<float*>(sOut + ((chunk_no & 1) * 4 + wq) * 4096);
           if (lane == 0) tma_store_wait_read<1>();  // the store that used this buffer has read it
@@ -349,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&mapY, st_out, col0, row0);
+            tma_store_3d(&mapY, st_out, col0, row0, ks);
             tma_store_commit();
           }
           ++chunk_no;
@@ -365,25 +500,110 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
+      if (lane == 0) {
+        if constexpr (PAIR == 2)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+        else
+          mbar_arrive(&tempty[b]);
+      }
     }
     if (lane == 0) tma_store_wait0();
     __syncwarp();
   }
 
   __syncthreads();
+  // In a pair, neither CTA leaves while the other may still touch its shared memory or TMEM.
+  if constexpr (PAIR == 2) cluster_sync();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR == 2)
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   if (threadIdx.x == 0 && *abort_flag && p.err) atomicExch(p.err, 1);
 }
 
-template <int BN, int CB, int MODE, bool RES>
+// Split-K finish: y = epilogue(alpha * sum_k ws[k] + bias (+ residual)), the planes summed in
+// index order so that the result does not depend on which CTA finished first.  Four output
+// columns per thread; the pad columns of y beyond N are never written.
+__global__ void __launch_bounds__(256)
+    splitk_finish_kernel(const float* __restrict__ ws, int ksplit, int M, int N, int ldw, float alpha,
+                         const float* __restrict__ bias, const float* __restrict__ res, int ldr, int act,
+                         int round_out, float* __restrict__ y, int ldy) {
+  const int groups = (N + 3) >> 2;
+  const long total = (long)M * groups;
+  const size_t plane = (size_t)M * ldw;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / groups);
+    const int n = (int)(i - (long)m * groups) * 4;
+    const float* src = ws + (size_t)m * ldw + n;
+    float4 acc = __ldcs(reinterpret_cast<const float4*>(src));
+    for (int k = 1; k < ksplit; ++k) {
+      const float4 t = __ldcs(reinterpret_cast<const float4*>(src + k * plane));
+      acc.x += t.x;
+      acc.y += t.y;
+      acc.z += t.z;
+      acc.w += t.w;
+    }
+    float v[4] = {alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w};
+    if (bias) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] += n + j < N ? __ldg(bias + n + j) : 0.0f;
+    }
+    if (res) {
+      const float4 r = *reinterpret_cast<const float4*>(res + (size_t)m * ldr + n);
+      v[0] += r.x;
+      v[1] += r.y;
+      v[2] += r.z;
+      v[3] += r.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (act == 1 || act == 5) v[j] = v[j] < 0.0f ? 0.0f : v[j];
+      else if (act == 3) v[j] = v[j] / (1.0f + expf(-v[j]));
+      if (round_out) v[j] = to_tf32_rna(v[j]);
+    }
+    float* dst = y + (size_t)m * ldy + n;
+    if (n + 4 <= N) {
+      *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      for (int j = 0; j < N - n; ++j) dst[j] = v[j];
+    }
+  }
+}
+
+// Co-resident clusters of two CTAs for a pair variant, per device (0 until queried).
+template <typename K>
+int pair_clusters(K kern, uint32_t smem, int dev, int sms) {
+  static std::atomic<int> cached[64];
+  int v = cached[dev & 63].load();
+  if (v > 0) return v;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = sms / 2;
+  }
+  cached[dev & 63].store(n);
+  return n;
+}
+
+template <int BN, int CB, int MODE, bool RES, int PAIR, int BK>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr,
-                   const TcParams& p, int grid, cudaStream_t stream) {
-  using C = Cfg<BN, CB, RES>;
-  auto kern = tc_gemm_kernel<BN, CB, MODE, RES>;
+                   const TcParams& p, int sms, cudaStream_t stream) {
+  using C = Cfg<BN, CB, RES, PAIR, BK>;
+  auto kern = tc_gemm_kernel<BN, CB, MODE, RES, PAIR, BK>;
   // The opt-in shared-memory size is a per-device function attribute: set it once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -393,24 +613,57 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     SPINN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     configured.fetch_or(bit);
   }
-  kern<<<grid, kThreads, C::SMEM, stream>>>(ma, mb, my, mr, p);
+  TcParams q = p;
+  q.nstages = C::STAGES;
+  if (const char* e = getenv("SPINN_TC_STAGES")) {  // tuning: use fewer ring stages
+    const int v = atoi(e);
+    if (v >= 2 && v < C::STAGES) q.nstages = v;
+  }
+  if constexpr (PAIR == 1) {
+    const int grid = (int)std::min<long>(q.num_units, sms);
+    kern<<<grid, kThreads, C::SMEM, stream>>>(ma, mb, my, mr, q);
+  } else {
+    const int clusters = (int)std::min<long>(q.num_units, pair_clusters(kern, C::SMEM, dev, sms));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    SPINN_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, my, mr, q));
+  }
   SPINN_CUDA_TRY(cudaGetLastError());
   return 0;
 }
 
 template <int MODE, bool RES>
-int dispatch_bn_cb(int bn, int cb, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
-                   const CUtensorMap& mr, const TcParams& p, int grid, cudaStream_t s) {
-#define SPINN_TC_CASE(BNV, CBV) \
-  if (bn == BNV && cb == CBV) return launch_variant<BNV, CBV, MODE, RES>(ma, mb, my, mr, p, grid, s);
-  SPINN_TC_CASE(256, 32) SPINN_TC_CASE(128, 32) SPINN_TC_CASE(64, 32)
+int dispatch_bn_cb(int bn, int cb, int pair, int bk, const CUtensorMap& ma, const CUtensorMap& mb,
+                   const CUtensorMap& my, const CUtensorMap& mr, const TcParams& p, int sms, cudaStream_t s) {
+#define SPINN_TC_CASE(BNV, CBV, PV, BKV)                      \
+  if (bn == BNV && cb == CBV && pair == PV && bk == BKV) \
+    return launch_variant<BNV, CBV, MODE, RES, PV, BKV>(ma, mb, my, mr, p, sms, s);
+  SPINN_TC_CASE(256, 32, 1, 32) SPINN_TC_CASE(128, 32, 1, 32) SPINN_TC_CASE(64, 32, 1, 32)
+  if constexpr (!RES) {
+    SPINN_TC_CASE(128, 32, 1, 64) SPINN_TC_CASE(64, 32, 1, 64)
+    SPINN_TC_CASE(256, 32, 2, 64) SPINN_TC_CASE(128, 32, 2, 64)
+  }
   if constexpr (MODE == kIm2col) {
-    SPINN_TC_CASE(256, 16) SPINN_TC_CASE(128, 16) SPINN_TC_CASE(64, 16)
-    SPINN_TC_CASE(256, 8) SPINN_TC_CASE(128, 8) SPINN_TC_CASE(64, 8)
-    SPINN_TC_CASE(256, 4) SPINN_TC_CASE(128, 4) SPINN_TC_CASE(64, 4)
+    SPINN_TC_CASE(256, 16, 1, 32) SPINN_TC_CASE(128, 16, 1, 32) SPINN_TC_CASE(64, 16, 1, 32)
+    SPINN_TC_CASE(256, 8, 1, 32) SPINN_TC_CASE(128, 8, 1, 32) SPINN_TC_CASE(64, 8, 1, 32)
+    SPINN_TC_CASE(256, 4, 1, 32) SPINN_TC_CASE(128, 4, 1, 32) SPINN_TC_CASE(64, 4, 1, 32)
+    if constexpr (!RES) {
+      SPINN_TC_CASE(128, 16, 1, 64) SPINN_TC_CASE(64, 16, 1, 64)
+      SPINN_TC_CASE(256, 16, 2, 64) SPINN_TC_CASE(128, 16, 2, 64)
+    }
   }
 #undef SPINN_TC_CASE
-  set_error("tcgen05 gemm: no variant for BN=%d CB=%d mode=%d", bn, cb, MODE);
+  set_error("tcgen05 gemm: no variant for BN=%d CB=%d pair=%d BK=%d mode=%d", bn, cb, pair, bk, MODE);
   return SPINN_CUDA_EUNSUPPORTED;
 }
 
@@ -436,29 +689,108 @@ CUtensorMapSwizzle swizzle_for(int cb) {
                   : cb == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : cb == 8 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
 }
 
-int choose_bn(int M, int N, int sms) {
-  // Cost model: waves of tiles times the per-tile time; narrow tiles pay a shared-memory
-  // bandwidth penalty (the W tile is re-read per 8-wide K step for fewer output columns).
-  const int cands[3] = {256, 128, 64};
-  int best = 256;
+// Largest split-K workspace a launch may use.
+constexpr size_t kWsCap = size_t(64) << 20;
+
+struct TilePlan {
+  int bn = 256;
+  int pair = 1;  // 2: CTA pairs with 256-row tiles (cta_group::2)
+  int bk = 32;   // K depth of a pipeline stage
+  int ksplit = 1;
+  int kb_per = 1;
+  size_t ws_bytes = 0;
+};
+
+// Optional override for tuning sweeps: SPINN_TC_TILES="bn,ksplit[,pair[,bk]]" (read at each
+// launch; a captured graph keeps the choice made when it was captured).
+void forced_tiles(int* bn, int* ks, int* pair, int* bk) {
+  *bn = -1;
+  *ks = 0;
+  *pair = 0;
+  *bk = 0;
+  const char* e = getenv("SPINN_TC_TILES");
+  if (e && sscanf(e, "%d,%d,%d,%d", bn, ks, pair, bk) < 1) *bn = -1;
+}
+
+// Chooses the tile shape (BN, single CTA or CTA pair, stage depth) and the K split from a
+// cost model fitted to measured B200 layer times at batches 32 and 256 (microseconds,
+// ~1.9 GHz; geometric error ~13%).  A launch costs a fixed 14 (launch ramp, pipeline fill,
+// the last tile's exposed epilogue) plus 2 per extra wave of work units.  A unit costs the
+// larger of its main loop and its epilogue (0.4 per 32 output columns, overlapped with the
+// next unit's main loop through the second TMEM accumulator).  Main-loop stages cost about
+// the same whatever their width -- they are bounded by the per-stage barrier handoff as much
+// as by tensor throughput -- so deep stages and CTA pairs (twice the rows per MMA) pay off.
+// A split adds the finish pass: (ksplit + 2) x M x N floats at 8 TB/s (the partials are
+// L2-resident).  64-deep stages need channel blocks of 16 or 32 and no fused residual
+// (the residual ring would leave too few of them).
+TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t ws_limit, int force_bn) {
+  int fbn, fks, fpair, fbk;
+  forced_tiles(&fbn, &fks, &fpair, &fbk);
+  if (force_bn <= 0 && (fbn == 64 || fbn == 128 || fbn == 256)) force_bn = fbn;
+  struct Shape {
+    int bn, pair, bk;
+    double per_stage;
+  };
+  const Shape shapes[7] = {{256, 1, 32, 0.332}, {128, 1, 32, 0.266}, {64, 1, 32, 0.237}, {128, 1, 64, 0.405},
+                           {64, 1, 64, 0.319},  {256, 2, 64, 0.617}, {128, 2, 64, 0.456}};
+  const size_t ldw = (size_t)((N + 3) & ~3);
+  TilePlan best;
   double best_cost = 1e300;
-  const int tm = (M + kBM - 1) / kBM;
-  for (int bn : cands) {
-    if (bn > 64 && bn >= 2 * ((N + 63) / 64) * 64) continue;  // far wider than N
-    const int tn = (N + bn - 1) / bn;
-    const long tiles = (long)tm * tn;
-    const long waves = (tiles + sms - 1) / sms;
-    const double per_tile = bn == 256 ? 256.0 : bn == 128 ? 128.0 * 1.15 : 64.0 * 1.6;
-    const double cost = waves * per_tile;
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = bn;
+  for (const Shape& sh : shapes) {
+    const int bn = sh.bn;
+    if (force_bn > 0 && bn != force_bn) continue;
+    if (fpair > 0 && sh.pair != fpair) continue;
+    if (fbk > 0 && sh.bk != fbk) continue;
+    if (sh.bk == 64 && ((cb != 32 && cb != 16) || has_res)) continue;
+    if (force_bn <= 0 && sh.pair == 1 && bn > 64 && bn >= 2 * ((N + 63) / 64) * 64) continue;  // far wider than N
+    const int slots = sh.pair == 2 ? sms / 2 : sms;
+    const int num_kb = (K + sh.bk - 1) / sh.bk;
+    const long tiles = (long)((M + kBM * sh.pair - 1) / (kBM * sh.pair)) * ((N + bn - 1) / bn);
+    for (int ks = 1; ks <= 32; ++ks) {
+      const int kb_per = (num_kb + ks - 1) / ks;
+      const int kse = (num_kb + kb_per - 1) / kb_per;  // slices actually used
+      if (kse != ks) continue;
+      if (fks > 0 && ks != fks) continue;
+      if (ks > 1 && kb_per * sh.bk < 128 && fks <= 0) break;
+      const size_t ws = ks > 1 ? (size_t)ks * M * ldw * 4 : 0;
+      if (ws > ws_limit) break;
+      const long units = tiles * ks;
+      const long waves = (units + slots - 1) / slots;
+      double cost = 14.0 + (waves - 1) * 2.0 + waves * std::max(kb_per * sh.per_stage, 0.4 * bn / 32);
+      if (ks > 1) cost += (double)(ks + 2) * M * N * 4 / 8.0e6;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best.bn = bn;
+        best.pair = sh.pair;
+        best.bk = sh.bk;
+        best.ksplit = ks;
+        best.kb_per = kb_per;
+        best.ws_bytes = ws;
+      }
     }
+  }
+  if (best_cost == 1e300) {  // forced shape infeasible: single-CTA tiles of the forced width, no split
+    best.bn = force_bn > 0 ? force_bn : 256;
+    best.pair = 1;
+    best.bk = 32;
+    best.ksplit = 1;
+    best.kb_per = (K + 31) / 32;
+    best.ws_bytes = 0;
   }
   return best;
 }
 
+int problem_k(const TcGemmArgs& a) { return a.a_mode == 0 ? a.kh * a.kw * a.cpad : a.K; }
+int problem_cb(const TcGemmArgs& a) { return a.a_mode == 0 ? channel_block(a.cpad) : 32; }
+
 }  // namespace
+
+size_t tc_gemm_workspace_bytes(const TcGemmArgs& a) {
+  if (!tc_gemm_supported(a, nullptr)) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  return plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), kWsCap, a.bn).ws_bytes;
+}
 
 bool tc_gemm_supported(const TcGemmArgs& a, std::string* why) {
   auto fail = [&](const char* m) {
@@ -506,8 +838,6 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   int rc;
   if (a.a_mode == 0) {
     cb = channel_block(a.cpad);
-    const int K = a.kh * a.kw * a.cpad;
-    p.num_kb = tc_num_kb(K);
     p.cpad = a.cpad;
     p.taps = a.kh * a.kw;
     p.kw = a.kw;
@@ -524,7 +854,6 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     rc = encode_im2col_4d(&ma, a.x, a.n, a.h, a.w, a.cpad, lw, lh, uw, uh, cb, kBM, a.sw, a.sh, swizzle_for(cb));
     if (rc) return rc;
   } else {
-    p.num_kb = tc_num_kb(a.K);
     p.cpad = a.K;
     p.taps = 1;
     p.kw = 1;
@@ -532,18 +861,26 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  if (p.num_kb * 32 > a.kpad) {
-    set_error("tcgen05 gemm: weights padded to %d, need %d", a.kpad, p.num_kb * 32);
+  const int K = problem_k(a);
+  if (tc_num_kb(K) * 32 > a.kpad) {
+    set_error("tcgen05 gemm: weights padded to %d, need %d", a.kpad, tc_num_kb(K) * 32);
     return SPINN_CUDA_EINVAL;
   }
-  const int bn = a.bn ? a.bn : choose_bn(a.M, a.N, sms);
+  const TilePlan tp =
+      plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, a.ws ? std::min(a.ws_bytes, kWsCap) : 0, a.bn);
+  p.num_kb = (K + tp.bk - 1) / tp.bk;  // stages beyond kpad read zero weights
+  const int bn = tp.bn;
+  const bool split = tp.ksplit > 1;
   rc = encode_tiled_2d(&mb, a.wt, (uint64_t)a.kpad, (uint64_t)a.N, (uint64_t)a.kpad * 4, (uint32_t)cb,
-                       (uint32_t)bn, swizzle_for(cb));
+                       (uint32_t)(bn / tp.pair), swizzle_for(cb));
   if (rc) return rc;
-  rc = encode_tiled_2d(&my, a.y, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.ldy * 4, 32, 32,
-                       CU_TENSOR_MAP_SWIZZLE_128B);
+  const int ldw = (a.N + 3) & ~3;
+  rc = split ? encode_tiled_3d(&my, a.ws, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)tp.ksplit, (uint64_t)ldw * 4, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_128B)
+             : encode_tiled_3d(&my, a.y, (uint64_t)a.N, (uint64_t)a.M, 1, (uint64_t)a.ldy * 4, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (a.res) {
+  if (a.res && !split) {
     rc = encode_tiled_2d(&mr, a.res, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.ldr * 4, 32, kBM,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -551,24 +888,39 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     mr = my;
   }
   p.tiles_n = (a.N + bn - 1) / bn;
-  const long tiles = (long)((a.M + kBM - 1) / kBM) * p.tiles_n;
+  const long tiles = (long)((a.M + kBM * tp.pair - 1) / (kBM * tp.pair)) * p.tiles_n;
   if (tiles > 0x7FFFFFFF) {
     set_error("tcgen05 gemm: too many tiles");
     return SPINN_CUDA_EINVAL;
   }
   p.num_tiles = (int)tiles;
-  p.has_res = a.res != nullptr;
+  p.ksplit = tp.ksplit;
+  p.kb_per = split ? tp.kb_per : p.num_kb;
+  if (tiles * tp.ksplit > 0x7FFFFFFF) {
+    set_error("tcgen05 gemm: too many work units");
+    return SPINN_CUDA_EINVAL;
+  }
+  p.num_units = (int)(tiles * tp.ksplit);
+  p.has_res = a.res != nullptr && !split;
   p.act = a.act;
   p.round_out = a.round_out;
   p.alpha = a.alpha;
   p.bias = a.bias;
   p.err = a.err ? a.err : device_error_flag(dev);
-  const int grid = (int)std::min<long>(tiles, sms);
+  const int pr = tp.pair;
   if (a.a_mode == 0)
-    return a.res ? dispatch_bn_cb<kIm2col, true>(bn, cb, ma, mb, my, mr, p, grid, stream)
-                 : dispatch_bn_cb<kIm2col, false>(bn, cb, ma, mb, my, mr, p, grid, stream);
-  return a.res ? dispatch_bn_cb<kTiled, true>(bn, cb, ma, mb, my, mr, p, grid, stream)
-               : dispatch_bn_cb<kTiled, false>(bn, cb, ma, mb, my, mr, p, grid, stream);
+    rc = p.has_res ? dispatch_bn_cb<kIm2col, true>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream)
+                   : dispatch_bn_cb<kIm2col, false>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream);
+  else
+    rc = p.has_res ? dispatch_bn_cb<kTiled, true>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream)
+                   : dispatch_bn_cb<kTiled, false>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream);
+  if (rc || !split) return rc;
+  const long groups = (long)a.M * ((a.N + 3) / 4);
+  const int fgrid = (int)std::min<long>((groups + 255) / 256, (long)sms * 8);
+  splitk_finish_kernel<<<fgrid, 256, 0, stream>>>(a.ws, tp.ksplit, a.M, a.N, ldw, a.alpha, a.bias, a.res, a.ldr, a.act,
+                                                  a.round_out, a.y, a.ldy);
+  SPINN_CUDA_TRY(cudaGetLastError());
+  return 0;
 }
 
 }  // namespace spinn

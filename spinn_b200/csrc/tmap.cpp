@@ -82,6 +82,30 @@ int encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   return 0;
 }
 
+int encode_tiled_3d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t planes,
+                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  std::call_once(g_once, load_entry_points);
+  if (!g_tiled) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return SPINN_CUDA_ECUDA;
+  }
+  SPINN_CHECK_ARG((reinterpret_cast<uintptr_t>(base) & 15) == 0, "tensor map base %p not 16-B aligned", base);
+  SPINN_CHECK_ARG(row_stride_bytes % 16 == 0, "tensor map row stride not a multiple of 16");
+  cuuint64_t dims[3] = {inner, outer, planes};
+  cuuint64_t strides[2] = {row_stride_bytes, row_stride_bytes * outer};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    return SPINN_CUDA_ECUDA;
+  }
+  small_tensor_fixup(map, row_stride_bytes * outer * planes);
+  return 0;
+}
+
 int encode_im2col_4d(CUtensorMap* map, const void* base, int n, int h, int w, int c, int lower_w, int lower_h,
                      int upper_w, int upper_h, int channels_per_pixel, int pixels_per_column, int stride_w,
                      int stride_h, CUtensorMapSwizzle swizzle) {

@@ -33,6 +33,8 @@ CONV_CASES = [
     (1, 8, 12, 12, 24, 3, 1, 1, 1, 4, False, True),      # C=8 (32-B swizzle), +residual, no bias
     (2, 256, 7, 7, 512, 1, 2, 0, 1, 0, True, False),     # 1x1 stride 2 downsample shape
     (1, 1024, 14, 14, 256, 1, 1, 0, 1, 1, True, False),  # deep K
+    (1, 256, 7, 7, 256, 3, 1, 1, 1, 5, True, True),      # split-K (2 tiles, 72 K blocks) + residual in the finish
+    (3, 512, 7, 7, 2048, 1, 1, 0, 1, 3, True, False),    # split-K, SiLU applied after the reduction
     (1, 32, 40, 40, 32, 3, 1, 1, 32, 3, True, False),    # depthwise (CUDA cores)
     (1, 32, 10, 10, 64, 3, 1, 1, 4, 1, True, False),     # grouped (CUDA cores)
 ]
@@ -129,3 +131,60 @@ def test_weight_cache_follows_content_at_a_reused_address(cuda_lib, port_oracle)
     w[...] = rng.normal(0, 0.3, w.shape)
     runtime.conv2d(x, w, yc, None, None, params)
     assert rel_l2(yc, port_oracle.conv2d(x, w, None, None, (1, 1), (1, 1))) <= TOL
+
+
+def test_split_k_is_deterministic(cuda_lib):
+    """A split-K launch (one tile, many K slices) reduces its partial sums in a fixed order:
+    repeated runs are bit-identical."""
+    from spinn_b200 import runtime
+    rng = np.random.default_rng(5)
+    x, wt, b, _, yshape = _conv_case(rng, 1, 512, 7, 7, 128, 3, 1, 1)
+    params = runtime.conv_params((3, 3), (1, 1), (1, 1, 1, 1), (1, 1), 1, 0, 1)
+    outs = []
+    for _ in range(3):
+        y = np.zeros(yshape, np.float32)
+        runtime.conv2d(x, wt, y, b, None, params)
+        outs.append(y)
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+
+
+PAIR_SHAPES = ["256,1,2", "128,1,2", "256,3,2", "128,2,2"]
+TC_CASES = [c for c in CONV_CASES if c[8] == 1]
+
+
+@pytest.mark.parametrize("tiles", PAIR_SHAPES)
+@pytest.mark.parametrize("case", TC_CASES, ids=lambda c: "x".join(map(str, c[:9])) + f"-a{c[9]}")
+def test_conv2d_cta_pair_tiles(cuda_lib, port_oracle, monkeypatch, case, tiles):
+    """The 2-SM (cta_group::2) tiles, with and without split-K, forced on every conv shape;
+    pairs whose second half lies past the last row must store nothing there."""
+    from spinn_b200 import runtime
+    monkeypatch.setenv("SPINN_TC_TILES", tiles)
+    n, c, h, w, oc, k, s, p, g, act, bias, res = case
+    rng = np.random.default_rng(hash(case) & 0xFFFF)
+    x, wt, b, r, yshape = _conv_case(rng, n, c, h, w, oc, k, s, p, g, act, bias, res)
+    params = runtime.conv_params((k, k), (s, s), (p, p, p, p), (1, 1), g, 0, act)
+    y = np.full(yshape, np.nan, np.float32)
+    runtime.conv2d(x, wt, y, b, r, params)
+    ref = port_oracle.conv2d(x, wt, b, r, (s, s), (p, p), (1, 1), g, act, yshape[2:])
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) <= TOL, rel_l2(y, ref)
+
+
+@pytest.mark.parametrize("tiles", PAIR_SHAPES)
+@pytest.mark.parametrize("case", GEMM_CASES, ids=lambda c: "x".join(map(str, c[:5])))
+def test_gemm_cta_pair_tiles(cuda_lib, port_oracle, monkeypatch, case, tiles):
+    from spinn_b200 import runtime
+    monkeypatch.setenv("SPINN_TC_TILES", tiles)
+    m, n, k, ta, tb, alpha, beta, cmode = case
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    a = rng.uniform(-1, 1, (k, m) if ta else (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (n, k) if tb else (k, n)).astype(np.float32)
+    c = None
+    if cmode == "vector":
+        c = rng.uniform(-1, 1, n).astype(np.float32)
+    elif cmode == "full":
+        c = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+    y = np.zeros((m, n), np.float32)
+    runtime.gemm(a, b, y, c, runtime.gemm_params(alpha, beta, ta, tb))
+    ref = port_oracle.gemm(a, b, c, m, n, k, ta, tb, alpha, beta)
+    assert rel_l2(y, ref) <= TOL, rel_l2(y, ref)
