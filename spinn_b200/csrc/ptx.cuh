@@ -121,6 +121,16 @@ __device__ __forceinline__ void tma_store_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with the programmatic-serialization attribute may start while the
+// previous kernel in the stream is finishing; griddep_wait() blocks until that kernel has
+// completed and its memory is visible, and must precede every access to data it produced or
+// reads.  griddep_launch_dependents() lets the next such kernel start its own prologue.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ CTA pairs (2-SM MMA)
 // A cluster of two CTAs shares one tcgen05 MMA (cta_group::2): each CTA holds half of A (its
 // 128 rows) and half of B, and its TMEM receives its 128 rows of the accumulator.

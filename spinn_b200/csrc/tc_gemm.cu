@@ -9,12 +9,14 @@
 // (SPINN/run_time/ops/conv/conv2d.c:49-79,172-225, ops/mm/gemm_kernel.c:346-590) and its
 // epilogue (gemm_kernel.c:316-338), which here runs on the accumulator before the store.
 //
-// Structure (one persistent CTA per SM, 256 threads):
-//   warp 0      TMA producer: STAGES-deep ring of (A 128x32, W BNx32) tiles in shared memory
-//   warp 1      MMA issuer: 4 x tcgen05.mma (128 x BN x 8) per stage into TMEM
+// Structure (one persistent CTA per SM, 384 threads):
+//   warp 0      TMA producer: STAGES-deep ring of (A 128xBK, W BNxBK) tiles in shared memory
+//   warp 1      MMA issuer: BK/8 x tcgen05.mma (128 x BN x 8) per stage into TMEM
 //   warp 2      TMEM allocator (2 accumulators x BN columns)
-//   warps 4..7  epilogue: tcgen05.ld -> bias / residual / activation / tf32 rounding ->
-//               swizzled shared staging -> TMA store; each warp owns 32 accumulator lanes
+//   warp 3      residual producer (fused residual variants)
+//   warps 4..11 epilogue: tcgen05.ld -> bias / residual / activation / tf32 rounding ->
+//               swizzled shared staging -> TMA store; warps w and w+4 share the 32
+//               accumulator lanes of quarter w % 4 and take alternate 32-column chunks
 // Tiles are 128 output pixels x BN output channels, scheduled n-fastest so that CTAs running
 // together share the activation tile in L2.  Two TMEM accumulators let the epilogue of one
 // tile overlap the main loop of the next.
@@ -40,7 +42,6 @@ namespace spinn {
 namespace {
 
 constexpr int kBM = 128;       // tile rows (output pixels) = TMEM lanes
-constexpr int kThreads = 256;
 constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s per wait; a stage takes microseconds
 constexpr uint64_t kDrainNs = 200000000ull;
 constexpr int kSmemBudget = 232448 - 2048;      // 227 KiB opt-in minus barriers and alignment slack
@@ -76,9 +77,17 @@ struct Cfg {
   static constexpr uint32_t A_STAGE = kBM * BK * 4;
   static constexpr uint32_t B_STAGE = BNC * BK * 4;
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
-  // epilogue: two 32x32 fp32 staging blocks per epilogue warp (double-buffered TMA stores)
-  static constexpr uint32_t OUT_BYTES = 2 * 4 * 4096;
-  // residual ring: 128 rows x 32 columns per slot, filled by the residual producer warp
+  // Epilogue: groups of four warps (one per TMEM lane quarter); with two groups, group g
+  // takes the 32-column chunks c with c % 2 == g.  Fused-residual variants keep one group:
+  // their residual ring (128 rows x 32 columns per slot, filled by the residual producer) needs
+  // three slots of prefetch, and a ring shared by two groups would let one group wait on a
+  // slot two phases ahead of the other's, which the parity test cannot tell apart.
+  static constexpr int EPI_GROUPS = RES ? 1 : 2;
+  static constexpr int EPI_WARPS = 4 * EPI_GROUPS;
+  static constexpr int THREADS = 128 + 32 * EPI_WARPS;
+  // output staging: 32x32 fp32 blocks, two per warp with one group, one per warp with two
+  static constexpr int OUT_BUFS = 2 / EPI_GROUPS;
+  static constexpr uint32_t OUT_BYTES = 8 * 4096;
   static constexpr int RES_SLOTS = RES ? 3 : 0;
   static constexpr uint32_t RES_SLOT = kBM * 32 * 4;
   static constexpr uint32_t EPI = OUT_BYTES + RES_SLOTS * RES_SLOT;
@@ -129,7 +138,7 @@ __device__ __forceinline__ bool warp_aborted(volatile int* abort) { return __any
 // The producer and MMA warps run their loops with all 32 lanes (lane 0 issues): a single
 // diverged lane spends about half again as long per barrier handoff.
 template <int BN, int CB, int MODE, bool RES, int PAIR, int BK_>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapY, const __grid_constant__ CUtensorMap mapR,
                    const TcParams p) {
@@ -142,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * C::A_STAGE;
-  uint8_t* sOut = sB + STAGES * C::B_STAGE;  // [2][4 warps][4 KiB], 1024-aligned
+  uint8_t* sOut = sB + STAGES * C::B_STAGE;  // [OUT_BUFS][EPI_WARPS][4 KiB], 1024-aligned
   uint8_t* sRes = sOut + C::OUT_BYTES;       // [RES_SLOTS][16 KiB]
   uint64_t* full = reinterpret_cast<uint64_t*>(sRes + C::RES_SLOTS * C::RES_SLOT);
   uint64_t* empty = full + STAGES;
@@ -165,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4 * PAIR);
+      mbar_init(&tempty[b], C::EPI_WARPS * PAIR);
     }
     for (int r = 0; r < NRS; ++r) {
       mbar_init(&rfull[r], 1);
@@ -195,6 +204,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (PAIR == 2) cluster_sync();  // the peer's barriers are initialised before use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above overlapped the previous kernel's tail; from here on its outputs (our
+  // activations, residual) are visible and the buffers it read may be overwritten.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (A, W)
@@ -361,14 +374,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // loads overlap the main loop instead of sitting on the epilogue's critical path.
     if constexpr (RES) {
       if (lane == 0) {
-        int slot = 0;
-        uint32_t ph = 0;
+        int count = 0;  // chunks loaded so far
         uint32_t armed = 0, armed_ph = 0;
         for (int tile = unit0; tile < p.num_tiles && !*abort_flag; tile += unit_step) {  // ksplit == 1
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
           const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
           bool ok = true;
           for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
+            const int slot = count % C::RES_SLOTS;
+            const uint32_t ph = (count / C::RES_SLOTS) & 1;
             if (!mbar_wait(&rempty[slot], ph ^ 1, abort_flag, kTimeoutNs)) {
               ok = false;
               break;
@@ -377,10 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             armed |= 1u << slot;
             armed_ph = (armed_ph & ~(1u << slot)) | (ph << slot);
             tma_load_2d(&mapR, &rfull[slot], sRes + slot * C::RES_SLOT, n0 + c * 32, m0);
-            if (++slot == C::RES_SLOTS) {
-              slot = 0;
-              ph ^= 1;
-            }
+            ++count;
           }
           if (!ok) break;
         }
@@ -393,10 +404,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
-    const int wq = warp & 3;  // TMEM lane quarter this warp may access
-    int rslot = 0;
-    uint32_t rph = 0;
-    uint32_t chunk_no = 0;  // selects the output staging buffer
+    const int wq = warp & 3;         // TMEM lane quarter this warp may access
+    const int eg = (warp - 4) >> 2;  // epilogue group
+    int rcount = 0;                  // residual chunks consumed (one group when RES)
+    uint32_t nstore = 0;             // stores issued by this warp (selects the staging buffer)
     int it = 0;
     // A split launch (ksplit > 1) stores raw partial sums into plane `ks` of the workspace;
     // the finish kernel applies the epilogue after reducing the planes.
@@ -415,9 +426,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = n0 + c * 32;
         if (col0 >= p.N) break;
+        if (c % C::EPI_GROUPS != eg) continue;
         const float* res_row = nullptr;
+        const int rslot = C::RES_SLOTS > 0 ? rcount % C::RES_SLOTS : 0;
         if constexpr (RES) {
-          if (!warp_wait(&rfull[rslot], rph, abort_flag, kTimeoutNs)) break;
+          if (!warp_wait(&rfull[rslot], (rcount / C::RES_SLOTS) & 1, abort_flag, kTimeoutNs)) break;
           res_row = reinterpret_cast<const float*>(sRes + rslot * C::RES_SLOT) + (wq * 32 + lane) * 32;
         }
         if (rows_live) {
@@ -473,8 +486,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 32; ++i) v[i] = to_tf32_rna(v[i]);
             }
           }
-          float* st_out = reinterpret_cast<float*>(sOut + ((chunk_no & 1) * 4 + wq) * 4096);
-          if (lane == 0) tma_store_wait_read<1>();  // the store that used this buffer has read it
+          float* st_out =
+              reinterpret_cast<float*>(sOut + ((nstore % C::OUT_BUFS) * C::EPI_WARPS + (warp - 4)) * 4096);
+          // the store that last used this buffer has read it
+          if (lane == 0) tma_store_wait_read<C::OUT_BUFS - 1>();
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -487,15 +502,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_3d(&mapY, st_out, col0, row0, ks);
             tma_store_commit();
           }
-          ++chunk_no;
+          ++nstore;
         }
         if constexpr (RES) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&rempty[rslot]);
-          if (++rslot == C::RES_SLOTS) {
-            rslot = 0;
-            rph ^= 1;
-          }
+          ++rcount;
         }
       }
       tc_fence_before();
@@ -573,15 +585,20 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Co-resident clusters of two CTAs for a pair variant, per device (0 until queried).
+// Launches overlap the previous kernel's tail (programmatic dependent launch) unless
+// SPINN_NO_PDL is set.
+bool pdl_enabled() {
+  static const bool on = getenv("SPINN_NO_PDL") == nullptr;
+  return on;
+}
+
+// Co-resident clusters of two CTAs for a pair variant (queried once per variant and device
+// by the caller).
 template <typename K>
-int pair_clusters(K kern, uint32_t smem, int dev, int sms) {
-  static std::atomic<int> cached[64];
-  int v = cached[dev & 63].load();
-  if (v > 0) return v;
+int pair_clusters(K kern, uint32_t smem, int threads, int sms) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -595,7 +612,6 @@ int pair_clusters(K kern, uint32_t smem, int dev, int sms) {
     cudaGetLastError();
     n = sms / 2;
   }
-  cached[dev & 63].store(n);
   return n;
 }
 
@@ -619,25 +635,41 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     const int v = atoi(e);
     if (v >= 2 && v < C::STAGES) q.nstages = v;
   }
-  if constexpr (PAIR == 1) {
-    const int grid = (int)std::min<long>(q.num_units, sms);
-    kern<<<grid, kThreads, C::SMEM, stream>>>(ma, mb, my, mr, q);
-  } else {
-    const int clusters = (int)std::min<long>(q.num_units, pair_clusters(kern, C::SMEM, dev, sms));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = C::SMEM;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    SPINN_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, my, mr, q));
+  int grid;
+  if constexpr (PAIR == 1)
+    grid = (int)std::min<long>(q.num_units, sms);
+  else
+  {
+    static std::atomic<int> clusters[64];
+    int nc = clusters[dev & 63].load();
+    if (nc <= 0) {
+      nc = pair_clusters(kern, C::SMEM, C::THREADS, sms);
+      clusters[dev & 63].store(nc);
+    }
+    grid = 2 * (int)std::min<long>(q.num_units, nc);
   }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(C::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if constexpr (PAIR == 2) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 2;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  SPINN_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, my, mr, q));
   SPINN_CUDA_TRY(cudaGetLastError());
   return 0;
 }
