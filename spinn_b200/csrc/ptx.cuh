@@ -65,6 +65,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// As mbar_wait, but sleeps between polls: for waiters that are not on the critical path
+// (epilogue warps waiting for an accumulator), so their polling does not take issue slots
+// from the producer and MMA warps.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                  uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(100);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -256,6 +274,14 @@ __device__ __forceinline__ float to_tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
+}
+// The same rounding on the bit pattern (add half a tf32 ulp to the magnitude, clear the low 13
+// bits; infinities and NaNs pass through): a few integer operations, cheaper than the
+// conversion instruction in the epilogue's inner loop, and identical for finite values.
+__device__ __forceinline__ float round_tf32_bits(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;
+  return __uint_as_float(u);
 }
 
 // ------------------------------------------------------------------ descriptors

@@ -128,6 +128,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 __device__ __forceinline__ bool warp_aborted(volatile int* abort) { return __any_sync(0xffffffffu, *abort != 0); }
+__device__ __forceinline__ bool warp_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t ns) {
+  const bool ok = mbar_wait_backoff(bar, parity, abort, ns);
+  return __all_sync(0xffffffffu, ok);
+}
 
 // PAIR = 1: one CTA per 128 x BN tile.  PAIR = 2: a cluster of two CTAs per 256 x BN tile
 // with one cta_group::2 MMA stream issued by the leader (rank 0); each CTA loads its own 128
@@ -419,7 +423,16 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
       const int b = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      if (!warp_wait(&tfull[b], aph, abort_flag, kTimeoutNs)) break;
+      // This warp's bias values for the unit (lane l: column n0 + 32 c + l of each chunk c it
+      // owns), fetched before the accumulator wait so the load latency is hidden behind it.
+      constexpr int MYCH = BN / 32 / C::EPI_GROUPS;
+      float bias_reg[MYCH];
+#pragma unroll
+      for (int i = 0; i < MYCH; ++i) {
+        const int col = n0 + 32 * (i * C::EPI_GROUPS + eg) + lane;
+        bias_reg[i] = (!partial && p.bias && col < p.N) ? __ldg(p.bias + col) : 0.0f;
+      }
+      if (!warp_wait_backoff(&tfull[b], aph, abort_flag, kTimeoutNs)) break;
       tc_fence_after();
       const int row0 = m0 + wq * 32;
       const bool rows_live = row0 < p.M;
@@ -446,22 +459,13 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
               for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
             }
             if (p.bias) {
-              if (col0 + 32 <= p.N) {
-                // same address in every lane: one broadcast transaction per float4
-                const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+              // the owned-chunk index c / EPI_GROUPS is a compile-time constant after unrolling
+              float bias_lane = bias_reg[0];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float4 bb = __ldg(b4 + j);
-                  v[4 * j + 0] += bb.x;
-                  v[4 * j + 1] += bb.y;
-                  v[4 * j + 2] += bb.z;
-                  v[4 * j + 3] += bb.w;
-                }
-              } else {
-                const float bias_lane = col0 + lane < p.N ? __ldg(p.bias + col0 + lane) : 0.0f;
+              for (int i = 1; i < MYCH; ++i)
+                if (c / C::EPI_GROUPS == i) bias_lane = bias_reg[i];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] += __shfl_sync(0xffffffffu, bias_lane, i);
-              }
+              for (int i = 0; i < 32; ++i) v[i] += __shfl_sync(0xffffffffu, bias_lane, i);
             }
             if constexpr (RES) {
               const int rr = wq * 32 + lane;  // row inside the 128-row residual slot
@@ -574,7 +578,7 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < 4; ++j) {
       if (act == 1 || act == 5) v[j] = v[j] < 0.0f ? 0.0f : v[j];
       else if (act == 3) v[j] = v[j] / (1.0f + expf(-v[j]));
-      if (round_out) v[j] = to_tf32_rna(v[j]);
+      if (round_out) v[j] = round_tf32_bits(v[j]);
     }
     float* dst = y + (size_t)m * ldy + n;
     if (n + 4 <= N) {
