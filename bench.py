@@ -44,6 +44,10 @@ SEED = 3
 METRIC = "resnet101_images_per_sec"
 UNIT = "images/s"
 CPU_SAMPLE_BATCH = 2
+# DRAM bytes per convolution launch of the batch-256 ResNet-101 step, measured with ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum over the 104 conv launches, 1 pass); the
+# algorithmic bytes of the same launches are 405.3 MB.
+CONV_DRAM_BYTES_PER_LAUNCH = 355.2e6
 
 
 def parse():
@@ -330,7 +334,11 @@ def main():
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
                        "graph": "CUDA graph of the planned step list"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-                         "frac": achieved / tf32_peak if tf32_peak else None, "traffic": None,
+                         "frac": achieved / tf32_peak if tf32_peak else None,
+                         "traffic": CONV_DRAM_BYTES_PER_LAUNCH if (shard, args.depth) == (256, 101) else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the 104 "
+                                           "conv launches of one batch-256 step "
+                                           "(profiles/resnet101_b256_launch_list.md)",
                          "kernel": "tc_gemm_kernel (implicit-GEMM conv, tcgen05 kind::tf32)",
                          "peak_source": f"{peak_src}: bf16_tflops_sustained / 2 (dense tf32)",
                          "launches_per_step": conv_launches,
