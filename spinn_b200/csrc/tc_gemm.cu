@@ -78,17 +78,19 @@ struct Cfg {
   static constexpr uint32_t B_STAGE = BNC * BK * 4;
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
   // Epilogue: groups of four warps (one per TMEM lane quarter); with two groups, group g
-  // takes the 32-column chunks c with c % 2 == g.  Fused-residual variants keep one group:
-  // their residual ring (128 rows x 32 columns per slot, filled by the residual producer) needs
-  // three slots of prefetch, and a ring shared by two groups would let one group wait on a
-  // slot two phases ahead of the other's, which the parity test cannot tell apart.
-  static constexpr int EPI_GROUPS = RES ? 1 : 2;
+  // takes the 32-column chunks c with c % 2 == g.  The residual (128 rows x 32 columns per
+  // slot, filled by the residual producer warp) goes through one ring per group -- a ring
+  // shared by two groups would let one group wait on a slot two phases ahead of the other's,
+  // which the parity test cannot tell apart.  256-wide residual tiles keep a single group
+  // with a 3-slot ring: two 2-slot rings would leave too few stages beside a 256-wide W tile.
+  static constexpr int EPI_GROUPS = (RES && BN == 256) ? 1 : 2;
   static constexpr int EPI_WARPS = 4 * EPI_GROUPS;
   static constexpr int THREADS = 128 + 32 * EPI_WARPS;
   // output staging: 32x32 fp32 blocks, two per warp with one group, one per warp with two
   static constexpr int OUT_BUFS = 2 / EPI_GROUPS;
   static constexpr uint32_t OUT_BYTES = 8 * 4096;
-  static constexpr int RES_SLOTS = RES ? 3 : 0;
+  static constexpr int RES_G = !RES ? 0 : EPI_GROUPS == 1 ? 3 : 2;  // slots per group
+  static constexpr int RES_SLOTS = RES_G * EPI_GROUPS;
   static constexpr uint32_t RES_SLOT = kBM * 32 * 4;
   static constexpr uint32_t EPI = OUT_BYTES + RES_SLOTS * RES_SLOT;
   static constexpr int STAGES_FIT = (kSmemBudget - (int)EPI) / (int)STAGE;
@@ -378,15 +380,16 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     // loads overlap the main loop instead of sitting on the epilogue's critical path.
     if constexpr (RES) {
       if (lane == 0) {
-        int count = 0;  // chunks loaded so far
+        int count[2] = {0, 0};  // chunks loaded so far for each epilogue group
         uint32_t armed = 0, armed_ph = 0;
         for (int tile = unit0; tile < p.num_tiles && !*abort_flag; tile += unit_step) {  // ksplit == 1
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
           const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
           bool ok = true;
           for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
-            const int slot = count % C::RES_SLOTS;
-            const uint32_t ph = (count / C::RES_SLOTS) & 1;
+            const int g = c % C::EPI_GROUPS;
+            const int slot = g * C::RES_G + count[g] % C::RES_G;
+            const uint32_t ph = (count[g] / C::RES_G) & 1;
             if (!mbar_wait(&rempty[slot], ph ^ 1, abort_flag, kTimeoutNs)) {
               ok = false;
               break;
@@ -395,7 +398,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
             armed |= 1u << slot;
             armed_ph = (armed_ph & ~(1u << slot)) | (ph << slot);
             tma_load_2d(&mapR, &rfull[slot], sRes + slot * C::RES_SLOT, n0 + c * 32, m0);
-            ++count;
+            ++count[g];
           }
           if (!ok) break;
         }
@@ -410,7 +413,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int wq = warp & 3;         // TMEM lane quarter this warp may access
     const int eg = (warp - 4) >> 2;  // epilogue group
-    int rcount = 0;                  // residual chunks consumed (one group when RES)
+    int rcount = 0;                  // residual chunks this group has consumed
     uint32_t nstore = 0;             // stores issued by this warp (selects the staging buffer)
     int it = 0;
     // A split launch (ksplit > 1) stores raw partial sums into plane `ks` of the workspace;
@@ -441,9 +444,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
         if (col0 >= p.N) break;
         if (c % C::EPI_GROUPS != eg) continue;
         const float* res_row = nullptr;
-        const int rslot = C::RES_SLOTS > 0 ? rcount % C::RES_SLOTS : 0;
+        const int rslot = C::RES_G > 0 ? eg * C::RES_G + rcount % C::RES_G : 0;
         if constexpr (RES) {
-          if (!warp_wait(&rfull[rslot], (rcount / C::RES_SLOTS) & 1, abort_flag, kTimeoutNs)) break;
+          if (!warp_wait(&rfull[rslot], (rcount / C::RES_G) & 1, abort_flag, kTimeoutNs)) break;
           res_row = reinterpret_cast<const float*>(sRes + rslot * C::RES_SLOT) + (wq * 32 + lane) * 32;
         }
         if (rows_live) {
@@ -752,8 +755,8 @@ void forced_tiles(int* bn, int* ks, int* pair, int* bk) {
 // cost model fitted to measured B200 layer times at batches 32 and 256 (microseconds,
 // ~1.9 GHz; geometric error ~13%).  A launch costs a fixed 14 (launch ramp, pipeline fill,
 // the last tile's exposed epilogue) plus 2 per extra wave of work units.  A unit costs the
-// larger of its main loop and its epilogue (0.4 per 32 output columns, overlapped with the
-// next unit's main loop through the second TMEM accumulator).  Main-loop stages cost about
+// larger of its main loop and its epilogue (0.8 per 32 output columns and epilogue warp
+// group, overlapped with the next unit's main loop through the second TMEM accumulator).  Main-loop stages cost about
 // the same whatever their width -- they are bounded by the per-stage barrier handoff as much
 // as by tensor throughput -- so deep stages and CTA pairs (twice the rows per MMA) pay off.
 // A split adds the finish pass: (ksplit + 2) x M x N floats at 8 TB/s (the partials are
@@ -792,7 +795,9 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
       if (ws > ws_limit) break;
       const long units = tiles * ks;
       const long waves = (units + slots - 1) / slots;
-      double cost = 14.0 + (waves - 1) * 2.0 + waves * std::max(kb_per * sh.per_stage, 0.4 * bn / 32);
+      // epilogue: ~0.8 us per 32-column chunk and warp group; 256-wide residual tiles use one group
+      const double epi = 0.8 * (bn / 32) / ((has_res && bn == 256) ? 1 : 2);
+      double cost = 14.0 + (waves - 1) * 2.0 + waves * std::max(kb_per * sh.per_stage, epi);
       if (ks > 1) cost += (double)(ks + 2) * M * N * 4 / 8.0e6;
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
