@@ -67,12 +67,13 @@ __global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, float* __restri
 }
 
 // One thread per output pixel (b, i, j): 16 channels = 4 phases (dy, dx) x 4 input channels.
+template <typename Idx>
 __global__ void space_to_depth2_kernel(const float* __restrict__ x, float4* __restrict__ y, int n, int c, int h,
                                        int w, int h2, int w2, int ph, int pw, int round_tf32) {
-  const long total = (long)n * h2 * w2;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+  const Idx total = (Idx)n * h2 * w2;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
     const int j = (int)(i % w2);
-    long t = i / w2;
+    Idx t = i / w2;
     const int r = (int)(t % h2);
     const int b = (int)(t / h2);
 #pragma unroll
@@ -82,7 +83,7 @@ __global__ void space_to_depth2_kernel(const float* __restrict__ x, float4* __re
       float v[4];
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch)
-        v[ch] = (in && ch < c) ? x[(((size_t)b * c + ch) * h + iy) * w + ix] : 0.0f;
+        v[ch] = (in && ch < c) ? __ldg(x + (((size_t)b * c + ch) * h + iy) * w + ix) : 0.0f;
       if (round_tf32) {
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) v[ch] = to_tf32_rna(v[ch]);
@@ -93,24 +94,26 @@ __global__ void space_to_depth2_kernel(const float* __restrict__ x, float4* __re
 }
 
 // MaxPool (SPINN/run_time/ops/pool/maxpool.c:5-49): -1e30 start, padded taps skipped.
+template <typename Idx>
 __global__ void maxpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
                                     int c4, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw) {
-  const long total = (long)n * oh * ow * c4;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+  // Idx = int when the element count fits: 64-bit division would dominate this HBM-bound loop.
+  const Idx total = (Idx)n * oh * ow * c4;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
     const int cq = (int)(i % c4);
-    long t = i / c4;
+    Idx t = i / c4;
     const int ox = (int)(t % ow);
     t /= ow;
     const int oy = (int)(t % oh);
     const int b = (int)(t / oh);
-    float4 m = make_float4(-1e30f, -1e30f, -1e30f, -1e30f);
+    float4 m = make_float4(-1e30f, -1e30f, -1e30f, -1e30f);  // the reference's initial value (maxpool.c:32)
     for (int r = 0; r < kh; ++r) {
       const int iy = oy * sh - ph + r;
       if (iy < 0 || iy >= h) continue;
       for (int s = 0; s < kw; ++s) {
         const int ix = ox * sw - pw + s;
         if (ix < 0 || ix >= w) continue;
-        const float4 v = x[(((size_t)b * h + iy) * w + ix) * c4 + cq];
+        const float4 v = __ldg(x + (((size_t)b * h + iy) * w + ix) * c4 + cq);
         m.x = v.x > m.x ? v.x : m.x;
         m.y = v.y > m.y ? v.y : m.y;
         m.z = v.z > m.z ? v.z : m.z;
@@ -418,8 +421,13 @@ int launch_space_to_depth2(const float* x, float* y, int n, int c, int h, int w,
                            cudaStream_t s, int round_tf32) {
   SPINN_CHECK_ARG(c >= 1 && c <= 4, "space_to_depth2: %d channels (at most 4)", c);
   const long work = (long)n * h2 * w2;
-  space_to_depth2_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(x, reinterpret_cast<float4*>(y), n, c, h,
-                                                                             w, h2, w2, ph, pw, round_tf32);
+  const long span = (long)grid_for(work, kEltThreads) * kEltThreads;  // the loop index reaches work + span
+  if (work < (1l << 31) - span)
+    space_to_depth2_kernel<int><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        x, reinterpret_cast<float4*>(y), n, c, h, w, h2, w2, ph, pw, round_tf32);
+  else
+    space_to_depth2_kernel<long><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        x, reinterpret_cast<float4*>(y), n, c, h, w, h2, w2, ph, pw, round_tf32);
   SPINN_LAUNCH_CHECK();
 }
 
@@ -434,8 +442,14 @@ int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad,
                         int sh, int sw, int ph, int pw, cudaStream_t s) {
   SPINN_CHECK_ARG(cpad % 4 == 0, "maxpool: channel stride %d not a multiple of 4", cpad);
   const long work = (long)n * oh * ow * (cpad / 4);
-  maxpool_nhwc_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
-      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow, kh, kw, sh, sw, ph, pw);
+  if (work < (1l << 31) - (long)grid_for(work, kEltThreads) * kEltThreads)
+    maxpool_nhwc_kernel<int><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow, kh, kw, sh, sw, ph,
+        pw);
+  else
+    maxpool_nhwc_kernel<long><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow, kh, kw, sh, sw, ph,
+        pw);
   SPINN_LAUNCH_CHECK();
 }
 
