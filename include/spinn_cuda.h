@@ -163,6 +163,14 @@ void *spinn_cuda_io_ptr(SpinnCudaModel *m, int is_output, int index, size_t *byt
 int spinn_cuda_io_count(SpinnCudaModel *m, int is_output);
 int spinn_cuda_io_dims(SpinnCudaModel *m, int is_output, int index, uint32_t *dims);
 
+/* ENNF data type of graph input / output `index` (1 fp32, 7 int64 -- TopK indices keep 8
+ * bytes per element on the device), or < 0. */
+int spinn_cuda_io_dtype(SpinnCudaModel *m, int is_output, int index);
+
+/* Synchronous copy of graph output `index` (after a run) into host memory; `bytes` must be
+ * the output's size (spinn_cuda_io_ptr). */
+int spinn_cuda_copy_output(SpinnCudaModel *m, int index, void *host, size_t bytes);
+
 /* Planned sizes: device arena bytes and pre-transformed weight bytes. */
 int spinn_cuda_plan_info(SpinnCudaModel *m, uint64_t *arena_bytes, uint64_t *weight_bytes,
                          int *num_steps, int *num_kernels);

@@ -85,9 +85,9 @@ def _tensor(name: str, arr: np.ndarray) -> bytes:
     return msg
 
 
-def _value_info(name: str, shape) -> bytes:
+def _value_info(name: str, shape, elem_type: int = _FLOAT32) -> bytes:
     dims = b"".join(_f_bytes(1, _f_varint(1, d)) for d in shape)
-    tensor_type = _f_varint(1, _FLOAT32) + _f_bytes(2, dims)
+    tensor_type = _f_varint(1, elem_type) + _f_bytes(2, dims)
     return _f_str(1, name) + _f_bytes(2, _f_bytes(1, tensor_type))
 
 
@@ -105,8 +105,9 @@ def graph_to_onnx(g) -> bytes:
     gm = b"".join(_f_bytes(1, _node(n)) for n in g.nodes)
     gm += _f_str(2, g.name)
     gm += b"".join(_f_bytes(5, _tensor(k, v)) for k, v in g.initializers.items())
-    gm += b"".join(_f_bytes(11, _value_info(n, s)) for n, s in g.inputs)
-    gm += b"".join(_f_bytes(12, _value_info(n, s)) for n, s in g.outputs)
-    gm += b"".join(_f_bytes(13, _value_info(n, s)) for n, s in g.value_info.items())
+    et = getattr(g, "elem_types", {})
+    gm += b"".join(_f_bytes(11, _value_info(n, s, et.get(n, _FLOAT32))) for n, s in g.inputs)
+    gm += b"".join(_f_bytes(12, _value_info(n, s, et.get(n, _FLOAT32))) for n, s in g.outputs)
+    gm += b"".join(_f_bytes(13, _value_info(n, s, et.get(n, _FLOAT32))) for n, s in g.value_info.items())
     opset = _f_str(1, "") + _f_varint(2, g.opset)
     return _f_varint(1, 8) + _f_str(2, "spinn_b200.netdef") + _f_bytes(7, gm) + _f_bytes(8, opset)

@@ -336,6 +336,20 @@ class PortOracle:
         return y
 
     # ---------------------------------------------------------------- model runner
+    @staticmethod
+    def topk(x: np.ndarray, k: int):
+        """TopK as SPINN/run_time/ops/tensor/topk.c:20-87: last axis, k clamped to its length,
+        values descending; equal values keep ascending index order (the reference's qsort is
+        glibc's merge sort, stable for its comparator, which treats -0.0 and +0.0 as equal)."""
+        x = np.asarray(x, np.float32)
+        n = x.shape[-1]
+        k = max(0, min(k, n))
+        rows = x.reshape(-1, n)
+        key = np.where(rows == 0, np.float32(0), rows)        # -0.0 and +0.0 tie
+        order = np.argsort(-key.astype(np.float64), axis=1, kind="stable")[:, :k]
+        v = np.take_along_axis(rows, order, axis=1)
+        return v.reshape(x.shape[:-1] + (k,)), order.astype(np.int64).reshape(x.shape[:-1] + (k,))
+
     def run_model(self, image: bytes, x: np.ndarray) -> Dict[int, np.ndarray]:
         """Runs an ENNF image node by node over the port operators."""
         m = ennf.read(image)
@@ -398,6 +412,10 @@ class PortOracle:
                 self.L.oracle_relu(_fp(a), _fp(y), a.size)
             elif op == "MatMul":
                 y = self.matmul(get(nd.inputs[0]), get(nd.inputs[1])).reshape(out_dims)
+            elif op == "TopK":
+                v, ix = self.topk(get(nd.inputs[0]), int(np.asarray(get(nd.inputs[1])).reshape(-1)[0]))
+                vals[nd.outputs[1]] = ix.reshape(m.tensors[nd.outputs[1]].dims)
+                y = v
             else:
                 raise NotImplementedError(f"port oracle: operator {op} ({nd.op_type})")
             vals[nd.outputs[0]] = y.reshape(out_dims)

@@ -5,6 +5,8 @@
 //
 // Semantics follow the reference operators cited at each kernel; layouts are NHWC with the
 // channel dimension padded to `cpad` (a multiple of 4) where the tensor-core path needs it.
+#include <atomic>
+
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -121,6 +123,49 @@ __global__ void maxpool_nhwc_kernel(const float4* __restrict__ x, float4* __rest
       }
     }
     y[i] = m;
+  }
+}
+
+// TopK (SPINN/run_time/ops/tensor/topk.c:20-87): for every row of the last axis, the k largest
+// values in descending order and their int64 indices.  One CTA sorts a row in shared memory
+// (bitonic network over 64-bit keys: order-preserving bits of the value, inverted, above the
+// index), so equal values come out in ascending index order -- the order the reference's
+// qsort (glibc merge sort, a stable sort for its comparator) produces.  -0.0 and +0.0 share a
+// key, as they compare equal there; values are copied from the row itself.
+__global__ void __launch_bounds__(1024) topk_rows_kernel(const float* __restrict__ x, int n, int k, int npow2,
+                                                         float* __restrict__ vals, int64_t* __restrict__ idx) {
+  extern __shared__ unsigned long long keys[];
+  const float* row = x + (size_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < npow2; i += blockDim.x) {
+    unsigned long long key = ~0ull;  // padding sorts last
+    if (i < n) {
+      uint32_t u = __float_as_uint(row[i]);
+      if (u == 0x80000000u) u = 0;  // -0.0 == +0.0
+      const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // increases with the value
+      key = ((unsigned long long)(~ord) << 32) | (uint32_t)i;
+    }
+    keys[i] = key;
+  }
+  __syncthreads();
+  for (int size = 2; size <= npow2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int t = threadIdx.x; t < npow2 / 2; t += blockDim.x) {
+        const int lo = 2 * t - (t & (stride - 1));
+        const int hi = lo + stride;
+        const bool ascending = (lo & size) == 0;
+        const unsigned long long a = keys[lo], b = keys[hi];
+        if ((a > b) == ascending) {
+          keys[lo] = b;
+          keys[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const uint32_t j = (uint32_t)keys[i];
+    vals[(size_t)blockIdx.x * k + i] = row[j];
+    idx[(size_t)blockIdx.x * k + i] = (int64_t)j;
   }
 }
 
@@ -450,6 +495,26 @@ int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad,
     maxpool_nhwc_kernel<long><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
         reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow, kh, kw, sh, sw, ph,
         pw);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_topk(const float* x, long rows, int n, int k, float* vals, int64_t* idx, cudaStream_t s) {
+  SPINN_CHECK_ARG(n >= 1 && n <= kTopkMaxN, "topk: row length %d outside [1, %d]", n, kTopkMaxN);
+  SPINN_CHECK_ARG(k >= 0 && k <= n, "topk: k=%d outside [0, %d]", k, n);
+  SPINN_CHECK_ARG(rows >= 0 && rows <= 0x7FFFFFFF, "topk: %ld rows", rows);
+  if (rows == 0 || k == 0) return 0;
+  int npow2 = 1;
+  while (npow2 < n) npow2 <<= 1;
+  const size_t smem = (size_t)npow2 * 8;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  SPINN_CUDA_TRY(cudaGetDevice(&dev));
+  if (!(configured.load() & (1ull << (dev & 63)))) {
+    SPINN_CUDA_TRY(cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)((size_t)kTopkMaxN * 8)));
+    configured.fetch_or(1ull << (dev & 63));
+  }
+  topk_rows_kernel<<<(unsigned)rows, 1024, smem, s>>>(x, n, k, npow2, vals, idx);
   SPINN_LAUNCH_CHECK();
 }
 

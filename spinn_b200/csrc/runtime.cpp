@@ -34,8 +34,9 @@ enum : uint16_t {
   OP_ADD = 4, OP_DIV = 23, OP_MUL = 39, OP_SUB = 50, OP_CONV = 60, OP_AVGPOOL = 80, OP_GAP = 81, OP_MAXPOOL = 85,
   OP_BN = 100, OP_RELU = 130, OP_SIGMOID = 133, OP_GEMM = 160, OP_MATMUL = 161, OP_FLATTEN = 189,
   OP_IDENTITY = 193, OP_RESHAPE = 197, OP_SOFTMAX = 134, OP_CONCAT = 183, OP_RESIZE = 198, OP_SPLIT = 206,
-  OP_TRANSPOSE = 211
+  OP_TOPK = 210, OP_TRANSPOSE = 211
 };
+constexpr uint8_t kDtypeInt64 = 7;  // ENNF_TYPE_INT64 (SPINN/ennf_def.h)
 constexpr uint32_t kMagic = 0x454E4E46;
 
 #pragma pack(push, 1)
@@ -304,9 +305,12 @@ void set_nhwc(Buf& b, const TensorRec& t) {
   b.cpad = round4(b.c);
   b.bytes = (uint64_t)b.n * b.h * b.w * b.cpad * 4;
 }
+// Bytes per element on the device: int64 tensors (TopK indices) keep 8, everything else is fp32.
+uint64_t elem_bytes(const TensorRec& t) { return t.dtype == kDtypeInt64 ? 8 : 4; }
+
 void set_row(Buf& b, const TensorRec& t) {
   b.lay = LAY_ROW;
-  b.bytes = t.elems * 4;
+  b.bytes = t.elems * elem_bytes(t);
 }
 
 // Best-fit allocation over the step intervals (reference algorithm, 64-bit).
@@ -403,7 +407,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     const TensorRec& t = m->tensors[id];
     Buf st;
     st.lay = LAY_ROW;
-    st.bytes = t.elems * 4;
+    st.bytes = t.elems * elem_bytes(t);
     st.external = 1;
     const int sb = P.new_buf(st);
     m->in_buf.push_back(sb);
@@ -1199,6 +1203,57 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         produced[yb] = 1;
         break;
       }
+      case OP_TOPK: {
+        // TopK (SPINN/run_time/ops/tensor/topk.c): last axis, k largest, sorted descending,
+        // as the reference (which ignores the axis/largest/sorted attributes).
+        if (nd.in.size() < 2 || nd.out.size() < 2) {
+          set_error("plan: TopK node %d needs inputs X, K and outputs values, indices", ni);
+          return SPINN_CUDA_EFORMAT;
+        }
+        const TensorRec& X = m->tensors[nd.in[0]];
+        const TensorRec& Kt = m->tensors[nd.in[1]];
+        if (!Kt.is_weight || !Kt.host || Kt.elems < 1) {
+          set_error("plan: TopK node %d: K must be a constant", ni);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        int64_t kv = 0;
+        if (Kt.dtype == kDtypeInt64)
+          std::memcpy(&kv, Kt.host, 8);
+        else
+          kv = (int64_t)Kt.host[0];
+        const int n = X.ndim ? (int)X.dims[X.ndim - 1] : 1;
+        if (n < 1 || n > kTopkMaxN) {
+          set_error("plan: TopK node %d: last axis %d outside [1, %d]", ni, n, kTopkMaxN);
+          return SPINN_CUDA_EUNSUPPORTED;
+        }
+        const int k = (int)std::max<int64_t>(0, std::min<int64_t>(kv, n));
+        const long rows = (long)(X.elems / n);
+        const TensorRec& V = m->tensors[nd.out[0]];
+        const TensorRec& I = m->tensors[nd.out[1]];
+        if (V.elems != (uint64_t)rows * k || I.elems != (uint64_t)rows * k || I.dtype != kDtypeInt64) {
+          set_error("plan: TopK node %d: outputs must be [rows, %d] float and int64", ni, k);
+          return SPINN_CUDA_EFORMAT;
+        }
+        const int xb = ensure_row(nd.in[0], ni);
+        const int vb = nd.out[0], ib = nd.out[1];
+        set_row(m->bufs[vb], V);
+        set_row(m->bufs[ib], I);
+        const int s = add_step(ni, nd.op, 6, 0, [=](StepRec& r) {
+          const Buf* x = &m->bufs[xb];
+          const Buf* v = &m->bufs[vb];
+          const Buf* ix = &m->bufs[ib];
+          r.run = [=](cudaStream_t st) {
+            return launch_topk(x->ptr, rows, n, k, v->ptr, reinterpret_cast<int64_t*>(ix->ptr), st);
+          };
+          return 0;
+        });
+        P.touch(xb, s);
+        P.touch(vb, s);
+        P.touch(ib, s);
+        produced[vb] = 1;
+        produced[ib] = 1;
+        break;
+      }
       case OP_SOFTMAX: {
         const TensorRec& X = m->tensors[nd.in[0]];
         int axis = -1;
@@ -1366,7 +1421,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     const TensorRec& t = m->tensors[id];
     Buf st;
     st.lay = LAY_ROW;
-    st.bytes = t.elems * 4;
+    st.bytes = t.elems * elem_bytes(t);
     st.external = 1;
     const int sb = P.new_buf(st);
     m->out_buf.push_back(sb);
@@ -1620,6 +1675,35 @@ __attribute__((visibility("default"))) int spinn_cuda_io_dims(SpinnCudaModel* m,
   const TensorRec& t = m->tensors[v[index]];
   if (dims) std::memcpy(dims, t.dims, sizeof(t.dims));
   return t.ndim;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_io_dtype(SpinnCudaModel* m, int is_output, int index) {
+  if (!m) return SPINN_CUDA_EINVAL;
+  const auto& v = is_output ? m->outputs : m->inputs;
+  if (index < 0 || index >= (int)v.size()) return SPINN_CUDA_EINVAL;
+  return m->tensors[v[index]].dtype == kDtypeInt64 ? kDtypeInt64 : 1;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_copy_output(SpinnCudaModel* m, int index, void* host,
+                                                                  size_t bytes) {
+  if (!m || !m->planned || !host) {
+    set_error("spinn_cuda_copy_output: model not planned or no host buffer");
+    return SPINN_CUDA_ESTATE;
+  }
+  if (index < 0 || index >= (int)m->out_buf.size()) {
+    set_error("spinn_cuda_copy_output: output %d of %d", index, (int)m->out_buf.size());
+    return SPINN_CUDA_EINVAL;
+  }
+  const Buf& b = m->bufs[m->out_buf[index]];
+  if (bytes != b.bytes) {
+    set_error("spinn_cuda_copy_output: output %d has %llu bytes, not %zu", index, (unsigned long long)b.bytes,
+              bytes);
+    return SPINN_CUDA_EINVAL;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(m->device));
+  SPINN_CUDA_TRY(cudaMemcpyAsync(host, b.ptr, bytes, cudaMemcpyDeviceToHost, m->stream));
+  SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return 0;
 }
 
 __attribute__((visibility("default"))) int spinn_cuda_plan_info(SpinnCudaModel* m, uint64_t* arena_bytes,

@@ -38,7 +38,7 @@ OP = {
     "Relu": 130, "Sigmoid": 133, "Softmax": 134,
     "Gemm": 160, "MatMul": 161,
     "Concat": 183, "Flatten": 189, "Identity": 193, "Reshape": 197, "Resize": 198,
-    "Split": 206, "Transpose": 211,
+    "Split": 206, "TopK": 210, "Transpose": 211,
 }
 OP_NAME = {v: k for k, v in OP.items()}
 
@@ -377,6 +377,12 @@ def _params(node, op_code: int, fused_act: int, pbuf: bytearray) -> bytes:
     if op_code == OP["Split"]:
         struct.pack_into("<i", pbuf, 0, int(a.get("axis", 0)))
         return bytes(pbuf[:8])
+    if op_code == OP["TopK"]:
+        # ENNF_TopKParams {i32 axis; u8 largest, sorted, reserved[2]} (ennf_op_params.h:218-224):
+        # the extractor (onnx2ennf_ops.c:331-337) leaves `reserved` as the scratch held it
+        struct.pack_into("<iBB", pbuf, 0, int(a.get("axis", -1)), int(a.get("largest", 1)) & 0xFF,
+                         int(a.get("sorted", 1)) & 0xFF)
+        return bytes(pbuf[:8])
     out = _params_fixed(node, op_code, fused_act)
     pbuf[:len(out)] = out
     return out
@@ -479,7 +485,8 @@ def convert(graph, disable_add: bool = False, disable_silu: bool = False) -> byt
             dims, w, dt = arr.shape, 1, (7 if arr.dtype == np.int64 else 1)
         else:
             dims, w = shapes.get(name, ()), 0
-            dt = 1 if name in shapes else 0      # map_dtype(0) = UNDEFINED without value_info
+            # map_dtype of the value_info elem_type; UNDEFINED (0) without value_info
+            dt = getattr(g, "elem_types", {}).get(name, 1) if name in shapes else 0
         dims = tuple(int(d) for d in dims)[:8]
         elem = int(np.prod(dims)) if dims else 1
         meta_blob += struct.pack(META_FMT, k, dt, len(dims), *(list(dims) + [0] * (8 - len(dims))),

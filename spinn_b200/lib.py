@@ -71,6 +71,8 @@ _SIGS = {
     "spinn_cuda_io_ptr": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                            ctypes.POINTER(ctypes.c_size_t)]),
     "spinn_cuda_io_count": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "spinn_cuda_io_dtype": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
+    "spinn_cuda_copy_output": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t]),
     "spinn_cuda_io_dims": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_uint32)]),
     "spinn_cuda_plan_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64),

@@ -46,6 +46,8 @@ class Graph:
     outputs: List[Tuple[str, Shape]] = field(default_factory=list)
     value_info: Dict[str, Shape] = field(default_factory=dict)
     opset: int = 13
+    # ONNX element type of non-initializer tensors that are not float32 (7 = int64)
+    elem_types: Dict[str, int] = field(default_factory=dict)
 
     # ------------------------------------------------------------------ helpers
     def shape(self, name: str) -> Shape:
@@ -67,9 +69,11 @@ class Graph:
         return name
 
     def add_node(self, op: str, inputs: Sequence[str], outputs: Sequence[str],
-                 out_shapes: Sequence[Shape], **attrs) -> List[str]:
-        for o, s in zip(outputs, out_shapes):
+                 out_shapes: Sequence[Shape], out_types: Optional[Sequence[int]] = None, **attrs) -> List[str]:
+        for i, (o, s) in enumerate(zip(outputs, out_shapes)):
             self.value_info[o] = tuple(int(d) for d in s)
+            if out_types is not None and out_types[i] != 1:
+                self.elem_types[o] = int(out_types[i])
         self.nodes.append(Node(op, list(inputs), list(outputs), dict(attrs),
                                name=f"{op}_{len(self.nodes)}"))
         return list(outputs)
@@ -83,7 +87,8 @@ class Graph:
         g = Graph(self.name, [Node(n.op_type, list(n.inputs), list(n.outputs), dict(n.attrs), n.name)
                               for n in self.nodes],
                   {k: v.copy() for k, v in self.initializers.items()},
-                  list(self.inputs), list(self.outputs), dict(self.value_info), self.opset)
+                  list(self.inputs), list(self.outputs), dict(self.value_info), self.opset,
+                  dict(self.elem_types))
         return g
 
     def flops(self) -> int:
@@ -232,6 +237,15 @@ class _Builder:
 
     def softmax(self, x: str) -> str:
         return self.g.add_node("Softmax", [x], [self._id("softmax")], [self.g.shape(x)], axis=-1)[0]
+
+    def topk(self, x: str, k: int, axis: int = -1):
+        """ONNX TopK (largest, sorted) over the last axis: returns (values, int64 indices)."""
+        s = self.g.shape(x)
+        kk = self.g.add_init(self._id("k"), np.array([k], np.int64))
+        out = tuple(s[:-1]) + (min(k, s[-1]),)
+        v, i = self.g.add_node("TopK", [x, kk], [self._id("topk_v"), self._id("topk_i")], [out, out],
+                               out_types=[1, 7], axis=axis, largest=1, sorted=1)
+        return v, i
 
     def scale(self, x: str, v: float) -> str:
         c = self.g.add_init(self._id("scale"), np.array([v], np.float32))

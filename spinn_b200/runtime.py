@@ -159,6 +159,14 @@ class Model:
             raise _L.SpinnCudaError(_L.ESTATE, "spinn_cuda_io_ptr", "no such buffer")
         return p, n.value
 
+    def output(self, index: int) -> np.ndarray:
+        """Graph output `index` of the last run, copied to host (fp32 or int64)."""
+        dt = np.int64 if check(lib().spinn_cuda_io_dtype(self._h, 1, index), "spinn_cuda_io_dtype") == 7 \
+            else np.float32
+        out = np.empty(self.io_dims(True, index), dt)
+        check(lib().spinn_cuda_copy_output(self._h, index, out.ctypes.data, out.nbytes), "spinn_cuda_copy_output")
+        return out
+
     def run(self, x: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
         """Host input -> host output 0 (``spinn_run``)."""
         x = np.ascontiguousarray(x, dtype=np.float32)

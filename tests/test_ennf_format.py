@@ -26,7 +26,20 @@ def _graphs():
         # Split (stale num_outputs bytes), Concat, Resize, Reshape (int64 shape), Transpose,
         # MatMul, Softmax, scalar Mul, depthwise convolutions
         "yolo_shaped_128px": netdef.yolo_shaped(batch=1, image=128),
+        # TopK after a Gemm: ENNF_TopKParams.reserved keeps the Gemm's beta bytes (stale scratch)
+        "gemm_topk": _gemm_topk(),
     }
+
+
+def _gemm_topk():
+    from spinn_b200 import netdef
+    g = netdef.Graph("gemm_topk")
+    b = netdef._Builder(g, np.random.default_rng(0))
+    x = g.add_input("x", (3, 64))
+    v, i = b.topk(b.gemm(x, 500), 40)
+    g.mark_output(v)
+    g.mark_output(i)
+    return g
 
 
 @pytest.mark.parametrize("name", list(_graphs()))

@@ -73,3 +73,29 @@ def test_row_concat_and_sigmoid(cuda_lib, ref_oracle, tmp_path):
     g.mark_output(y)
     out, ref = _run_both(ref_oracle, tmp_path, g, xv)
     assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
+
+
+@pytest.mark.parametrize("shape,k", [((2, 1000), 50), ((2, 8400), 300), ((4, 37), 100), ((3, 16384), 5)])
+def test_topk_matches_reference(cuda_lib, ref_oracle, tmp_path, shape, k):
+    """Device TopK against the reference op_topk: values and int64 indices identical,
+    including ties and signed zeros."""
+    from spinn_b200 import ennf, netdef, runtime
+    g = netdef.Graph("topk")
+    b = netdef._Builder(g, np.random.default_rng(0))
+    x = g.add_input("x", shape)
+    v, i = b.topk(x, k)
+    g.mark_output(v)
+    g.mark_output(i)
+    rng = np.random.default_rng(sum(shape) + k)
+    xv = rng.normal(0, 1, shape).astype(np.float32)
+    xv[:, ::7] = np.round(xv[:, ::7], 1)       # ties
+    xv[:, ::11] = np.float32(-0.0)
+    img = ennf.convert(g)
+    p = tmp_path / "topk.ennf"
+    p.write_bytes(img)
+    m = ennf.read(img)
+    ref = ref_oracle.run_model(str(p), xv)
+    model = runtime.Model(img)
+    model.run(xv)
+    assert np.array_equal(model.output(0).ravel(), ref[m.outputs[0]])
+    assert np.array_equal(model.output(1).ravel(), ref[m.outputs[1]].view(np.int64))

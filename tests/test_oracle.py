@@ -151,3 +151,33 @@ def test_winograd_f43_matches_direct(port_oracle):
         direct = port_oracle.conv2d(x, w, b, None, (1, 1), (1, 1), (1, 1), 1, 1)
         wino = port_oracle.winograd_f43(x, w, b, act=1)
         assert rel_l2(wino, direct) < 1e-5
+
+
+def _topk_graph(shape, k):
+    from spinn_b200 import netdef
+    g = netdef.Graph("topk")
+    b = netdef._Builder(g, np.random.default_rng(0))
+    x = g.add_input("x", shape)
+    v, i = b.topk(x, k)
+    g.mark_output(v)
+    g.mark_output(i)
+    return g
+
+
+@pytest.mark.parametrize("shape,k", [((2, 1000), 50), ((1, 8400), 300), ((4, 37), 100)])
+def test_topk_reference_matches_port_with_ties(ref_oracle, port_oracle, tmp_path, shape, k):
+    """op_topk (topk.c) on inputs with many equal values and signed zeros: values descending,
+    ties in ascending index order (glibc qsort is a stable merge sort), k clamped to the axis."""
+    from spinn_b200 import ennf
+    rng = np.random.default_rng(sum(shape) + k)
+    x = (rng.integers(-6, 7, shape) * 0.25).astype(np.float32)
+    x[x == 0] = np.where(rng.random(int((x == 0).sum())) < 0.5, np.float32(-0.0), np.float32(0.0))
+    img = ennf.convert(_topk_graph(shape, k))
+    path = tmp_path / "topk.ennf"
+    path.write_bytes(img)
+    m = ennf.read(img)
+    vid, iid = m.outputs
+    ref = ref_oracle.run_model(str(path), x)
+    port = port_oracle.run_model(img, x)
+    assert np.array_equal(ref[vid], port[vid])
+    assert np.array_equal(ref[iid].view(np.int64), port[iid])
