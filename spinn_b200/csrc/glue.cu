@@ -169,6 +169,27 @@ __global__ void __launch_bounds__(1024) topk_rows_kernel(const float* __restrict
   }
 }
 
+// Row-strided copy for Concat/Split (SPINN/run_time/ops/tensor/concat.c, split.c): row r of
+// dst gets src's first `width` values and zeros up to `fill_to`.  V = 4: float4 accesses
+// (pointers, pitches and both widths multiples of 4 floats).
+template <int V, typename Idx>
+__global__ void copy_rows_kernel(const float* __restrict__ src, int src_ld, float* __restrict__ dst, int dst_ld,
+                                 Idx rows, int width, int fill_to) {
+  const int q = fill_to / V;
+  const Idx total = rows * q;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
+    const Idx r = i / q;
+    const int c = (int)(i - r * q) * V;
+    if constexpr (V == 4) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < width) v = __ldg(reinterpret_cast<const float4*>(src + (size_t)r * src_ld + c));
+      *reinterpret_cast<float4*>(dst + (size_t)r * dst_ld + c) = v;
+    } else {
+      dst[(size_t)r * dst_ld + c] = c < width ? __ldg(src + (size_t)r * src_ld + c) : 0.0f;
+    }
+  }
+}
+
 // AveragePool (SPINN/run_time/ops/pool/avgpool.c): divisor = window taps inside the image,
 // or the full window when count_include_pad.
 __global__ void avgpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
@@ -515,6 +536,27 @@ int launch_topk(const float* x, long rows, int n, int k, float* vals, int64_t* i
     configured.fetch_or(1ull << (dev & 63));
   }
   topk_rows_kernel<<<(unsigned)rows, 1024, smem, s>>>(x, n, k, npow2, vals, idx);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_copy_rows(const float* src, int src_ld, float* dst, int dst_ld, long rows, int width, int fill_to,
+                     cudaStream_t s) {
+  SPINN_CHECK_ARG(width >= 0 && fill_to >= width && src_ld >= width && dst_ld >= fill_to && rows >= 0,
+                  "copy_rows: width %d fill %d src_ld %d dst_ld %d", width, fill_to, src_ld, dst_ld);
+  if (rows == 0 || fill_to == 0) return 0;
+  const bool v4 = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 &&
+                  src_ld % 4 == 0 && dst_ld % 4 == 0 && width % 4 == 0 && fill_to % 4 == 0;
+  const long work = rows * (v4 ? fill_to / 4 : fill_to);
+  const int grid = grid_for(work, kEltThreads);
+  const bool small = work < (1l << 31) - (long)grid * kEltThreads;
+  if (v4 && small)
+    copy_rows_kernel<4, int><<<grid, kEltThreads, 0, s>>>(src, src_ld, dst, dst_ld, (int)rows, width, fill_to);
+  else if (v4)
+    copy_rows_kernel<4, long><<<grid, kEltThreads, 0, s>>>(src, src_ld, dst, dst_ld, rows, width, fill_to);
+  else if (small)
+    copy_rows_kernel<1, int><<<grid, kEltThreads, 0, s>>>(src, src_ld, dst, dst_ld, (int)rows, width, fill_to);
+  else
+    copy_rows_kernel<1, long><<<grid, kEltThreads, 0, s>>>(src, src_ld, dst, dst_ld, rows, width, fill_to);
   SPINN_LAUNCH_CHECK();
 }
 

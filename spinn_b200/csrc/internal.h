@@ -165,6 +165,9 @@ int launch_transpose(const float* x, float* y, int batch, int rows, int cols, cu
 // A_hi B_hi + A_lo B_hi + A_hi B_lo.  Only the first `cols` entries of each segment are written.
 int launch_split_tf32(const float* src, float* dst, long rows, int cols, int src_ld, int seg, int dst_ld, int o0,
                       int o1, int o2, cudaStream_t s);
+// dst[r][0..fill_to) = src[r][0..width) followed by zeros, for r < rows (pitches in floats).
+int launch_copy_rows(const float* src, int src_ld, float* dst, int dst_ld, long rows, int width, int fill_to,
+                     cudaStream_t s);
 // TopK over the last axis of a row-major [rows][n] tensor (n <= kTopkMaxN): k largest values
 // (descending, ties by ascending index) and their int64 indices, each [rows][k].
 constexpr int kTopkMaxN = 16384;

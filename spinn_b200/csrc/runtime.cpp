@@ -1118,35 +1118,24 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           for (int b : pb) pp.push_back(&m->bufs[b]);
           const Buf* w = &m->bufs[wb];
           r.run = [=](cudaStream_t st) -> int {
-            size_t off = 0;
+            // one row-strided copy kernel per part; NHWC pad lanes of every destination are
+            // written as zeros by the copy that owns them
+            int off = 0;
+            const long rows = nhwc ? (long)w->n * w->h * w->w : outer;
+            const int wld = nhwc ? w->cpad : (int)(w->bytes / 4 / outer);
             for (size_t i = 0; i < pp.size(); ++i) {
               const Buf* p = pp[i];
-              size_t rows, width, wpitch, ppitch;
-              if (nhwc) {
-                rows = (size_t)w->n * w->h * w->w;
-                width = (size_t)sizes[i] * 4;
-                wpitch = (size_t)w->cpad * 4;
-                ppitch = (size_t)p->cpad * 4;
-              } else {
-                rows = outer;
-                width = (size_t)sizes[i] * inner * 4;
-                wpitch = (size_t)(w->bytes / 4 / outer) * 4;
-                ppitch = width;
-              }
-              char* wp = reinterpret_cast<char*>(w->ptr) + off;
+              const int width = nhwc ? sizes[i] : (int)(sizes[i] * inner);
+              const int pld = nhwc ? p->cpad : width;
+              int rc;
               if (is_cat) {
-                SPINN_CUDA_TRY(cudaMemcpy2DAsync(wp, wpitch, p->ptr, ppitch, width, rows, cudaMemcpyDeviceToDevice, st));
+                const int fill = (nhwc && i + 1 == pp.size()) ? wld - off : width;
+                rc = launch_copy_rows(p->ptr, pld, w->ptr + off, wld, rows, width, fill, st);
               } else {
-                if (nhwc && p->cpad != sizes[i])
-                  SPINN_CUDA_TRY(cudaMemsetAsync(p->ptr, 0, p->bytes, st));
-                SPINN_CUDA_TRY(cudaMemcpy2DAsync(p->ptr, ppitch, wp, wpitch, width, rows, cudaMemcpyDeviceToDevice, st));
+                rc = launch_copy_rows(w->ptr + off, wld, p->ptr, pld, rows, width, pld, st);
               }
+              if (rc) return rc;
               off += width;
-            }
-            if (is_cat && nhwc && off / 4 != (size_t)w->cpad) {  // zero the channel padding
-              const size_t rows = (size_t)w->n * w->h * w->w;
-              SPINN_CUDA_TRY(cudaMemset2DAsync(reinterpret_cast<char*>(w->ptr) + off, (size_t)w->cpad * 4, 0,
-                                               (size_t)w->cpad * 4 - off, rows, st));
             }
             return 0;
           };
