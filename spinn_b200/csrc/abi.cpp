@@ -634,7 +634,8 @@ __attribute__((visibility("default"))) int spinn_cuda_matmul(SpinnTensor** in, i
   const int Kp = round4(K), Np = round4(N), kpad = tc_num_kb(K) * 32;
   const size_t ab = (size_t)batch * M * K * 4, bb = (size_t)batch_b * K * N * 4, yb = (size_t)batch * M * N * 4;
   rc = scratch_reserve(pad256(ab) + pad256((size_t)batch * M * Kp * 4) + 2 * pad256(bb) +
-                       pad256((size_t)batch_b * Np * kpad * 4) + pad256(yb) + 2 * pad256((size_t)M * Np * 4) + 8192);
+                       pad256((size_t)batch_b * Np * kpad * 4) + pad256(yb) + 2 * pad256((size_t)batch * M * Np * 4) +
+                       8192);
   if (rc) return rc;
   cudaStream_t st = g_sess.stream;
   const float* a;
@@ -660,11 +661,30 @@ __attribute__((visibility("default"))) int spinn_cuda_matmul(SpinnTensor** in, i
   if (rc) return rc;
   const bool dev_out = is_device_ptr(out[0]->data);
   float* y = dev_out ? static_cast<float*>(out[0]->data) : scratch_take(yb);
-  const size_t mark = g_sess.scratch_used;
-  for (long i = 0; i < batch; ++i) {
-    g_sess.scratch_used = mark;  // per-batch temporaries are reused
-    rc = gemm_core(a_use + (size_t)i * M * Kp, Kp, bp + (size_t)(batch_b == 1 ? 0 : i) * Np * kpad, kpad, M, N, K, 1.0f,
-                   nullptr, nullptr, y + (size_t)i * M * N, st);
+  if (batch == 1) {
+    rc = gemm_core(a_use, Kp, bp, kpad, M, N, K, 1.0f, nullptr, nullptr, y, st);
+    if (rc) return rc;
+    return finish_output(out[0], y, yb);
+  }
+  // every batch in one launch: A, B and Y planes back to back
+  float* yt = Np == N ? y : scratch_take((size_t)batch * M * Np * 4);
+  TcGemmArgs g;
+  g.a_mode = 1;
+  g.x = a_use;
+  g.M = M;
+  g.K = K;
+  g.lda = Kp;
+  g.wt = bp;
+  g.kpad = kpad;
+  g.N = Np;
+  g.y = yt;
+  g.ldy = Np;
+  g.batch = (int)batch;
+  g.b_batched = batch_b > 1;
+  rc = tc_gemm_launch(g, st);
+  if (rc) return rc;
+  if (yt != y) {
+    rc = launch_copy_rows(yt, Np, y, N, batch * M, N, N, st);
     if (rc) return rc;
   }
   return finish_output(out[0], y, yb);

@@ -80,6 +80,10 @@ struct TcGemmArgs {
   int act = 0;
   int round_out = 0;
   int bn = 0;  // 0 = choose
+  // Batched GEMM (tiled A only): `batch` problems whose A, Y (and W when b_batched) planes are
+  // stored back to back ([batch][M][lda], [batch][M][ldy], [batch][N][kpad]); one launch.
+  int batch = 1;
+  int b_batched = 0;
   int* err = nullptr;  // device error word; nullptr = the per-device flag
   // Split-K workspace (optional).  With one, problems that leave SMs idle are split along K
   // into raw fp32 partials (ksplit x M x N floats) reduced in a fixed order by a finish kernel

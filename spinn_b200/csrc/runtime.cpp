@@ -1322,7 +1322,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         set_row(m->bufs[yb], Y);
         int yt = -1;
         if (Np != N) {
-          t.bytes = (uint64_t)M * Np * 4;
+          t.bytes = (uint64_t)batch * M * Np * 4;
           yt = P.new_buf(t);
         }
         const int s = add_step(ni, nd.op, 2, 2.0 * batch * M * N * K, [=](StepRec& r) {
@@ -1341,6 +1341,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           q.kpad = kpad;
           q.N = Np;
           q.ldy = Np;
+          q.batch = (int)batch;
+          q.b_batched = batch_b > 1;
           note_ws(m, q);
           r.run = [=](cudaStream_t st) -> int {
             if (seg != K) SPINN_CUDA_TRY(cudaMemsetAsync(ap->ptr, 0, ap->bytes, st));
@@ -1351,33 +1353,37 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
               rc = launch_transpose(b->ptr, bt->ptr, (int)batch_b, K, N, st);  // -> [batch_b][N][K]
               if (rc) return rc;
               SPINN_CUDA_TRY(cudaMemsetAsync(bp->ptr, 0, bp->bytes, st));
-              for (long bi = 0; bi < batch_b; ++bi) {
-                rc = launch_split_tf32(bt->ptr + (size_t)bi * N * K, bp->ptr + (size_t)bi * Np * kpad, N, K, K, seg,
-                                       kpad, 0, 0, 1, st);
+              if (Np == N) {  // the planes are contiguous rows: one packing pass
+                rc = launch_split_tf32(bt->ptr, bp->ptr, batch_b * N, K, K, seg, kpad, 0, 0, 1, st);
                 if (rc) return rc;
+              } else {
+                for (long bi = 0; bi < batch_b; ++bi) {
+                  rc = launch_split_tf32(bt->ptr + (size_t)bi * N * K, bp->ptr + (size_t)bi * Np * kpad, N, K, K, seg,
+                                         kpad, 0, 0, 1, st);
+                  if (rc) return rc;
+                }
               }
               wbase = bp->ptr;
             }
-            for (long i = 0; i < batch; ++i) {
-              TcGemmArgs g;
-              g.a_mode = 1;
-              g.x = ap->ptr + (size_t)i * M * 3 * seg;
-              g.M = M;
-              g.K = 3 * seg;
-              g.lda = 3 * seg;
-              g.wt = wbase + (size_t)(batch_b == 1 ? 0 : i) * Np * kpad;
-              g.kpad = kpad;
-              g.N = Np;
-              g.y = ytp ? ytp->ptr : y->ptr + (size_t)i * M * N;
-              g.ldy = Np;
-              g.ws = m->splitk_ws;
-              g.ws_bytes = m->splitk_bytes;
-              rc = tc_gemm_launch(g, st);
-              if (rc) return rc;
-              if (ytp)
-                SPINN_CUDA_TRY(cudaMemcpy2DAsync(y->ptr + (size_t)i * M * N, (size_t)N * 4, ytp->ptr, (size_t)Np * 4,
-                                                 (size_t)N * 4, M, cudaMemcpyDeviceToDevice, st));
-            }
+            // every batch in one launch: A', Y (and B') planes back to back
+            TcGemmArgs g;
+            g.a_mode = 1;
+            g.x = ap->ptr;
+            g.M = M;
+            g.K = 3 * seg;
+            g.lda = 3 * seg;
+            g.wt = wbase;
+            g.kpad = kpad;
+            g.N = Np;
+            g.y = ytp ? ytp->ptr : y->ptr;
+            g.ldy = Np;
+            g.batch = (int)batch;
+            g.b_batched = batch_b > 1;
+            g.ws = m->splitk_ws;
+            g.ws_bytes = m->splitk_bytes;
+            rc = tc_gemm_launch(g, st);
+            if (rc) return rc;
+            if (ytp) return launch_copy_rows(ytp->ptr, Np, y->ptr, N, batch * M, N, N, st);
             return 0;
           };
           return 0;

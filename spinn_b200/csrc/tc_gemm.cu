@@ -54,7 +54,8 @@ struct TcParams {
   int cpad, taps, kw, dil_h, dil_w;
   int ohw, ow, stride_h, stride_w, pad_h, pad_w;
   int tiles_n, num_tiles;
-  int ksplit, kb_per, num_units;  // work unit u: tile u % num_tiles, K slice u / num_tiles
+  int ksplit, kb_per, num_units;  // work unit u: tile u % num_tiles, z = u / num_tiles
+  int batch, b_batched;           // batched GEMM: z is the batch index (then ksplit == 1)
   int nstages;                    // ring stages in use (<= the variant's STAGES)
   int has_res, act, round_out;
   float alpha;
@@ -221,7 +222,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     uint32_t ph = 0;
     uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
     for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step) {
-      const int ks = u / p.num_tiles, tile = u - ks * p.num_tiles;
+      const int z = u / p.num_tiles, tile = u - z * p.num_tiles;
+      const int ks = p.batch > 1 ? 0 : z, bz = p.batch > 1 ? z : 0;
+      const int bzb = p.b_batched ? bz : 0;  // batch plane of W
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       int m0 = tm * TM + (int)rank * kBM;
       if (m0 >= p.M) m0 = tm * TM;  // a pair's second half past the end: load valid rows, store none
@@ -274,14 +277,14 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
               }
             } else {
               if constexpr (PAIR == 2)
-                tma_load_2d_pair(&mapA, bar_leader, a_dst + j * C::A_SUB, k, m0);
+                tma_load_3d_pair(&mapA, bar_leader, a_dst + j * C::A_SUB, k, m0, bz);
               else
-                tma_load_2d(&mapA, &full[s], a_dst + j * C::A_SUB, k, m0);
+                tma_load_3d(&mapA, &full[s], a_dst + j * C::A_SUB, k, m0, bz);
             }
             if constexpr (PAIR == 2)
-              tma_load_2d_pair(&mapB, bar_leader, b_dst + j * C::B_SUB, k, nb0);
+              tma_load_3d_pair(&mapB, bar_leader, b_dst + j * C::B_SUB, k, nb0, bzb);
             else
-              tma_load_2d(&mapB, &full[s], b_dst + j * C::B_SUB, k, nb0);
+              tma_load_3d(&mapB, &full[s], b_dst + j * C::B_SUB, k, nb0, bzb);
           }
           if (rank == 0) {
             armed |= 1u << s;
@@ -316,7 +319,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step, ++it) {
         const int b = it & 1;
         const uint32_t aph = (it >> 1) & 1;
-        const int kb0 = (u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
+        const int kb0 = (p.batch > 1 ? 0 : u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
         if (!warp_wait(&tempty[b], aph ^ 1, abort_flag, kTimeoutNs)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + b * BN;
@@ -421,7 +424,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     const bool partial = p.ksplit > 1;
     const bool unit_alpha = p.alpha == 1.0f;
     for (int u = unit0; u < p.num_units; u += unit_step, ++it) {
-      const int ks = u / p.num_tiles, tile = u - ks * p.num_tiles;
+      const int z = u / p.num_tiles, tile = u - z * p.num_tiles;  // z: K slice or batch -> output plane
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
       const int b = it & 1;
@@ -506,7 +509,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&mapY, st_out, col0, row0, ks);
+            tma_store_3d(&mapY, st_out, col0, row0, z);
             tma_store_commit();
           }
           ++nstore;
@@ -827,7 +830,7 @@ int problem_cb(const TcGemmArgs& a) { return a.a_mode == 0 ? channel_block(a.cpa
 }  // namespace
 
 size_t tc_gemm_workspace_bytes(const TcGemmArgs& a) {
-  if (!tc_gemm_supported(a, nullptr)) return 0;
+  if (!tc_gemm_supported(a, nullptr) || a.batch > 1) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   return plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), kWsCap, a.bn).ws_bytes;
@@ -839,6 +842,8 @@ bool tc_gemm_supported(const TcGemmArgs& a, std::string* why) {
     return false;
   };
   if (a.N <= 0 || a.M <= 0) return fail("empty problem");
+  if (a.batch < 1) return fail("batch must be at least 1");
+  if (a.batch > 1 && (a.a_mode != 1 || a.res)) return fail("batched GEMM needs a row-major A and no residual");
   if (a.ldy % 4 != 0 || a.ldy < a.N) return fail("output row stride must be a multiple of 4 floats");
   if ((reinterpret_cast<uintptr_t>(a.y) & 15) || (reinterpret_cast<uintptr_t>(a.wt) & 15) ||
       (reinterpret_cast<uintptr_t>(a.x) & 15))
@@ -898,7 +903,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     p.cpad = a.K;
     p.taps = 1;
     p.kw = 1;
-    rc = encode_tiled_2d(&ma, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.lda * 4, 32, kBM,
+    rc = encode_tiled_3d(&ma, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.batch, (uint64_t)a.lda * 4, 32, kBM,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
@@ -907,19 +912,19 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     set_error("tcgen05 gemm: weights padded to %d, need %d", a.kpad, tc_num_kb(K) * 32);
     return SPINN_CUDA_EINVAL;
   }
-  const TilePlan tp =
-      plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, a.ws ? std::min(a.ws_bytes, kWsCap) : 0, a.bn);
+  const size_t ws_limit = (a.ws && a.batch == 1) ? std::min(a.ws_bytes, kWsCap) : 0;  // batched: no split
+  const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn);
   p.num_kb = (K + tp.bk - 1) / tp.bk;  // stages beyond kpad read zero weights
   const int bn = tp.bn;
   const bool split = tp.ksplit > 1;
-  rc = encode_tiled_2d(&mb, a.wt, (uint64_t)a.kpad, (uint64_t)a.N, (uint64_t)a.kpad * 4, (uint32_t)cb,
-                       (uint32_t)(bn / tp.pair), swizzle_for(cb));
+  rc = encode_tiled_3d(&mb, a.wt, (uint64_t)a.kpad, (uint64_t)a.N, (uint64_t)(a.b_batched ? a.batch : 1),
+                       (uint64_t)a.kpad * 4, (uint32_t)cb, (uint32_t)(bn / tp.pair), swizzle_for(cb));
   if (rc) return rc;
   const int ldw = (a.N + 3) & ~3;
   rc = split ? encode_tiled_3d(&my, a.ws, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)tp.ksplit, (uint64_t)ldw * 4, 32, 32,
                                CU_TENSOR_MAP_SWIZZLE_128B)
-             : encode_tiled_3d(&my, a.y, (uint64_t)a.N, (uint64_t)a.M, 1, (uint64_t)a.ldy * 4, 32, 32,
-                               CU_TENSOR_MAP_SWIZZLE_128B);
+             : encode_tiled_3d(&my, a.y, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.batch, (uint64_t)a.ldy * 4, 32,
+                               32, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (a.res && !split) {
     rc = encode_tiled_2d(&mr, a.res, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.ldr * 4, 32, kBM,
@@ -937,11 +942,14 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   p.num_tiles = (int)tiles;
   p.ksplit = tp.ksplit;
   p.kb_per = split ? tp.kb_per : p.num_kb;
-  if (tiles * tp.ksplit > 0x7FFFFFFF) {
+  p.batch = a.batch;
+  p.b_batched = a.b_batched;
+  const long zs = a.batch > 1 ? a.batch : tp.ksplit;
+  if (tiles * zs > 0x7FFFFFFF) {
     set_error("tcgen05 gemm: too many work units");
     return SPINN_CUDA_EINVAL;
   }
-  p.num_units = (int)(tiles * tp.ksplit);
+  p.num_units = (int)(tiles * zs);
   p.has_res = a.res != nullptr && !split;
   p.act = a.act;
   p.round_out = a.round_out;

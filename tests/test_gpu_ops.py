@@ -188,3 +188,19 @@ def test_gemm_cta_pair_tiles(cuda_lib, port_oracle, monkeypatch, case, tiles):
     runtime.gemm(a, b, y, c, runtime.gemm_params(alpha, beta, ta, tb))
     ref = port_oracle.gemm(a, b, c, m, n, k, ta, tb, alpha, beta)
     assert rel_l2(y, ref) <= TOL, rel_l2(y, ref)
+
+
+@pytest.mark.parametrize("tiles", [None, "256,1,2", "128,1,1"])
+def test_matmul_batched_one_launch(cuda_lib, port_oracle, monkeypatch, tiles):
+    """Batched MatMul runs as one launch over [batch][M][K] planes (3-D tensor maps, the batch
+    index in the work unit), with single CTAs and CTA pairs, shared and per-batch B."""
+    from spinn_b200 import runtime
+    if tiles:
+        monkeypatch.setenv("SPINN_TC_TILES", tiles)
+    rng = np.random.default_rng(13)
+    for sa, sb in (((6, 300, 64), (6, 64, 200)), ((5, 129, 36), (36, 70))):
+        a = rng.uniform(-1, 1, sa).astype(np.float32)
+        b = rng.uniform(-1, 1, sb).astype(np.float32)
+        y = np.zeros(np.broadcast_shapes(a.shape[:-2], b.shape[:-2]) + (a.shape[-2], b.shape[-1]), np.float32)
+        runtime.matmul(a, b, y)
+        assert rel_l2(y, port_oracle.matmul(a, b)) <= TOL
