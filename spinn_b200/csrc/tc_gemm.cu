@@ -18,8 +18,8 @@
 //               swizzled shared staging -> TMA store; warps w and w+4 share the 32
 //               accumulator lanes of quarter w % 4 and take alternate 32-column chunks
 // Tiles are 128 output pixels x BN output channels, scheduled n-fastest so that CTAs running
-// together share the activation tile in L2.  Two TMEM accumulators let the epilogue of one
-// tile overlap the main loop of the next.
+// together share the activation tile in L2.  The TMEM accumulators (2 at BN=256, 4 at 128, 8
+// at 64 -- all 512 columns) let the epilogue of one tile overlap the main loop of the next ones.
 //
 // Problems with fewer tiles than SMs (small batches, the last stages of a ResNet, the FC
 // layer) are split along K when the caller supplies a workspace: each (tile, K slice) unit
@@ -96,8 +96,11 @@ struct Cfg {
   static constexpr uint32_t EPI = OUT_BYTES + RES_SLOTS * RES_SLOT;
   static constexpr int STAGES_FIT = (kSmemBudget - (int)EPI) / (int)STAGE;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;  // BN in {64,128,256} -> 128/256/512, powers of two
-  static constexpr uint32_t SMEM = STAGES * STAGE + EPI + 256 + 1024;
+  // TMEM accumulators: all 512 columns, so narrow tiles (BN 128 / 64) get 4 / 8 buffers and
+  // the MMA can run that many tiles ahead of the epilogue
+  static constexpr int NACC = 512 / BN;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t SMEM = STAGES * STAGE + EPI + 512 + 1024;
   static_assert(STAGES >= 2, "pipeline needs two stages");
   static_assert(PAIR == 1 || BNC >= 64, "pair tiles split BN into halves of at least 64 rows");
 };
@@ -163,8 +166,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sRes + C::RES_SLOTS * C::RES_SLOT);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* rfull = tempty + 2;
+  uint64_t* tempty = tfull + C::NACC;
+  uint64_t* rfull = tempty + C::NACC;
   uint64_t* rempty = rfull + NRS;
   uint64_t* drain = rempty + NRS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -179,7 +182,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::NACC; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], C::EPI_WARPS * PAIR);
     }
@@ -317,8 +320,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       int it = 0;
       bool issued = false;
       for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step, ++it) {
-        const int b = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
+        const int b = it % C::NACC;
+        const uint32_t aph = (it / C::NACC) & 1;
         const int kb0 = (p.batch > 1 ? 0 : u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
         if (!warp_wait(&tempty[b], aph ^ 1, abort_flag, kTimeoutNs)) break;
         tc_fence_after();
@@ -385,12 +388,13 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       if (lane == 0) {
         int count[2] = {0, 0};  // chunks loaded so far for each epilogue group
         uint32_t armed = 0, armed_ph = 0;
-        for (int tile = unit0; tile < p.num_tiles && !*abort_flag; tile += unit_step) {  // ksplit == 1
+        int it = 0;  // units so far: chunk c goes to epilogue group (c + it) % EPI_GROUPS
+        for (int tile = unit0; tile < p.num_tiles && !*abort_flag; tile += unit_step, ++it) {  // ksplit == 1
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
           const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
           bool ok = true;
           for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
-            const int g = c % C::EPI_GROUPS;
+            const int g = (c + it) % C::EPI_GROUPS;
             const int slot = g * C::RES_G + count[g] % C::RES_G;
             const uint32_t ph = (count[g] / C::RES_G) & 1;
             if (!mbar_wait(&rempty[slot], ph ^ 1, abort_flag, kTimeoutNs)) {
@@ -427,15 +431,18 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       const int z = u / p.num_tiles, tile = u - z * p.num_tiles;  // z: K slice or batch -> output plane
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
-      const int b = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
+      const int b = it % C::NACC;
+      const uint32_t aph = (it / C::NACC) & 1;
+      // Chunk c of this unit belongs to group (c + it) % EPI_GROUPS: rotating the ownership
+      // spreads units with a single live chunk (N <= 32) over both groups.
+      const int eo = (eg + C::EPI_GROUPS - it % C::EPI_GROUPS) % C::EPI_GROUPS;
       // This warp's bias values for the unit (lane l: column n0 + 32 c + l of each chunk c it
       // owns), fetched before the accumulator wait so the load latency is hidden behind it.
       constexpr int MYCH = BN / 32 / C::EPI_GROUPS;
       float bias_reg[MYCH];
 #pragma unroll
       for (int i = 0; i < MYCH; ++i) {
-        const int col = n0 + 32 * (i * C::EPI_GROUPS + eg) + lane;
+        const int col = n0 + 32 * (i * C::EPI_GROUPS + eo) + lane;
         bias_reg[i] = (!partial && p.bias && col < p.N) ? __ldg(p.bias + col) : 0.0f;
       }
       if (!warp_wait_backoff(&tfull[b], aph, abort_flag, kTimeoutNs)) break;
@@ -445,7 +452,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = n0 + c * 32;
         if (col0 >= p.N) break;
-        if (c % C::EPI_GROUPS != eg) continue;
+        if (c % C::EPI_GROUPS != eo) continue;
         const float* res_row = nullptr;
         const int rslot = C::RES_G > 0 ? eg * C::RES_G + rcount % C::RES_G : 0;
         if constexpr (RES) {
