@@ -671,6 +671,12 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             a.ldr = ocpad;
             a.act = act;
             a.round_out = rnd;
+            if (KHc == 1 && KWc == 1 && SHc == 1 && SWc == 1 && PHc == 0 && PWc == 0 && OH == Hc && OW == Wc) {
+              // a pointwise conv over NHWC rows is a plain GEMM: tiled TMA boxes for A
+              a.a_mode = 1;
+              a.K = Cc;
+              a.lda = Cc;
+            }
             const Buf* xbp = &m->bufs[xb];
             const Buf* ybp = &m->bufs[yb];
             const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
