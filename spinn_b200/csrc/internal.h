@@ -84,6 +84,9 @@ struct TcGemmArgs {
   // stored back to back ([batch][M][lda], [batch][M][ldy], [batch][N][kpad]); one launch.
   int batch = 1;
   int b_batched = 0;
+  // Visit the tiles from the last one: a planner alternates the direction between consecutive
+  // layers so that each starts on the rows its producer wrote last, which are still in L2.
+  int reverse = 0;
   int* err = nullptr;  // device error word; nullptr = the per-device flag
   // Split-K workspace (optional).  With one, problems that leave SMs idle are split along K
   // into raw fp32 partials (ksplit x M x N floats) reduced in a fixed order by a finish kernel

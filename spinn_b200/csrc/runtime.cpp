@@ -139,6 +139,7 @@ struct SpinnCudaModel {
   uint64_t arena_bytes = 0;
   float* wdev = nullptr;
   uint64_t wbytes = 0;
+  int tc_layers = 0;               // tensor-core conv steps planned so far (tile walk direction)
   float* splitk_ws = nullptr;      // split-K partial sums, shared by all steps (one stream)
   size_t splitk_bytes = 0;
   std::vector<float> whost;        // pre-transformed weights before upload
@@ -671,6 +672,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             a.ldr = ocpad;
             a.act = act;
             a.round_out = rnd;
+            a.reverse = (m->tc_layers++) & 1;
             if (KHc == 1 && KWc == 1 && SHc == 1 && SWc == 1 && PHc == 0 && PWc == 0 && OH == Hc && OW == Wc) {
               // a pointwise conv over NHWC rows is a plain GEMM: tiled TMA boxes for A
               a.a_mode = 1;

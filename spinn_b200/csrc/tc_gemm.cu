@@ -56,6 +56,7 @@ struct TcParams {
   int tiles_n, num_tiles;
   int ksplit, kb_per, num_units;  // work unit u: tile u % num_tiles, z = u / num_tiles
   int batch, b_batched;           // batched GEMM: z is the batch index (then ksplit == 1)
+  int reverse;                    // walk the tiles from the last one (alternates between layers)
   int nstages;                    // ring stages in use (<= the variant's STAGES)
   int has_res, act, round_out;
   float alpha;
@@ -225,7 +226,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     uint32_t ph = 0;
     uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
     for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step) {
-      const int z = u / p.num_tiles, tile = u - z * p.num_tiles;
+      const int z = u / p.num_tiles, t = u - z * p.num_tiles;
+      const int tile = p.reverse ? p.num_tiles - 1 - t : t;
       const int ks = p.batch > 1 ? 0 : z, bz = p.batch > 1 ? z : 0;
       const int bzb = p.b_batched ? bz : 0;  // batch plane of W
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
@@ -389,7 +391,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
         int count[2] = {0, 0};  // chunks loaded so far for each epilogue group
         uint32_t armed = 0, armed_ph = 0;
         int it = 0;  // units so far: chunk c goes to epilogue group (c + it) % EPI_GROUPS
-        for (int tile = unit0; tile < p.num_tiles && !*abort_flag; tile += unit_step, ++it) {  // ksplit == 1
+        for (int t = unit0; t < p.num_tiles && !*abort_flag; t += unit_step, ++it) {  // ksplit == 1
+          const int tile = p.reverse ? p.num_tiles - 1 - t : t;
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
           const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
           bool ok = true;
@@ -428,7 +431,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     const bool partial = p.ksplit > 1;
     const bool unit_alpha = p.alpha == 1.0f;
     for (int u = unit0; u < p.num_units; u += unit_step, ++it) {
-      const int z = u / p.num_tiles, tile = u - z * p.num_tiles;  // z: K slice or batch -> output plane
+      const int z = u / p.num_tiles, t = u - z * p.num_tiles;  // z: K slice or batch -> output plane
+      const int tile = p.reverse ? p.num_tiles - 1 - t : t;
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
       const int b = it % C::NACC;
@@ -951,6 +955,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   p.kb_per = split ? tp.kb_per : p.num_kb;
   p.batch = a.batch;
   p.b_batched = a.b_batched;
+  p.reverse = a.reverse;
   const long zs = a.batch > 1 ? a.batch : tp.ksplit;
   if (tiles * zs > 0x7FFFFFFF) {
     set_error("tcgen05 gemm: too many work units");
