@@ -58,6 +58,8 @@ struct TcParams {
   int batch, b_batched;           // batched GEMM: z is the batch index (then ksplit == 1)
   int reverse;                    // walk the tiles from the last one (alternates between layers)
   int nstages;                    // ring stages in use (<= the variant's STAGES)
+  int pf_a;                       // tiled A: L2 prefetch this many k-blocks ahead (0: off)
+  int pf_res;                     // residual: L2 prefetch of the next tile's rows (0: off)
   int has_res, act, round_out;
   float alpha;
   const float* bias;
@@ -68,15 +70,23 @@ struct TcParams {
 // K (each handoff costs a few hundred cycles of single-thread latency); CTA pairs use 64 (one
 // handoff feeds 1024 MMA cycles per SM), 256-wide single-CTA tiles keep 32 so that four
 // stages fit beside the W tile.
-template <int BN, int CB, bool RES, int PAIR, int BK_>
+//
+// MS: M sub-tiles per CTA.  MS = 2 gives one CTA a 256 x BN unit computed as two 128-row MMA
+// streams that share each W stage; A arrives in 256-row boxes.  A TMA box costs the same few
+// hundred cycles of issue whether it holds 128 or 256 rows (measured on B200), so for narrow
+// tiles (BN 64 / 128), whose main loop is bounded by box issue rather than by the tensor
+// pipe, this doubles the bytes per box and halves the W boxes per output.
+template <int BN, int CB, bool RES, int PAIR, int BK_, int MS_ = 1>
 struct Cfg {
   static constexpr int BK = BK_;
+  static constexpr int MS = MS_;
+  static constexpr int AROWS = kBM * MS;  // A rows held by each CTA
   static constexpr int BNC = BN / PAIR;  // B rows (output channels) held by each CTA
   static constexpr int NSUB = BK / CB;   // TMA boxes per operand per stage
-  static constexpr int KSTEPS = BK / 8;  // MMAs per stage
-  static constexpr uint32_t A_SUB = kBM * CB * 4;
+  static constexpr int KSTEPS = BK / 8;  // MMAs per stage (per M sub-tile)
+  static constexpr uint32_t A_SUB = AROWS * CB * 4;
   static constexpr uint32_t B_SUB = BNC * CB * 4;
-  static constexpr uint32_t A_STAGE = kBM * BK * 4;
+  static constexpr uint32_t A_STAGE = AROWS * BK * 4;
   static constexpr uint32_t B_STAGE = BNC * BK * 4;
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
   // Epilogue: groups of four warps (one per TMEM lane quarter); with two groups, group g
@@ -85,6 +95,7 @@ struct Cfg {
   // shared by two groups would let one group wait on a slot two phases ahead of the other's,
   // which the parity test cannot tell apart.  256-wide residual tiles keep a single group
   // with a 3-slot ring: two 2-slot rings would leave too few stages beside a 256-wide W tile.
+  // With MS = 2, group g drains M sub-tile g (all of its chunks).
   static constexpr int EPI_GROUPS = (RES && BN == 256) ? 1 : 2;
   static constexpr int EPI_WARPS = 4 * EPI_GROUPS;
   static constexpr int THREADS = 128 + 32 * EPI_WARPS;
@@ -99,11 +110,12 @@ struct Cfg {
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   // TMEM accumulators: all 512 columns, so narrow tiles (BN 128 / 64) get 4 / 8 buffers and
   // the MMA can run that many tiles ahead of the epilogue
-  static constexpr int NACC = 512 / BN;
+  static constexpr int NACC = 512 / (BN * MS);
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t SMEM = STAGES * STAGE + EPI + 512 + 1024;
   static_assert(STAGES >= 2, "pipeline needs two stages");
   static_assert(PAIR == 1 || BNC >= 64, "pair tiles split BN into halves of at least 64 rows");
+  static_assert(MS == 1 || (PAIR == 1 && !RES && CB >= 16 && BN <= 128), "two M sub-tiles: narrow plain tiles only");
 };
 
 // Start-address offset (bytes) of the j-th 8-wide K slice of a stage, and the descriptor
@@ -148,16 +160,17 @@ __device__ __forceinline__ bool warp_wait_backoff(uint64_t* bar, uint32_t parity
 //
 // The producer and MMA warps run their loops with all 32 lanes (lane 0 issues): a single
 // diverged lane spends about half again as long per barrier handoff.
-template <int BN, int CB, int MODE, bool RES, int PAIR, int BK_>
-__global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
+template <int BN, int CB, int MODE, bool RES, int PAIR, int BK_, int MS_>
+__global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapY, const __grid_constant__ CUtensorMap mapR,
                    const TcParams p) {
-  using C = Cfg<BN, CB, RES, PAIR, BK_>;
+  using C = Cfg<BN, CB, RES, PAIR, BK_, MS_>;
   constexpr int STAGES = C::STAGES;
   constexpr int BK = C::BK;
+  constexpr int MS = C::MS;
   constexpr int NRS = C::RES_SLOTS > 0 ? C::RES_SLOTS : 1;
-  constexpr int TM = kBM * PAIR;  // rows of one work unit
+  constexpr int TM = kBM * PAIR * MS;  // rows of one work unit
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -225,6 +238,34 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
     int s = 0;
     uint32_t ph = 0;
     uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
+    // Tiled A only: the memory-bound pointwise layers stream A from HBM, and the ring holds
+    // only a few k-blocks. L2 prefetches pf_a k-blocks ahead (into the next unit near the end
+    // of a unit) keep more of A in flight than shared memory can.
+    struct UnitA {
+      int m0, bz, kb0, kb1;
+    };
+    auto unit_a = [&](int u) {
+      UnitA r;
+      const int z = u / p.num_tiles, t = u - z * p.num_tiles;
+      const int tile = p.reverse ? p.num_tiles - 1 - t : t;
+      const int ks = p.batch > 1 ? 0 : z;
+      r.bz = p.batch > 1 ? z : 0;
+      const int tm = tile / p.tiles_n;
+      r.m0 = tm * TM + (int)rank * kBM;
+      if (r.m0 >= p.M) r.m0 = tm * TM;
+      r.kb0 = ks * p.kb_per;
+      r.kb1 = min(p.num_kb, r.kb0 + p.kb_per);
+      return r;
+    };
+    auto prefetch_a = [&](const UnitA& ua, int kb) {
+#pragma unroll
+      for (int j = 0; j < C::NSUB; ++j) tma_prefetch_3d(&mapA, kb * BK + j * CB, ua.m0, ua.bz);
+    };
+    const bool pf_a = MODE != kIm2col && p.pf_a > 0;
+    if (pf_a && lane == 0 && unit0 < p.num_units) {
+      const UnitA ua = unit_a(unit0);
+      for (int kb = ua.kb0 + p.nstages; kb < min(ua.kb1, ua.kb0 + p.pf_a); ++kb) prefetch_a(ua, kb);
+    }
     for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step) {
       const int z = u / p.num_tiles, t = u - z * p.num_tiles;
       const int tile = p.reverse ? p.num_tiles - 1 - t : t;
@@ -250,9 +291,20 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
         r = tap / p.kw;
         q = tap - r * p.kw;
       }
+      UnitA next{0, 0, 0, 0};
+      if (pf_a && u + unit_step < p.num_units) next = unit_a(u + unit_step);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!warp_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs)) break;
         if (lane == 0) {
+          if (pf_a) {
+            const int kp = kb + p.pf_a;
+            if (kp < kb1) {
+              prefetch_a(UnitA{m0, bz, kb0, kb1}, kp);
+            } else {
+              const int kn = next.kb0 + (kp - kb1);
+              if (kn < next.kb1) prefetch_a(next, kn);
+            }
+          }
           if (rank == 0) mbar_arrive_expect_tx(&full[s], C::STAGE * PAIR);
           uint8_t* a_dst = sA + s * C::A_STAGE;
           uint8_t* b_dst = sB + s * C::B_STAGE;
@@ -314,7 +366,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (pair leader)
     if (rank == 0) {
-      constexpr uint32_t idesc = make_idesc_tf32(TM, BN);
+      constexpr uint32_t idesc = make_idesc_tf32(kBM * PAIR, BN);
       const uint64_t adesc0 = stage_desc0<CB>(smem_u32(sA), C::A_SUB);
       const uint64_t bdesc0 = stage_desc0<CB>(smem_u32(sB), C::B_SUB);
       int s = 0;
@@ -327,7 +379,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
         const int kb0 = (p.batch > 1 ? 0 : u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
         if (!warp_wait(&tempty[b], aph ^ 1, abort_flag, kTimeoutNs)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + b * BN;
+        const uint32_t d = tmem_base + b * (BN * MS);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!warp_wait(&full[s], ph, abort_flag, kTimeoutNs)) {
@@ -342,10 +394,13 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
               const uint64_t ad = as + (kslice_offset<CB>(j, C::A_SUB) >> 4);
               const uint64_t bd = bs + (kslice_offset<CB>(j, C::B_SUB) >> 4);
               const uint32_t acc = (kb != kb0 || j != 0) ? 1u : 0u;
-              if constexpr (PAIR == 2)
+              if constexpr (PAIR == 2) {
                 umma_tf32_pair(d, ad, bd, idesc, acc);
-              else
-                umma_tf32(d, ad, bd, idesc, acc);
+              } else {
+#pragma unroll
+                for (int ms = 0; ms < MS; ++ms)  // sub-tile ms: A rows 128 ms.., accumulator columns BN ms..
+                  umma_tf32(d + ms * BN, ad + ((uint64_t)(ms * kBM * CB * 4) >> 4), bd, idesc, acc);
+              }
             }
             if constexpr (PAIR == 2) {
               umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
@@ -391,10 +446,21 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
         int count[2] = {0, 0};  // chunks loaded so far for each epilogue group
         uint32_t armed = 0, armed_ph = 0;
         int it = 0;  // units so far: chunk c goes to epilogue group (c + it) % EPI_GROUPS
+        // L2 prefetch of a tile's residual rows, issued one tile ahead: the ring holds only a
+        // few chunks, too few to cover HBM latency at full bandwidth on its own.
+        auto prefetch_res = [&](int t) {
+          if (!p.pf_res || t >= p.num_tiles) return;
+          const int tile = p.reverse ? p.num_tiles - 1 - t : t;
+          const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+          const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
+          for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) tma_prefetch_2d(&mapR, n0 + c * 32, m0);
+        };
+        prefetch_res(unit0);
         for (int t = unit0; t < p.num_tiles && !*abort_flag; t += unit_step, ++it) {  // ksplit == 1
           const int tile = p.reverse ? p.num_tiles - 1 - t : t;
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
           const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
+          prefetch_res(t + unit_step);
           bool ok = true;
           for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
             const int g = (c + it) % C::EPI_GROUPS;
@@ -442,21 +508,23 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
       const int eo = (eg + C::EPI_GROUPS - it % C::EPI_GROUPS) % C::EPI_GROUPS;
       // This warp's bias values for the unit (lane l: column n0 + 32 c + l of each chunk c it
       // owns), fetched before the accumulator wait so the load latency is hidden behind it.
-      constexpr int MYCH = BN / 32 / C::EPI_GROUPS;
+      // With two M sub-tiles a group owns every chunk of its sub-tile.
+      constexpr int MYCH = MS == 2 ? BN / 32 : BN / 32 / C::EPI_GROUPS;
       float bias_reg[MYCH];
 #pragma unroll
       for (int i = 0; i < MYCH; ++i) {
-        const int col = n0 + 32 * (i * C::EPI_GROUPS + eo) + lane;
+        const int col = n0 + 32 * (MS == 2 ? i : i * C::EPI_GROUPS + eo) + lane;
         bias_reg[i] = (!partial && p.bias && col < p.N) ? __ldg(p.bias + col) : 0.0f;
       }
       if (!warp_wait_backoff(&tfull[b], aph, abort_flag, kTimeoutNs)) break;
       tc_fence_after();
-      const int row0 = m0 + wq * 32;
+      const int row0 = m0 + (MS == 2 ? eg * kBM : 0) + wq * 32;
       const bool rows_live = row0 < p.M;
+      const uint32_t acc_col = b * (BN * MS) + (MS == 2 ? eg * BN : 0);
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = n0 + c * 32;
         if (col0 >= p.N) break;
-        if (c % C::EPI_GROUPS != eo) continue;
+        if (MS == 1 && c % C::EPI_GROUPS != eo) continue;
         const float* res_row = nullptr;
         const int rslot = C::RES_G > 0 ? eg * C::RES_G + rcount % C::RES_G : 0;
         if constexpr (RES) {
@@ -465,7 +533,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
         }
         if (rows_live) {
           uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + b * BN + c * 32 + ((uint32_t)(wq * 32) << 16), r);
+          tmem_ld_32x32b_x32(tmem_base + acc_col + c * 32 + ((uint32_t)(wq * 32) << 16), r);
           tmem_ld_wait();
           float v[32];
 #pragma unroll
@@ -480,7 +548,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_>::THREADS, 1)
               float bias_lane = bias_reg[0];
 #pragma unroll
               for (int i = 1; i < MYCH; ++i)
-                if (c / C::EPI_GROUPS == i) bias_lane = bias_reg[i];
+                if ((MS == 2 ? c : c / C::EPI_GROUPS) == i) bias_lane = bias_reg[i];
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] += __shfl_sync(0xffffffffu, bias_lane, i);
             }
@@ -636,11 +704,11 @@ int pair_clusters(K kern, uint32_t smem, int threads, int sms) {
   return n;
 }
 
-template <int BN, int CB, int MODE, bool RES, int PAIR, int BK>
+template <int BN, int CB, int MODE, bool RES, int PAIR, int BK, int MS = 1>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr,
                    const TcParams& p, int sms, cudaStream_t stream) {
-  using C = Cfg<BN, CB, RES, PAIR, BK>;
-  auto kern = tc_gemm_kernel<BN, CB, MODE, RES, PAIR, BK>;
+  using C = Cfg<BN, CB, RES, PAIR, BK, MS>;
+  auto kern = tc_gemm_kernel<BN, CB, MODE, RES, PAIR, BK, MS>;
   // The opt-in shared-memory size is a per-device function attribute: set it once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -652,6 +720,15 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   }
   TcParams q = p;
   q.nstages = C::STAGES;
+  q.pf_a = 0;
+  q.pf_res = 1;
+  if (const char* e = getenv("SPINN_TC_PF")) {  // tuning: "a,res" prefetch distances
+    int a = 0, r = 1;
+    if (sscanf(e, "%d,%d", &a, &r) >= 1) {
+      q.pf_a = a < 0 ? 0 : a;
+      q.pf_res = r;
+    }
+  }
   if (const char* e = getenv("SPINN_TC_STAGES")) {  // tuning: use fewer ring stages
     const int v = atoi(e);
     if (v >= 2 && v < C::STAGES) q.nstages = v;
@@ -696,15 +773,19 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
 }
 
 template <int MODE, bool RES>
-int dispatch_bn_cb(int bn, int cb, int pair, int bk, const CUtensorMap& ma, const CUtensorMap& mb,
+int dispatch_bn_cb(int bn, int cb, int pair, int bk, int ms, const CUtensorMap& ma, const CUtensorMap& mb,
                    const CUtensorMap& my, const CUtensorMap& mr, const TcParams& p, int sms, cudaStream_t s) {
-#define SPINN_TC_CASE(BNV, CBV, PV, BKV)                      \
-  if (bn == BNV && cb == CBV && pair == PV && bk == BKV) \
+#define SPINN_TC_CASE(BNV, CBV, PV, BKV)                                  \
+  if (bn == BNV && cb == CBV && pair == PV && bk == BKV && ms == 1) \
     return launch_variant<BNV, CBV, MODE, RES, PV, BKV>(ma, mb, my, mr, p, sms, s);
+#define SPINN_TC_CASE2(BNV, CBV, BKV)                                    \
+  if (bn == BNV && cb == CBV && pair == 1 && bk == BKV && ms == 2) \
+    return launch_variant<BNV, CBV, MODE, RES, 1, BKV, 2>(ma, mb, my, mr, p, sms, s);
   SPINN_TC_CASE(256, 32, 1, 32) SPINN_TC_CASE(128, 32, 1, 32) SPINN_TC_CASE(64, 32, 1, 32)
   if constexpr (!RES) {
     SPINN_TC_CASE(128, 32, 1, 64) SPINN_TC_CASE(64, 32, 1, 64)
     SPINN_TC_CASE(256, 32, 2, 64) SPINN_TC_CASE(128, 32, 2, 64)
+    SPINN_TC_CASE2(128, 32, 32) SPINN_TC_CASE2(64, 32, 32) SPINN_TC_CASE2(128, 32, 64) SPINN_TC_CASE2(64, 32, 64)
   }
   if constexpr (MODE == kIm2col) {
     SPINN_TC_CASE(256, 16, 1, 32) SPINN_TC_CASE(128, 16, 1, 32) SPINN_TC_CASE(64, 16, 1, 32)
@@ -713,10 +794,12 @@ int dispatch_bn_cb(int bn, int cb, int pair, int bk, const CUtensorMap& ma, cons
     if constexpr (!RES) {
       SPINN_TC_CASE(128, 16, 1, 64) SPINN_TC_CASE(64, 16, 1, 64)
       SPINN_TC_CASE(256, 16, 2, 64) SPINN_TC_CASE(128, 16, 2, 64)
+      SPINN_TC_CASE2(128, 16, 32) SPINN_TC_CASE2(64, 16, 32) SPINN_TC_CASE2(128, 16, 64) SPINN_TC_CASE2(64, 16, 64)
     }
   }
 #undef SPINN_TC_CASE
-  set_error("tcgen05 gemm: no variant for BN=%d CB=%d pair=%d BK=%d mode=%d", bn, cb, pair, bk, MODE);
+#undef SPINN_TC_CASE2
+  set_error("tcgen05 gemm: no variant for BN=%d CB=%d pair=%d BK=%d MS=%d mode=%d", bn, cb, pair, bk, ms, MODE);
   return SPINN_CUDA_EUNSUPPORTED;
 }
 
@@ -748,21 +831,23 @@ constexpr size_t kWsCap = size_t(64) << 20;
 struct TilePlan {
   int bn = 256;
   int pair = 1;  // 2: CTA pairs with 256-row tiles (cta_group::2)
+  int ms = 1;    // 2: one CTA, 256-row tiles as two 128-row sub-tiles
   int bk = 32;   // K depth of a pipeline stage
   int ksplit = 1;
   int kb_per = 1;
   size_t ws_bytes = 0;
 };
 
-// Optional override for tuning sweeps: SPINN_TC_TILES="bn,ksplit[,pair[,bk]]" (read at each
-// launch; a captured graph keeps the choice made when it was captured).
-void forced_tiles(int* bn, int* ks, int* pair, int* bk) {
+// Optional override for tuning sweeps: SPINN_TC_TILES="bn,ksplit[,pair[,bk[,ms]]]" (read at
+// each launch; a captured graph keeps the choice made when it was captured).
+void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms) {
   *bn = -1;
   *ks = 0;
   *pair = 0;
   *bk = 0;
+  *ms = 0;
   const char* e = getenv("SPINN_TC_TILES");
-  if (e && sscanf(e, "%d,%d,%d,%d", bn, ks, pair, bk) < 1) *bn = -1;
+  if (e && sscanf(e, "%d,%d,%d,%d,%d", bn, ks, pair, bk, ms) < 1) *bn = -1;
 }
 
 // Chooses the tile shape (BN, single CTA or CTA pair, stage depth) and the K split from a
@@ -770,22 +855,25 @@ void forced_tiles(int* bn, int* ks, int* pair, int* bk) {
 // ~1.9 GHz; geometric error ~13%).  A launch costs a fixed 14 (launch ramp, pipeline fill,
 // the last tile's exposed epilogue) plus 2 per extra wave of work units.  A unit costs the
 // larger of its main loop and its epilogue (0.8 per 32 output columns and epilogue warp
-// group, overlapped with the next unit's main loop through the second TMEM accumulator).  Main-loop stages cost about
-// the same whatever their width -- they are bounded by the per-stage barrier handoff as much
-// as by tensor throughput -- so deep stages and CTA pairs (twice the rows per MMA) pay off.
-// A split adds the finish pass: (ksplit + 2) x M x N floats at 8 TB/s (the partials are
-// L2-resident).  64-deep stages need channel blocks of 16 or 32 and no fused residual
-// (the residual ring would leave too few of them).
+// group, overlapped with the next unit's main loop through the other TMEM accumulators).
+// Main-loop stages cost about the same whatever their width -- they are bounded by the
+// per-stage barrier handoff and the per-box TMA issue cost as much as by tensor throughput --
+// so deep stages, CTA pairs (twice the rows per MMA) and two M sub-tiles per CTA (256-row A
+// boxes, one W box per two MMAs) pay off.  A split adds the finish pass: (ksplit + 2) x M x N
+// floats at 8 TB/s (the partials are L2-resident).  64-deep stages and sub-tiles need channel
+// blocks of 16 or 32 and no fused residual (the residual ring would leave too few stages).
 TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t ws_limit, int force_bn) {
-  int fbn, fks, fpair, fbk;
-  forced_tiles(&fbn, &fks, &fpair, &fbk);
+  int fbn, fks, fpair, fbk, fms;
+  forced_tiles(&fbn, &fks, &fpair, &fbk, &fms);
   if (force_bn <= 0 && (fbn == 64 || fbn == 128 || fbn == 256)) force_bn = fbn;
   struct Shape {
-    int bn, pair, bk;
+    int bn, pair, bk, ms;
     double per_stage;
   };
-  const Shape shapes[7] = {{256, 1, 32, 0.332}, {128, 1, 32, 0.266}, {64, 1, 32, 0.237}, {128, 1, 64, 0.405},
-                           {64, 1, 64, 0.319},  {256, 2, 64, 0.617}, {128, 2, 64, 0.456}};
+  const Shape shapes[11] = {{256, 1, 32, 1, 0.332}, {128, 1, 32, 1, 0.266}, {64, 1, 32, 1, 0.237},
+                            {128, 1, 64, 1, 0.405}, {64, 1, 64, 1, 0.319},  {256, 2, 64, 1, 0.617},
+                            {128, 2, 64, 1, 0.456}, {128, 1, 32, 2, 0.46},  {64, 1, 32, 2, 0.38},
+                            {128, 1, 64, 2, 0.86},  {64, 1, 64, 2, 0.67}};
   const size_t ldw = (size_t)((N + 3) & ~3);
   TilePlan best;
   double best_cost = 1e300;
@@ -794,11 +882,14 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
     if (force_bn > 0 && bn != force_bn) continue;
     if (fpair > 0 && sh.pair != fpair) continue;
     if (fbk > 0 && sh.bk != fbk) continue;
+    if (fms > 0 && sh.ms != fms) continue;
     if (sh.bk == 64 && ((cb != 32 && cb != 16) || has_res)) continue;
+    if (sh.ms == 2 && ((cb != 32 && cb != 16) || has_res)) continue;
     if (force_bn <= 0 && sh.pair == 1 && bn > 64 && bn >= 2 * ((N + 63) / 64) * 64) continue;  // far wider than N
     const int slots = sh.pair == 2 ? sms / 2 : sms;
     const int num_kb = (K + sh.bk - 1) / sh.bk;
-    const long tiles = (long)((M + kBM * sh.pair - 1) / (kBM * sh.pair)) * ((N + bn - 1) / bn);
+    const int tm = kBM * sh.pair * sh.ms;
+    const long tiles = (long)((M + tm - 1) / tm) * ((N + bn - 1) / bn);
     for (int ks = 1; ks <= 32; ++ks) {
       const int kb_per = (num_kb + ks - 1) / ks;
       const int kse = (num_kb + kb_per - 1) / kb_per;  // slices actually used
@@ -809,8 +900,9 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
       if (ws > ws_limit) break;
       const long units = tiles * ks;
       const long waves = (units + slots - 1) / slots;
-      // epilogue: ~0.8 us per 32-column chunk and warp group; 256-wide residual tiles use one group
-      const double epi = 0.8 * (bn / 32) / ((has_res && bn == 256) ? 1 : 2);
+      // epilogue: ~0.8 us per 32-column chunk and warp group; 256-wide residual tiles use one
+      // group; with two M sub-tiles each group drains a whole sub-tile
+      const double epi = sh.ms == 2 ? 0.8 * (bn / 32) : 0.8 * (bn / 32) / ((has_res && bn == 256) ? 1 : 2);
       double cost = 14.0 + (waves - 1) * 2.0 + waves * std::max(kb_per * sh.per_stage, epi);
       if (ks > 1) cost += (double)(ks + 2) * M * N * 4 / 8.0e6;
       if (cost < best_cost - 1e-9) {
@@ -818,6 +910,7 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
         best.bn = bn;
         best.pair = sh.pair;
         best.bk = sh.bk;
+        best.ms = sh.ms;
         best.ksplit = ks;
         best.kb_per = kb_per;
         best.ws_bytes = ws;
@@ -828,6 +921,7 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
     best.bn = force_bn > 0 ? force_bn : 256;
     best.pair = 1;
     best.bk = 32;
+    best.ms = 1;
     best.ksplit = 1;
     best.kb_per = (K + 31) / 32;
     best.ws_bytes = 0;
@@ -890,11 +984,18 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   TcParams p{};
   p.M = a.M;
   p.N = a.N;
-  int cb = 32;
+  const int cb = problem_cb(a);
+  const int K = problem_k(a);
+  if (tc_num_kb(K) * 32 > a.kpad) {
+    set_error("tcgen05 gemm: weights padded to %d, need %d", a.kpad, tc_num_kb(K) * 32);
+    return SPINN_CUDA_EINVAL;
+  }
+  const size_t ws_limit = (a.ws && a.batch == 1) ? std::min(a.ws_bytes, kWsCap) : 0;  // batched: no split
+  const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn);
+  const int arows = kBM * tp.ms;  // A rows per box
   CUtensorMap ma, mb, my, mr;
   int rc;
   if (a.a_mode == 0) {
-    cb = channel_block(a.cpad);
     p.cpad = a.cpad;
     p.taps = a.kh * a.kw;
     p.kw = a.kw;
@@ -908,23 +1009,16 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     p.pad_w = a.pw;
     int lw, lh, uw, uh;
     im2col_corners(a, &lw, &lh, &uw, &uh);
-    rc = encode_im2col_4d(&ma, a.x, a.n, a.h, a.w, a.cpad, lw, lh, uw, uh, cb, kBM, a.sw, a.sh, swizzle_for(cb));
+    rc = encode_im2col_4d(&ma, a.x, a.n, a.h, a.w, a.cpad, lw, lh, uw, uh, cb, arows, a.sw, a.sh, swizzle_for(cb));
     if (rc) return rc;
   } else {
     p.cpad = a.K;
     p.taps = 1;
     p.kw = 1;
-    rc = encode_tiled_3d(&ma, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.batch, (uint64_t)a.lda * 4, 32, kBM,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = encode_tiled_3d(&ma, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.batch, (uint64_t)a.lda * 4, 32,
+                         (uint32_t)arows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  const int K = problem_k(a);
-  if (tc_num_kb(K) * 32 > a.kpad) {
-    set_error("tcgen05 gemm: weights padded to %d, need %d", a.kpad, tc_num_kb(K) * 32);
-    return SPINN_CUDA_EINVAL;
-  }
-  const size_t ws_limit = (a.ws && a.batch == 1) ? std::min(a.ws_bytes, kWsCap) : 0;  // batched: no split
-  const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn);
   p.num_kb = (K + tp.bk - 1) / tp.bk;  // stages beyond kpad read zero weights
   const int bn = tp.bn;
   const bool split = tp.ksplit > 1;
@@ -945,7 +1039,8 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     mr = my;
   }
   p.tiles_n = (a.N + bn - 1) / bn;
-  const long tiles = (long)((a.M + kBM * tp.pair - 1) / (kBM * tp.pair)) * p.tiles_n;
+  const int tm = kBM * tp.pair * tp.ms;
+  const long tiles = (long)((a.M + tm - 1) / tm) * p.tiles_n;
   if (tiles > 0x7FFFFFFF) {
     set_error("tcgen05 gemm: too many tiles");
     return SPINN_CUDA_EINVAL;
@@ -968,13 +1063,13 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   p.alpha = a.alpha;
   p.bias = a.bias;
   p.err = a.err ? a.err : device_error_flag(dev);
-  const int pr = tp.pair;
+  const int pr = tp.pair, ms = tp.ms;
   if (a.a_mode == 0)
-    rc = p.has_res ? dispatch_bn_cb<kIm2col, true>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream)
-                   : dispatch_bn_cb<kIm2col, false>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream);
+    rc = p.has_res ? dispatch_bn_cb<kIm2col, true>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream)
+                   : dispatch_bn_cb<kIm2col, false>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream);
   else
-    rc = p.has_res ? dispatch_bn_cb<kTiled, true>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream)
-                   : dispatch_bn_cb<kTiled, false>(bn, cb, pr, tp.bk, ma, mb, my, mr, p, sms, stream);
+    rc = p.has_res ? dispatch_bn_cb<kTiled, true>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream)
+                   : dispatch_bn_cb<kTiled, false>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream);
   if (rc || !split) return rc;
   const long groups = (long)a.M * ((a.N + 3) / 4);
   const int fgrid = (int)std::min<long>((groups + 255) / 256, (long)sms * 8);

@@ -148,15 +148,19 @@ def test_split_k_is_deterministic(cuda_lib):
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
 
 
-PAIR_SHAPES = ["256,1,2", "128,1,2", "256,3,2", "128,2,2"]
+# bn,ksplit,pair[,bk,ms]: CTA pairs (cta_group::2) and single CTAs with two 128-row M sub-tiles,
+# each with and without split-K
+PAIR_SHAPES = ["256,1,2", "128,1,2", "256,3,2", "128,2,2",
+               "64,1,1,32,2", "128,1,1,64,2", "64,2,1,64,2", "128,3,1,32,2"]
 TC_CASES = [c for c in CONV_CASES if c[8] == 1]
 
 
 @pytest.mark.parametrize("tiles", PAIR_SHAPES)
 @pytest.mark.parametrize("case", TC_CASES, ids=lambda c: "x".join(map(str, c[:9])) + f"-a{c[9]}")
 def test_conv2d_cta_pair_tiles(cuda_lib, port_oracle, monkeypatch, case, tiles):
-    """The 2-SM (cta_group::2) tiles, with and without split-K, forced on every conv shape;
-    pairs whose second half lies past the last row must store nothing there."""
+    """The 256-row tiles -- 2-SM (cta_group::2) pairs and single CTAs with two M sub-tiles --
+    with and without split-K, forced on every conv shape; a tile whose second half lies past
+    the last row must store nothing there."""
     from spinn_b200 import runtime
     monkeypatch.setenv("SPINN_TC_TILES", tiles)
     n, c, h, w, oc, k, s, p, g, act, bias, res = case
