@@ -720,10 +720,12 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   }
   TcParams q = p;
   q.nstages = C::STAGES;
+  // L2 prefetch ahead of the TMA loads: measured neutral to harmful on B200 (the prefetches
+  // are TMA operations too), so off unless a tuning run asks for it
   q.pf_a = 0;
-  q.pf_res = 1;
+  q.pf_res = 0;
   if (const char* e = getenv("SPINN_TC_PF")) {  // tuning: "a,res" prefetch distances
-    int a = 0, r = 1;
+    int a = 0, r = 0;
     if (sscanf(e, "%d,%d", &a, &r) >= 1) {
       q.pf_a = a < 0 ? 0 : a;
       q.pf_res = r;
