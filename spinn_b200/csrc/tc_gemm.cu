@@ -17,9 +17,11 @@
 //   warps 4..11 epilogue: tcgen05.ld -> bias / residual / activation / tf32 rounding ->
 //               swizzled shared staging -> TMA store; warps w and w+4 share the 32
 //               accumulator lanes of quarter w % 4 and take alternate 32-column chunks
-// Tiles are 128 output pixels x BN output channels, scheduled n-fastest so that CTAs running
-// together share the activation tile in L2.  The TMEM accumulators (2 at BN=256, 4 at 128, 8
-// at 64 -- all 512 columns) let the epilogue of one tile overlap the main loop of the next ones.
+//               (with two M sub-tiles: warps 4..7 drain sub-tile 0, warps 8..11 sub-tile 1)
+// Tiles are 128 output pixels x BN output channels (256 pixels for CTA pairs and for two M
+// sub-tiles), scheduled n-fastest so that CTAs running together share the activation tile in
+// L2.  The TMEM accumulators (all 512 columns: 512 / (BN x sub-tiles) of them) let the
+// epilogue of one tile overlap the main loop of the next ones.
 //
 // Problems with fewer tiles than SMs (small batches, the last stages of a ResNet, the FC
 // layer) are split along K when the caller supplies a workspace: each (tile, K slice) unit
@@ -58,8 +60,6 @@ struct TcParams {
   int batch, b_batched;           // batched GEMM: z is the batch index (then ksplit == 1)
   int reverse;                    // walk the tiles from the last one (alternates between layers)
   int nstages;                    // ring stages in use (<= the variant's STAGES)
-  int pf_a;                       // tiled A: L2 prefetch this many k-blocks ahead (0: off)
-  int pf_res;                     // residual: L2 prefetch of the next tile's rows (0: off)
   int has_res, act, round_out;
   float alpha;
   const float* bias;
@@ -115,7 +115,7 @@ struct Cfg {
   static constexpr uint32_t SMEM = STAGES * STAGE + EPI + 512 + 1024;
   static_assert(STAGES >= 2, "pipeline needs two stages");
   static_assert(PAIR == 1 || BNC >= 64, "pair tiles split BN into halves of at least 64 rows");
-  static_assert(MS == 1 || (PAIR == 1 && !RES && CB >= 16 && BN <= 128), "two M sub-tiles: narrow plain tiles only");
+  static_assert(MS == 1 || (PAIR == 1 && CB >= 16 && BN <= 128), "two M sub-tiles: narrow single-CTA tiles only");
 };
 
 // Start-address offset (bytes) of the j-th 8-wide K slice of a stage, and the descriptor
@@ -233,40 +233,22 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
   griddep_wait();
   griddep_launch_dependents();
 
+  // Work units of this CTA: unit0, unit0 + unit_step, ...  (A dynamic schedule -- units
+  // claimed from a global counter and handed to the other roles through a shared-memory
+  // queue -- evened out the CTAs' finishing times but measured 1-2% slower end to end.)
+  auto take_unit = [&](int it) -> int {
+    const long u = (long)unit0 + (long)it * unit_step;
+    return u < p.num_units ? (int)u : -1;
+  };
+
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (A, W)
     int s = 0;
     uint32_t ph = 0;
     uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
-    // Tiled A only: the memory-bound pointwise layers stream A from HBM, and the ring holds
-    // only a few k-blocks. L2 prefetches pf_a k-blocks ahead (into the next unit near the end
-    // of a unit) keep more of A in flight than shared memory can.
-    struct UnitA {
-      int m0, bz, kb0, kb1;
-    };
-    auto unit_a = [&](int u) {
-      UnitA r;
-      const int z = u / p.num_tiles, t = u - z * p.num_tiles;
-      const int tile = p.reverse ? p.num_tiles - 1 - t : t;
-      const int ks = p.batch > 1 ? 0 : z;
-      r.bz = p.batch > 1 ? z : 0;
-      const int tm = tile / p.tiles_n;
-      r.m0 = tm * TM + (int)rank * kBM;
-      if (r.m0 >= p.M) r.m0 = tm * TM;
-      r.kb0 = ks * p.kb_per;
-      r.kb1 = min(p.num_kb, r.kb0 + p.kb_per);
-      return r;
-    };
-    auto prefetch_a = [&](const UnitA& ua, int kb) {
-#pragma unroll
-      for (int j = 0; j < C::NSUB; ++j) tma_prefetch_3d(&mapA, kb * BK + j * CB, ua.m0, ua.bz);
-    };
-    const bool pf_a = MODE != kIm2col && p.pf_a > 0;
-    if (pf_a && lane == 0 && unit0 < p.num_units) {
-      const UnitA ua = unit_a(unit0);
-      for (int kb = ua.kb0 + p.nstages; kb < min(ua.kb1, ua.kb0 + p.pf_a); ++kb) prefetch_a(ua, kb);
-    }
-    for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step) {
+    for (int it = 0; !warp_aborted(abort_flag); ++it) {
+      const int u = take_unit(it);
+      if (u < 0) break;
       const int z = u / p.num_tiles, t = u - z * p.num_tiles;
       const int tile = p.reverse ? p.num_tiles - 1 - t : t;
       const int ks = p.batch > 1 ? 0 : z, bz = p.batch > 1 ? z : 0;
@@ -291,20 +273,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
         r = tap / p.kw;
         q = tap - r * p.kw;
       }
-      UnitA next{0, 0, 0, 0};
-      if (pf_a && u + unit_step < p.num_units) next = unit_a(u + unit_step);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!warp_wait(&empty[s], ph ^ 1, abort_flag, kTimeoutNs)) break;
         if (lane == 0) {
-          if (pf_a) {
-            const int kp = kb + p.pf_a;
-            if (kp < kb1) {
-              prefetch_a(UnitA{m0, bz, kb0, kb1}, kp);
-            } else {
-              const int kn = next.kb0 + (kp - kb1);
-              if (kn < next.kb1) prefetch_a(next, kn);
-            }
-          }
           if (rank == 0) mbar_arrive_expect_tx(&full[s], C::STAGE * PAIR);
           uint8_t* a_dst = sA + s * C::A_STAGE;
           uint8_t* b_dst = sB + s * C::B_STAGE;
@@ -373,7 +344,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
       uint32_t ph = 0;
       int it = 0;
       bool issued = false;
-      for (int u = unit0; u < p.num_units && !warp_aborted(abort_flag); u += unit_step, ++it) {
+      for (;; ++it) {
+        const int u = take_unit(it);
+        if (u < 0 || warp_aborted(abort_flag)) break;
         const int b = it % C::NACC;
         const uint32_t aph = (it / C::NACC) & 1;
         const int kb0 = (p.batch > 1 ? 0 : u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
@@ -446,35 +419,30 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
         int count[2] = {0, 0};  // chunks loaded so far for each epilogue group
         uint32_t armed = 0, armed_ph = 0;
         int it = 0;  // units so far: chunk c goes to epilogue group (c + it) % EPI_GROUPS
-        // L2 prefetch of a tile's residual rows, issued one tile ahead: the ring holds only a
-        // few chunks, too few to cover HBM latency at full bandwidth on its own.
-        auto prefetch_res = [&](int t) {
-          if (!p.pf_res || t >= p.num_tiles) return;
+        for (;; ++it) {  // ksplit == 1: a unit is a tile
+          const int t = take_unit(it);
+          if (t < 0 || *abort_flag) break;
           const int tile = p.reverse ? p.num_tiles - 1 - t : t;
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
           const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
-          for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) tma_prefetch_2d(&mapR, n0 + c * 32, m0);
-        };
-        prefetch_res(unit0);
-        for (int t = unit0; t < p.num_tiles && !*abort_flag; t += unit_step, ++it) {  // ksplit == 1
-          const int tile = p.reverse ? p.num_tiles - 1 - t : t;
-          const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
-          const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
-          prefetch_res(t + unit_step);
           bool ok = true;
-          for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
-            const int g = (c + it) % C::EPI_GROUPS;
-            const int slot = g * C::RES_G + count[g] % C::RES_G;
-            const uint32_t ph = (count[g] / C::RES_G) & 1;
-            if (!mbar_wait(&rempty[slot], ph ^ 1, abort_flag, kTimeoutNs)) {
-              ok = false;
-              break;
+          // chunk c goes to group (c + it) % EPI_GROUPS; with two M sub-tiles every chunk
+          // goes to both groups, each its own sub-tile's 128 rows
+          for (int c = 0; ok && c < BN / 32 && n0 + c * 32 < p.N; ++c) {
+            for (int h = 0; h < MS; ++h) {
+              const int g = MS == 2 ? h : (c + it) % C::EPI_GROUPS;
+              const int slot = g * C::RES_G + count[g] % C::RES_G;
+              const uint32_t ph = (count[g] / C::RES_G) & 1;
+              if (!mbar_wait(&rempty[slot], ph ^ 1, abort_flag, kTimeoutNs)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&rfull[slot], C::RES_SLOT);
+              armed |= 1u << slot;
+              armed_ph = (armed_ph & ~(1u << slot)) | (ph << slot);
+              tma_load_2d(&mapR, &rfull[slot], sRes + slot * C::RES_SLOT, n0 + c * 32, m0 + h * kBM);
+              ++count[g];
             }
-            mbar_arrive_expect_tx(&rfull[slot], C::RES_SLOT);
-            armed |= 1u << slot;
-            armed_ph = (armed_ph & ~(1u << slot)) | (ph << slot);
-            tma_load_2d(&mapR, &rfull[slot], sRes + slot * C::RES_SLOT, n0 + c * 32, m0);
-            ++count[g];
           }
           if (!ok) break;
         }
@@ -496,7 +464,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
     // the finish kernel applies the epilogue after reducing the planes.
     const bool partial = p.ksplit > 1;
     const bool unit_alpha = p.alpha == 1.0f;
-    for (int u = unit0; u < p.num_units; u += unit_step, ++it) {
+    for (;; ++it) {
+      const int u = take_unit(it);
+      if (u < 0) break;
       const int z = u / p.num_tiles, t = u - z * p.num_tiles;  // z: K slice or batch -> output plane
       const int tile = p.reverse ? p.num_tiles - 1 - t : t;
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
@@ -720,17 +690,6 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   }
   TcParams q = p;
   q.nstages = C::STAGES;
-  // L2 prefetch ahead of the TMA loads: measured neutral to harmful on B200 (the prefetches
-  // are TMA operations too), so off unless a tuning run asks for it
-  q.pf_a = 0;
-  q.pf_res = 0;
-  if (const char* e = getenv("SPINN_TC_PF")) {  // tuning: "a,res" prefetch distances
-    int a = 0, r = 0;
-    if (sscanf(e, "%d,%d", &a, &r) >= 1) {
-      q.pf_a = a < 0 ? 0 : a;
-      q.pf_res = r;
-    }
-  }
   if (const char* e = getenv("SPINN_TC_STAGES")) {  // tuning: use fewer ring stages
     const int v = atoi(e);
     if (v >= 2 && v < C::STAGES) q.nstages = v;
@@ -784,19 +743,21 @@ int dispatch_bn_cb(int bn, int cb, int pair, int bk, int ms, const CUtensorMap& 
   if (bn == BNV && cb == CBV && pair == 1 && bk == BKV && ms == 2) \
     return launch_variant<BNV, CBV, MODE, RES, 1, BKV, 2>(ma, mb, my, mr, p, sms, s);
   SPINN_TC_CASE(256, 32, 1, 32) SPINN_TC_CASE(128, 32, 1, 32) SPINN_TC_CASE(64, 32, 1, 32)
+  SPINN_TC_CASE2(128, 32, 32) SPINN_TC_CASE2(64, 32, 32)
   if constexpr (!RES) {
     SPINN_TC_CASE(128, 32, 1, 64) SPINN_TC_CASE(64, 32, 1, 64)
     SPINN_TC_CASE(256, 32, 2, 64) SPINN_TC_CASE(128, 32, 2, 64)
-    SPINN_TC_CASE2(128, 32, 32) SPINN_TC_CASE2(64, 32, 32) SPINN_TC_CASE2(128, 32, 64) SPINN_TC_CASE2(64, 32, 64)
+    SPINN_TC_CASE2(128, 32, 64) SPINN_TC_CASE2(64, 32, 64)
   }
   if constexpr (MODE == kIm2col) {
     SPINN_TC_CASE(256, 16, 1, 32) SPINN_TC_CASE(128, 16, 1, 32) SPINN_TC_CASE(64, 16, 1, 32)
     SPINN_TC_CASE(256, 8, 1, 32) SPINN_TC_CASE(128, 8, 1, 32) SPINN_TC_CASE(64, 8, 1, 32)
     SPINN_TC_CASE(256, 4, 1, 32) SPINN_TC_CASE(128, 4, 1, 32) SPINN_TC_CASE(64, 4, 1, 32)
+    SPINN_TC_CASE2(128, 16, 32) SPINN_TC_CASE2(64, 16, 32)
     if constexpr (!RES) {
       SPINN_TC_CASE(128, 16, 1, 64) SPINN_TC_CASE(64, 16, 1, 64)
       SPINN_TC_CASE(256, 16, 2, 64) SPINN_TC_CASE(128, 16, 2, 64)
-      SPINN_TC_CASE2(128, 16, 32) SPINN_TC_CASE2(64, 16, 32) SPINN_TC_CASE2(128, 16, 64) SPINN_TC_CASE2(64, 16, 64)
+      SPINN_TC_CASE2(128, 16, 64) SPINN_TC_CASE2(64, 16, 64)
     }
   }
 #undef SPINN_TC_CASE
@@ -886,7 +847,9 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
     if (fbk > 0 && sh.bk != fbk) continue;
     if (fms > 0 && sh.ms != fms) continue;
     if (sh.bk == 64 && ((cb != 32 && cb != 16) || has_res)) continue;
-    if (sh.ms == 2 && ((cb != 32 && cb != 16) || has_res)) continue;
+    // sub-tiles with a fused residual: correct (forced shapes) but measured no faster than
+    // 256-wide single tiles, and the model cannot tell them apart, so not chosen by default
+    if (sh.ms == 2 && ((cb != 32 && cb != 16) || (has_res && (sh.bk != 32 || fms != 2)))) continue;
     if (force_bn <= 0 && sh.pair == 1 && bn > 64 && bn >= 2 * ((N + 63) / 64) * 64) continue;  // far wider than N
     const int slots = sh.pair == 2 ? sms / 2 : sms;
     const int num_kb = (K + sh.bk - 1) / sh.bk;
@@ -1059,6 +1022,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     return SPINN_CUDA_EINVAL;
   }
   p.num_units = (int)(tiles * zs);
+
   p.has_res = a.res != nullptr && !split;
   p.act = a.act;
   p.round_out = a.round_out;
