@@ -146,6 +146,16 @@ int spinn_cuda_plan(SpinnCudaModel *m, int device, uint64_t max_arena_bytes, int
  * (spinn_runtime.h:125-131).  Synchronous. */
 int spinn_cuda_run(SpinnCudaModel *m, const void *input, void *output);
 
+/* Pipelined runs (serving loops): spinn_cuda_submit queues one inference -- input 0 copied
+ * from `input` (host, pinned for overlap) into one of two device staging buffers on a copy
+ * stream, the run, output 0 copied back to `output` -- and returns without waiting, so the
+ * input copy of the next submission overlaps this one's run.  `input` and `output` must stay
+ * valid and untouched until spinn_cuda_wait returns; results arrive in submission order.
+ * Either pointer may be NULL (no copy).  spinn_cuda_wait blocks until every submitted run has
+ * finished and reports a deferred error (a kernel's expired wait: SPINN_CUDA_ETIMEOUT). */
+int spinn_cuda_submit(SpinnCudaModel *m, const void *input, void *output);
+int spinn_cuda_wait(SpinnCudaModel *m);
+
 /* Device-resident run: inputs are taken from, and outputs left in, the model's device
  * buffers (spinn_cuda_io_ptr); work is queued on `stream` (NULL = the model's stream) and
  * not waited for. */

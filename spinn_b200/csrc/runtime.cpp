@@ -151,6 +151,13 @@ struct SpinnCudaModel {
   std::vector<cudaEvent_t> events;
   std::vector<float> step_ms;
   int kernels = 0;
+  // pipelined submission (spinn_cuda_submit): input 0 goes host -> staging[slot] on
+  // copy_stream, then staging -> the model's input buffer on the model stream before the run
+  cudaStream_t copy_stream = nullptr;
+  void* staging[2] = {nullptr, nullptr};
+  cudaEvent_t in_ready[2] = {nullptr, nullptr};  // staging[k] filled (copy stream)
+  cudaEvent_t in_free[2] = {nullptr, nullptr};   // staging[k] consumed (model stream)
+  uint64_t submitted = 0;
 };
 
 namespace spinn {
@@ -1507,6 +1514,13 @@ static void release_model(SpinnCudaModel* m) {
   if (m->arena) cudaFree(m->arena);
   if (m->wdev) cudaFree(m->wdev);
   if (m->splitk_ws) cudaFree(m->splitk_ws);
+  if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
+  for (int k = 0; k < 2; ++k) {
+    if (m->staging[k]) cudaFree(m->staging[k]);
+    if (m->in_ready[k]) cudaEventDestroy(m->in_ready[k]);
+    if (m->in_free[k]) cudaEventDestroy(m->in_free[k]);
+  }
+  if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }
@@ -1651,6 +1665,52 @@ __attribute__((visibility("default"))) int spinn_cuda_run(SpinnCudaModel* m, con
     const Buf& b = m->bufs[m->out_buf[0]];
     SPINN_CUDA_TRY(cudaMemcpyAsync(output, b.ptr, b.bytes, cudaMemcpyDeviceToHost, m->stream));
   }
+  SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return check_device_error_flag(m->device, m->stream);
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_submit(SpinnCudaModel* m, const void* input, void* output) {
+  if (!m || !m->planned) {
+    set_error("spinn_cuda_submit: model not planned");
+    return SPINN_CUDA_ESTATE;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(m->device));
+  if (input && !m->in_buf.empty()) {
+    const Buf& b = m->bufs[m->in_buf[0]];
+    if (!m->copy_stream) {
+      SPINN_CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
+      for (int k = 0; k < 2; ++k) {
+        SPINN_CUDA_TRY(cudaMalloc(&m->staging[k], b.bytes));
+        SPINN_CUDA_TRY(cudaEventCreateWithFlags(&m->in_ready[k], cudaEventDisableTiming));
+        SPINN_CUDA_TRY(cudaEventCreateWithFlags(&m->in_free[k], cudaEventDisableTiming));
+      }
+    }
+    const int k = (int)(m->submitted & 1);
+    // the staging buffer's previous contents (two submissions back) have been consumed; an
+    // event never recorded is no wait
+    SPINN_CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->in_free[k], 0));
+    SPINN_CUDA_TRY(cudaMemcpyAsync(m->staging[k], input, b.bytes, cudaMemcpyHostToDevice, m->copy_stream));
+    SPINN_CUDA_TRY(cudaEventRecord(m->in_ready[k], m->copy_stream));
+    SPINN_CUDA_TRY(cudaStreamWaitEvent(m->stream, m->in_ready[k], 0));
+    SPINN_CUDA_TRY(cudaMemcpyAsync(b.ptr, m->staging[k], b.bytes, cudaMemcpyDeviceToDevice, m->stream));
+    SPINN_CUDA_TRY(cudaEventRecord(m->in_free[k], m->stream));
+  }
+  int rc = spinn_cuda_run_device(m, nullptr);
+  if (rc) return rc;
+  if (output && !m->out_buf.empty()) {
+    const Buf& b = m->bufs[m->out_buf[0]];
+    SPINN_CUDA_TRY(cudaMemcpyAsync(output, b.ptr, b.bytes, cudaMemcpyDeviceToHost, m->stream));
+  }
+  ++m->submitted;
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_wait(SpinnCudaModel* m) {
+  if (!m || !m->planned) {
+    set_error("spinn_cuda_wait: model not planned");
+    return SPINN_CUDA_ESTATE;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(m->device));
   SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
   return check_device_error_flag(m->device, m->stream);
 }

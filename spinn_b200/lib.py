@@ -67,6 +67,8 @@ _SIGS = {
     "spinn_cuda_plan": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_int]),
     "spinn_cuda_run": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_run_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "spinn_cuda_submit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "spinn_cuda_wait": (ctypes.c_int, [ctypes.c_void_p]),
     "spinn_cuda_run_profiled": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_io_ptr": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                            ctypes.POINTER(ctypes.c_size_t)]),

@@ -178,6 +178,15 @@ class Model:
     def run_ptr(self, host_in: int, host_out: int) -> None:
         check(lib().spinn_cuda_run(self._h, host_in, host_out), "spinn_cuda_run")
 
+    def submit_ptr(self, host_in: int, host_out: int) -> None:
+        """Queues one run (``spinn_cuda_submit``): host buffers by address, pinned for overlap;
+        they must stay untouched until :meth:`wait` returns."""
+        check(lib().spinn_cuda_submit(self._h, host_in or None, host_out or None), "spinn_cuda_submit")
+
+    def wait(self) -> None:
+        """Waits for every submitted run (``spinn_cuda_wait``)."""
+        check(lib().spinn_cuda_wait(self._h), "spinn_cuda_wait")
+
     def run_device(self, stream: int = 0) -> None:
         check(lib().spinn_cuda_run_device(self._h, stream or None), "spinn_cuda_run_device")
 

@@ -143,3 +143,25 @@ def test_yolo_shaped_end_to_end(cuda_lib, ref_oracle, tmp_path, batch, image):
     assert (cls_y.argmax(1) == cls_r.argmax(1))[robust].all()
     kinds = m.step_kinds()
     assert 3 in kinds and 1 in kinds  # depthwise CUDA-core kernel and tcgen05 convolutions
+
+
+def test_submit_pipeline_matches_run(cuda_lib):
+    """spinn_cuda_submit / spinn_cuda_wait: several different inputs in flight through the
+    two staging buffers give the same outputs as one synchronous spinn_cuda_run each."""
+    import torch
+    from spinn_b200 import ennf, netdef, runtime
+    g = netdef.resnet(50, batch=2, image=64, width=16, seed=9)
+    m = runtime.Model(ennf.convert(g))
+    xs = [netdef.resnet_input(2, image=64, seed=s) for s in range(5)]
+    ref = [m.run(x).copy() for x in xs]
+    ins = [torch.from_numpy(x).pin_memory() for x in xs]
+    outs = [torch.empty(ref[0].shape, dtype=torch.float32).pin_memory() for _ in xs]
+    for _ in range(2):
+        for i, o in zip(ins, outs):
+            o.fill_(float("nan"))
+        for i, o in zip(ins, outs):
+            m.submit_ptr(i.data_ptr(), o.data_ptr())
+        m.wait()
+        for r, o in zip(ref, outs):
+            assert np.array_equal(o.numpy(), r)
+    m.close()
