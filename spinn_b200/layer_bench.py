@@ -2,6 +2,7 @@
 runtime -- a unit for tuning and for profiling a single kernel.
 
     python -m spinn_b200.layer_bench --batch 512 --c 256 --hw 14 --oc 256 --k 3 [--residual]
+    python -m spinn_b200.layer_bench --batch 128 --c 256 --hw 14 --oc 1024 --k 1 --projection
 
 Prints one JSON line: device ms per run (CUDA events around the planned step list, inputs
 resident), algorithmic TFLOP/s of the layer and algorithmic GB/s (input + output
@@ -22,6 +23,9 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=3)
     ap.add_argument("--stride", type=int, default=1)
     ap.add_argument("--residual", action="store_true", help="conv+BN+Add+ReLU (needs c == oc, stride 1)")
+    ap.add_argument("--projection", action="store_true",
+                    help="bottleneck end with a projection shortcut: ReLU(BN(conv(x)) + BN(conv1x1(x))); "
+                         "the second conv (c -> oc) carries the fused residual")
     ap.add_argument("--winograd", action="store_true", help="plan with Winograd F(4x4,3x3)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -33,7 +37,9 @@ def main(argv=None):
     from spinn_b200 import ennf, netdef, runtime
 
     pad = a.k // 2
-    if a.residual:
+    if a.projection:
+        g, x = netdef.conv_bn_proj_add_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k)
+    elif a.residual:
         g, x = netdef.conv_bn_add_relu(batch=a.batch, c=a.c, hw=a.hw)
     else:
         g, x = netdef.conv_bn_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k, stride=a.stride, pad=pad)
@@ -52,11 +58,14 @@ def main(argv=None):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
     oc = a.c if a.residual else a.oc
-    oh = (a.hw + 2 * pad - a.k) // a.stride + 1
-    flops = 2.0 * a.batch * oc * oh * oh * a.c * a.k * a.k
+    oh = a.hw if a.projection else (a.hw + 2 * pad - a.k) // a.stride + 1
+    # --projection: both convolutions (the shortcut 1x1 and the fused-residual one)
+    flops = 2.0 * a.batch * oc * oh * oh * a.c * (a.k * a.k + (1 if a.projection else 0))
     cpad = (a.c + 3) // 4 * 4
-    byts = 4.0 * (a.batch * a.hw * a.hw * cpad + a.batch * oh * oh * oc * (2 if a.residual else 1)
-                  + oc * a.c * a.k * a.k)
+    res = a.residual or a.projection
+    byts = 4.0 * (a.batch * a.hw * a.hw * cpad * (2 if a.projection else 1)
+                  + a.batch * oh * oh * oc * ((3 if a.projection else 2) if res else 1)
+                  + oc * a.c * (a.k * a.k + (1 if a.projection else 0)))
     print(json.dumps({"layer": vars(a), "ms_per_run": ms, "tflops": flops / ms / 1e9, "gbs": byts / ms / 1e6,
                       "steps": model.plan_info()["steps"]}))
     model.close()

@@ -298,6 +298,22 @@ def conv_bn_add_relu(batch: int = 1, c: int = 64, hw: int = 56, seed: int = 0
     return g, x_val
 
 
+def conv_bn_proj_add_relu(batch: int = 1, c: int = 256, hw: int = 14, oc: int = 1024, k: int = 1,
+                          seed: int = 0) -> Tuple[Graph, np.ndarray]:
+    """The last convolution of a bottleneck with a projection shortcut: the shortcut
+    BN(Conv1x1(x)) is added to BN(Conv kxk(x)) and ReLU'd, so the second convolution carries
+    the fused residual (c -> oc channels, stride 1)."""
+    rng = np.random.default_rng(seed)
+    x_val = rng.uniform(-1.0, 1.0, (batch, c, hw, hw)).astype(np.float32)
+    g = Graph("conv_bn_proj_add_relu")
+    b = _Builder(g, rng)
+    x = g.add_input("input", (batch, c, hw, hw))
+    r = b.bn(b.conv(x, oc, 1, 1, 0))
+    y = b.unary("Relu", b.add(b.bn(b.conv(x, oc, k, 1, k // 2)), r))
+    g.mark_output(y)
+    return g, x_val
+
+
 RESNET_DEPTHS = {18: None, 50: [3, 4, 6, 3], 101: [3, 4, 23, 3], 152: [3, 8, 36, 3]}
 
 
