@@ -126,6 +126,58 @@ __global__ void maxpool_nhwc_kernel(const float4* __restrict__ x, float4* __rest
   }
 }
 
+// MaxPool 3x3 stride 2 (the ResNet stem pool), one CTA per TY x TX output pixels of one image:
+// the (2 TY + 1) x (2 TX + 1) input window of all channels is read once with coalesced float4
+// loads into shared memory (taps outside the image read as -1e30, which a max over taps that
+// includes a real one ignores, as the reference skips them), then each output takes its nine
+// taps from there.  Nine global loads per output become ~1.2.
+constexpr int kPoolTY = 4, kPoolTX = 8, kPoolThreads = 256, kPoolMaxC4 = 16;
+__global__ void __launch_bounds__(kPoolThreads) maxpool3s2_tile_kernel(const float4* __restrict__ x,
+                                                                      float4* __restrict__ y, int h, int w, int c4,
+                                                                      int oh, int ow, int ph, int pw) {
+  constexpr int IH = 2 * kPoolTY + 1, IW = 2 * kPoolTX + 1;
+  __shared__ float4 tile[IH * IW * kPoolMaxC4];
+  const int ox0 = blockIdx.x * kPoolTX, oy0 = blockIdx.y * kPoolTY, b = blockIdx.z;
+  const int iy0 = 2 * oy0 - ph, ix0 = 2 * ox0 - pw;
+  const float4* xb = x + (size_t)b * h * w * c4;
+  const int nin = IH * IW * c4;
+  // all of this thread's loads issued before the first store, so they are in flight together
+  constexpr int PER = (IH * IW * kPoolMaxC4 + kPoolThreads - 1) / kPoolThreads;
+  float4 v[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int e = threadIdx.x + k * kPoolThreads;
+    const int cq = e % c4, px = e / c4, col = px % IW, r = px / IW;
+    const int iy = iy0 + r, ix = ix0 + col;
+    v[k] = (e < nin && iy >= 0 && iy < h && ix >= 0 && ix < w) ? __ldg(xb + ((size_t)iy * w + ix) * c4 + cq)
+                                                              : make_float4(-1e30f, -1e30f, -1e30f, -1e30f);
+  }
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int e = threadIdx.x + k * kPoolThreads;
+    if (e < nin) tile[e] = v[k];
+  }
+  __syncthreads();
+  const int nout = kPoolTY * kPoolTX * c4;
+  for (int e = threadIdx.x; e < nout; e += kPoolThreads) {
+    const int cq = e % c4, px = e / c4, tx = px % kPoolTX, ty = px / kPoolTX;
+    const int oy = oy0 + ty, ox = ox0 + tx;
+    if (oy >= oh || ox >= ow) continue;
+    float4 m = make_float4(-1e30f, -1e30f, -1e30f, -1e30f);  // the reference's initial value (maxpool.c:32)
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {
+        const float4 v = tile[((2 * ty + r) * IW + 2 * tx + s) * c4 + cq];
+        m.x = v.x > m.x ? v.x : m.x;
+        m.y = v.y > m.y ? v.y : m.y;
+        m.z = v.z > m.z ? v.z : m.z;
+        m.w = v.w > m.w ? v.w : m.w;
+      }
+    y[(((size_t)b * oh + oy) * ow + ox) * c4 + cq] = m;
+  }
+}
+
 // TopK (SPINN/run_time/ops/tensor/topk.c:20-87): for every row of the last axis, the k largest
 // values in descending order and their int64 indices.  One CTA sorts a row in shared memory
 // (bitonic network over 64-bit keys: order-preserving bits of the value, inverted, above the
@@ -507,6 +559,15 @@ int launch_nhwc_to_nchw(const float* x, float* y, int n, int c, int h, int w, in
 int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh, int kw,
                         int sh, int sw, int ph, int pw, cudaStream_t s) {
   SPINN_CHECK_ARG(cpad % 4 == 0, "maxpool: channel stride %d not a multiple of 4", cpad);
+  // The tiled kernel needs every output window to hold at least one real tap (pads <= 1 with
+  // the ONNX output size), which the -1e30 fill relies on like the generic kernel's skip.
+  if (kh == 3 && kw == 3 && sh == 2 && sw == 2 && cpad / 4 <= kPoolMaxC4 && ph >= 0 && ph <= 1 && pw >= 0 &&
+      pw <= 1 && (oh - 1) * 2 - ph < h && (ow - 1) * 2 - pw < w && n <= 65535) {
+    dim3 grid((ow + kPoolTX - 1) / kPoolTX, (oh + kPoolTY - 1) / kPoolTY, n);
+    maxpool3s2_tile_kernel<<<grid, kPoolThreads, 0, s>>>(reinterpret_cast<const float4*>(x),
+                                                         reinterpret_cast<float4*>(y), h, w, cpad / 4, oh, ow, ph, pw);
+    SPINN_LAUNCH_CHECK();
+  }
   const long work = (long)n * oh * ow * (cpad / 4);
   if (work < (1l << 31) - (long)grid_for(work, kEltThreads) * kEltThreads)
     maxpool_nhwc_kernel<int><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(

@@ -99,3 +99,15 @@ def test_topk_matches_reference(cuda_lib, ref_oracle, tmp_path, shape, k):
     model.run(xv)
     assert np.array_equal(model.output(0).ravel(), ref[m.outputs[0]])
     assert np.array_equal(model.output(1).ravel(), ref[m.outputs[1]].view(np.int64))
+
+
+@pytest.mark.parametrize("shape", [(2, 64, 23, 29), (1, 12, 9, 9), (3, 16, 112, 112), (1, 80, 15, 14)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_maxpool_3x3_s2(cuda_lib, ref_oracle, tmp_path, shape):
+    """The ResNet stem pool (3x3, stride 2, pad 1): tiled kernel for <= 64 channels (ragged
+    tiles, padded channel lanes), the generic kernel above; identical values to op_maxpool."""
+    g, b, x, xv = _builder(shape)
+    y = b.maxpool(b.conv_bn(x, shape[1], 3, 1), 3, 2, 1)
+    g.mark_output(y)
+    out, ref = _run_both(ref_oracle, tmp_path, g, xv)
+    assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
