@@ -602,6 +602,10 @@ __global__ void __launch_bounds__(256)
     splitk_finish_kernel(const float* __restrict__ ws, int ksplit, int M, int N, int ldw, float alpha,
                          const float* __restrict__ bias, const float* __restrict__ res, int ldr, int act,
                          int round_out, float* __restrict__ y, int ldy) {
+  // launched as a programmatic dependent of the split GEMM: its CTAs may be resident before
+  // the partials are complete, and wait here until they are
+  griddep_wait();
+  griddep_launch_dependents();
   const int groups = (N + 3) >> 2;
   const long total = (long)M * groups;
   const size_t plane = (size_t)M * ldw;
@@ -1039,8 +1043,17 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   if (rc || !split) return rc;
   const long groups = (long)a.M * ((a.N + 3) / 4);
   const int fgrid = (int)std::min<long>((groups + 255) / 256, (long)sms * 8);
-  splitk_finish_kernel<<<fgrid, 256, 0, stream>>>(a.ws, tp.ksplit, a.M, a.N, ldw, a.alpha, a.bias, a.res, a.ldr, a.act,
-                                                  a.round_out, a.y, a.ldy);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(fgrid, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  SPINN_CUDA_TRY(cudaLaunchKernelEx(&cfg, splitk_finish_kernel, (const float*)a.ws, tp.ksplit, a.M, a.N, ldw, a.alpha,
+                                    a.bias, a.res, a.ldr, a.act, a.round_out, a.y, a.ldy));
   SPINN_CUDA_TRY(cudaGetLastError());
   return 0;
 }

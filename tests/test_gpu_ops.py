@@ -194,10 +194,11 @@ def test_gemm_cta_pair_tiles(cuda_lib, port_oracle, monkeypatch, case, tiles):
     assert rel_l2(y, ref) <= TOL, rel_l2(y, ref)
 
 
-@pytest.mark.parametrize("tiles", [None, "256,1,2", "128,1,1"])
+@pytest.mark.parametrize("tiles", [None, "256,1,2", "128,1,1", "64,1,1,64,2"])
 def test_matmul_batched_one_launch(cuda_lib, port_oracle, monkeypatch, tiles):
     """Batched MatMul runs as one launch over [batch][M][K] planes (3-D tensor maps, the batch
-    index in the work unit), with single CTAs and CTA pairs, shared and per-batch B."""
+    index in the work unit), with single CTAs, CTA pairs and two M sub-tiles, shared and
+    per-batch B."""
     from spinn_b200 import runtime
     if tiles:
         monkeypatch.setenv("SPINN_TC_TILES", tiles)
