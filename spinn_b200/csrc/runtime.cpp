@@ -151,12 +151,15 @@ struct SpinnCudaModel {
   std::vector<cudaEvent_t> events;
   std::vector<float> step_ms;
   int kernels = 0;
-  // pipelined submission (spinn_cuda_submit): input 0 goes host -> staging[slot] on
-  // copy_stream, then staging -> the model's input buffer on the model stream before the run
+  // pipelined submission (spinn_cuda_submit): input 0 alternates between its own staging
+  // buffer (slot 0) and a second one (slot 1) read by a second captured graph, so the next
+  // input's host copy (copy_stream) never touches the buffer the running graph reads
   cudaStream_t copy_stream = nullptr;
-  void* staging[2] = {nullptr, nullptr};
-  cudaEvent_t in_ready[2] = {nullptr, nullptr};  // staging[k] filled (copy stream)
-  cudaEvent_t in_free[2] = {nullptr, nullptr};   // staging[k] consumed (model stream)
+  void* alt_in = nullptr;                        // slot 1 input buffer
+  cudaGraph_t graph_alt = nullptr;
+  cudaGraphExec_t gexec_alt = nullptr;           // the step list reading alt_in
+  cudaEvent_t in_ready[2] = {nullptr, nullptr};  // slot k filled (copy stream)
+  cudaEvent_t in_free[2] = {nullptr, nullptr};   // the run reading slot k is done (model stream)
   uint64_t submitted = 0;
 };
 
@@ -1515,8 +1518,10 @@ static void release_model(SpinnCudaModel* m) {
   if (m->wdev) cudaFree(m->wdev);
   if (m->splitk_ws) cudaFree(m->splitk_ws);
   if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
+  if (m->gexec_alt) cudaGraphExecDestroy(m->gexec_alt);
+  if (m->graph_alt) cudaGraphDestroy(m->graph_alt);
+  if (m->alt_in) cudaFree(m->alt_in);
   for (int k = 0; k < 2; ++k) {
-    if (m->staging[k]) cudaFree(m->staging[k]);
     if (m->in_ready[k]) cudaEventDestroy(m->in_ready[k]);
     if (m->in_free[k]) cudaEventDestroy(m->in_free[k]);
   }
@@ -1669,34 +1674,77 @@ __attribute__((visibility("default"))) int spinn_cuda_run(SpinnCudaModel* m, con
   return check_device_error_flag(m->device, m->stream);
 }
 
+// Points input 0 -- its staging buffer and every tensor aliasing it -- at `p`; returns the
+// previous address.
+static float* set_input0_ptr(SpinnCudaModel* m, float* p) {
+  const int sb = m->in_buf[0];
+  float* old = m->bufs[sb].ptr;
+  for (size_t i = 0; i < m->bufs.size(); ++i) {
+    int r = (int)i;
+    while (m->bufs[r].alias >= 0) r = m->bufs[r].alias;
+    if (r == sb) m->bufs[i].ptr = p;
+  }
+  return old;
+}
+
+// One run of the step list with input 0 read from slot `slot` (0: its own buffer, 1: alt_in).
+static int launch_slot(SpinnCudaModel* m, int slot) {
+  if (slot == 0 || m->in_buf.empty()) return spinn_cuda_run_device(m, nullptr);
+  if (m->gexec_alt) {
+    SPINN_CUDA_TRY(cudaGraphLaunch(m->gexec_alt, m->stream));
+    return 0;
+  }
+  float* own = set_input0_ptr(m, reinterpret_cast<float*>(m->alt_in));  // eager mode (no graph)
+  const int rc = run_steps(m, m->stream, false);
+  set_input0_ptr(m, own);
+  return rc;
+}
+
 __attribute__((visibility("default"))) int spinn_cuda_submit(SpinnCudaModel* m, const void* input, void* output) {
   if (!m || !m->planned) {
     set_error("spinn_cuda_submit: model not planned");
     return SPINN_CUDA_ESTATE;
   }
   SPINN_CUDA_TRY(cudaSetDevice(m->device));
+  int slot = 0;
   if (input && !m->in_buf.empty()) {
     const Buf& b = m->bufs[m->in_buf[0]];
     if (!m->copy_stream) {
+      SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
       SPINN_CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
       for (int k = 0; k < 2; ++k) {
-        SPINN_CUDA_TRY(cudaMalloc(&m->staging[k], b.bytes));
         SPINN_CUDA_TRY(cudaEventCreateWithFlags(&m->in_ready[k], cudaEventDisableTiming));
         SPINN_CUDA_TRY(cudaEventCreateWithFlags(&m->in_free[k], cudaEventDisableTiming));
       }
+      SPINN_CUDA_TRY(cudaMalloc(&m->alt_in, align_up(b.bytes, 256)));
+      if (m->gexec) {  // the same step list, captured once more with input 0 at alt_in
+        float* own = set_input0_ptr(m, reinterpret_cast<float*>(m->alt_in));
+        cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+        int rc = e == cudaSuccess ? run_steps(m, m->stream, false) : 0;
+        cudaGraph_t g = nullptr;
+        if (e == cudaSuccess) e = cudaStreamEndCapture(m->stream, &g);
+        set_input0_ptr(m, own);
+        if (rc || e != cudaSuccess) {
+          if (g) cudaGraphDestroy(g);
+          if (rc) return rc;
+          SPINN_CUDA_TRY(e);
+        }
+        m->graph_alt = g;
+        SPINN_CUDA_TRY(cudaGraphInstantiate(&m->gexec_alt, g, 0));
+      }
     }
-    const int k = (int)(m->submitted & 1);
-    // the staging buffer's previous contents (two submissions back) have been consumed; an
-    // event never recorded is no wait
-    SPINN_CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->in_free[k], 0));
-    SPINN_CUDA_TRY(cudaMemcpyAsync(m->staging[k], input, b.bytes, cudaMemcpyHostToDevice, m->copy_stream));
-    SPINN_CUDA_TRY(cudaEventRecord(m->in_ready[k], m->copy_stream));
-    SPINN_CUDA_TRY(cudaStreamWaitEvent(m->stream, m->in_ready[k], 0));
-    SPINN_CUDA_TRY(cudaMemcpyAsync(b.ptr, m->staging[k], b.bytes, cudaMemcpyDeviceToDevice, m->stream));
-    SPINN_CUDA_TRY(cudaEventRecord(m->in_free[k], m->stream));
+    slot = (int)(m->submitted & 1);
+    void* dst = slot == 0 ? (void*)b.ptr : m->alt_in;
+    // the run that last read this slot (two submissions back) has finished; an event never
+    // recorded is no wait
+    SPINN_CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->in_free[slot], 0));
+    SPINN_CUDA_TRY(cudaMemcpyAsync(dst, input, b.bytes, cudaMemcpyHostToDevice, m->copy_stream));
+    SPINN_CUDA_TRY(cudaEventRecord(m->in_ready[slot], m->copy_stream));
+    SPINN_CUDA_TRY(cudaStreamWaitEvent(m->stream, m->in_ready[slot], 0));
   }
-  int rc = spinn_cuda_run_device(m, nullptr);
+  int rc = launch_slot(m, slot);
   if (rc) return rc;
+  if (input && !m->in_buf.empty()) SPINN_CUDA_TRY(cudaEventRecord(m->in_free[slot], m->stream));
   if (output && !m->out_buf.empty()) {
     const Buf& b = m->bufs[m->out_buf[0]];
     SPINN_CUDA_TRY(cudaMemcpyAsync(output, b.ptr, b.bytes, cudaMemcpyDeviceToHost, m->stream));

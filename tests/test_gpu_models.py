@@ -145,13 +145,15 @@ def test_yolo_shaped_end_to_end(cuda_lib, ref_oracle, tmp_path, batch, image):
     assert 3 in kinds and 1 in kinds  # depthwise CUDA-core kernel and tcgen05 convolutions
 
 
-def test_submit_pipeline_matches_run(cuda_lib):
+@pytest.mark.parametrize("graph", [True, False], ids=["graph", "eager"])
+def test_submit_pipeline_matches_run(cuda_lib, graph):
     """spinn_cuda_submit / spinn_cuda_wait: several different inputs in flight through the
-    two staging buffers give the same outputs as one synchronous spinn_cuda_run each."""
+    two input slots (the second read by its own captured graph, or by an eager pass) give the
+    same outputs as one synchronous spinn_cuda_run each."""
     import torch
-    from spinn_b200 import ennf, netdef, runtime
+    from spinn_b200 import ennf, lib, netdef, runtime
     g = netdef.resnet(50, batch=2, image=64, width=16, seed=9)
-    m = runtime.Model(ennf.convert(g))
+    m = runtime.Model(ennf.convert(g), flags=0 if graph else lib.PLAN_NO_GRAPH)
     xs = [netdef.resnet_input(2, image=64, seed=s) for s in range(5)]
     ref = [m.run(x).copy() for x in xs]
     ins = [torch.from_numpy(x).pin_memory() for x in xs]
