@@ -147,9 +147,10 @@ int spinn_cuda_plan(SpinnCudaModel *m, int device, uint64_t max_arena_bytes, int
 int spinn_cuda_run(SpinnCudaModel *m, const void *input, void *output);
 
 /* Pipelined runs (serving loops): spinn_cuda_submit queues one inference -- input 0 copied
- * from `input` (host, pinned for overlap) into one of two device staging buffers on a copy
- * stream, the run, output 0 copied back to `output` -- and returns without waiting, so the
- * input copy of the next submission overlaps this one's run.  `input` and `output` must stay
+ * from `input` (host, pinned for overlap) on a copy stream into one of two device input
+ * buffers (the first submission captures a second graph reading the other one), the run,
+ * output 0 copied back to `output` -- and returns without waiting, so the input copy of the
+ * next submission overlaps this one's run.  `input` and `output` must stay
  * valid and untouched until spinn_cuda_wait returns; results arrive in submission order.
  * Either pointer may be NULL (no copy).  spinn_cuda_wait blocks until every submitted run has
  * finished and reports a deferred error (a kernel's expired wait: SPINN_CUDA_ETIMEOUT). */
