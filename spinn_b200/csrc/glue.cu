@@ -25,7 +25,7 @@ inline int grid_for(long work, int threads, int max_blocks = 148 * 32) {
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == 1 || act == 5) return v < 0.0f ? 0.0f : v;
-  if (act == 3) return v / (1.0f + expf(-v));
+  if (act == 3) return silu_fast(v);
   return v;
 }
 
@@ -313,7 +313,7 @@ __global__ void unary_kernel(const float* __restrict__ x, float* __restrict__ y,
     switch (op) {
       case UN_RELU: r = v > 0.0f ? v : 0.0f; break;
       case UN_SIGMOID: r = 1.0f / (1.0f + expf(-v)); break;
-      case UN_SILU: r = v / (1.0f + expf(-v)); break;
+      case UN_SILU: r = silu_fast(v); break;
       default: r = v; break;
     }
     y[i] = r;

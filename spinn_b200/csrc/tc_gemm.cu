@@ -76,10 +76,17 @@ struct TcParams {
 // hundred cycles of issue whether it holds 128 or 256 rows (measured on B200), so for narrow
 // tiles (BN 64 / 128), whose main loop is bounded by box issue rather than by the tensor
 // pipe, this doubles the bytes per box and halves the W boxes per output.
-template <int BN, int CB, bool RES, int PAIR, int BK_, int MS_ = 1>
+//
+// WR: resident weights.  When one N tile covers all of N and W is small (the stems: 64 output
+// channels, K <= 256), the whole W matrix is loaded once per CTA into shared memory and the
+// ring carries only A boxes: half the TMA boxes per stage for the box-bound narrow tiles.
+constexpr uint32_t kWresBytes = 64 * 1024;
+template <int BN, int CB, bool RES, int PAIR, int BK_, int MS_ = 1, bool WR_ = false>
 struct Cfg {
   static constexpr int BK = BK_;
   static constexpr int MS = MS_;
+  static constexpr bool WR = WR_;
+  static constexpr uint32_t W_BYTES = WR ? kWresBytes : 0;
   static constexpr int AROWS = kBM * MS;  // A rows held by each CTA
   static constexpr int BNC = BN / PAIR;  // B rows (output channels) held by each CTA
   static constexpr int NSUB = BK / CB;   // TMA boxes per operand per stage
@@ -88,7 +95,7 @@ struct Cfg {
   static constexpr uint32_t B_SUB = BNC * CB * 4;
   static constexpr uint32_t A_STAGE = AROWS * BK * 4;
   static constexpr uint32_t B_STAGE = BNC * BK * 4;
-  static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
+  static constexpr uint32_t STAGE = A_STAGE + (WR ? 0 : B_STAGE);
   // Epilogue: groups of four warps (one per TMEM lane quarter); with two groups, group g
   // takes the 32-column chunks c with c % 2 == g.  The residual (128 rows x 32 columns per
   // slot, filled by the residual producer warp) goes through one ring per group -- a ring
@@ -106,16 +113,17 @@ struct Cfg {
   static constexpr int RES_SLOTS = RES_G * EPI_GROUPS;
   static constexpr uint32_t RES_SLOT = kBM * 32 * 4;
   static constexpr uint32_t EPI = OUT_BYTES + RES_SLOTS * RES_SLOT;
-  static constexpr int STAGES_FIT = (kSmemBudget - (int)EPI) / (int)STAGE;
+  static constexpr int STAGES_FIT = (kSmemBudget - (int)EPI - (int)W_BYTES) / (int)STAGE;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   // TMEM accumulators: all 512 columns, so narrow tiles (BN 128 / 64) get 4 / 8 buffers and
   // the MMA can run that many tiles ahead of the epilogue
   static constexpr int NACC = 512 / (BN * MS);
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t SMEM = STAGES * STAGE + EPI + 512 + 1024;
+  static constexpr uint32_t SMEM = STAGES * STAGE + W_BYTES + EPI + 512 + 1024;
   static_assert(STAGES >= 2, "pipeline needs two stages");
   static_assert(PAIR == 1 || BNC >= 64, "pair tiles split BN into halves of at least 64 rows");
   static_assert(MS == 1 || (PAIR == 1 && CB >= 16 && BN <= 128), "two M sub-tiles: narrow single-CTA tiles only");
+  static_assert(!WR || (PAIR == 1 && !RES), "resident weights: single-CTA tiles without a fused residual");
 };
 
 // Start-address offset (bytes) of the j-th 8-wide K slice of a stage, and the descriptor
@@ -160,12 +168,13 @@ __device__ __forceinline__ bool warp_wait_backoff(uint64_t* bar, uint32_t parity
 //
 // The producer and MMA warps run their loops with all 32 lanes (lane 0 issues): a single
 // diverged lane spends about half again as long per barrier handoff.
-template <int BN, int CB, int MODE, bool RES, int PAIR, int BK_, int MS_>
-__global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
+template <int BN, int CB, int MODE, bool RES, int PAIR, int BK_, int MS_, bool WR_>
+__global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapY, const __grid_constant__ CUtensorMap mapR,
                    const TcParams p) {
-  using C = Cfg<BN, CB, RES, PAIR, BK_, MS_>;
+  using C = Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>;
+  constexpr bool WR = C::WR;
   constexpr int STAGES = C::STAGES;
   constexpr int BK = C::BK;
   constexpr int MS = C::MS;
@@ -175,7 +184,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * C::A_STAGE;
-  uint8_t* sOut = sB + STAGES * C::B_STAGE;  // [OUT_BUFS][EPI_WARPS][4 KiB], 1024-aligned
+  uint8_t* sOut = sB + (WR ? C::W_BYTES : STAGES * C::B_STAGE);  // [OUT_BUFS][EPI_WARPS][4 KiB], 1024-aligned
   uint8_t* sRes = sOut + C::OUT_BYTES;       // [RES_SLOTS][16 KiB]
   uint64_t* full = reinterpret_cast<uint64_t*>(sRes + C::RES_SLOTS * C::RES_SLOT);
   uint64_t* empty = full + STAGES;
@@ -184,7 +193,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
   uint64_t* rfull = tempty + C::NACC;
   uint64_t* rempty = rfull + NRS;
   uint64_t* drain = rempty + NRS;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* wfull = drain + 1;  // resident weights landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -205,6 +215,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
       mbar_init(&rempty[r], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(wfull, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -246,6 +257,16 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
     int s = 0;
     uint32_t ph = 0;
     uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
+    // resident weights: all num_kb k-blocks of the single N tile, once, on `wfull`
+    const bool w_issued = WR && unit0 < p.num_units;
+    if (w_issued && lane == 0) {
+      mbar_arrive_expect_tx(wfull, (uint32_t)p.num_kb * C::B_STAGE);
+      for (int kb = 0; kb < p.num_kb; ++kb)
+#pragma unroll
+        for (int j = 0; j < C::NSUB; ++j)
+          tma_load_3d(&mapB, wfull, sB + kb * C::B_STAGE + j * C::B_SUB, kb * BK + j * CB, 0, 0);
+    }
+    __syncwarp();
     for (int it = 0; !warp_aborted(abort_flag); ++it) {
       const int u = take_unit(it);
       if (u < 0) break;
@@ -311,7 +332,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
             }
             if constexpr (PAIR == 2)
               tma_load_3d_pair(&mapB, bar_leader, b_dst + j * C::B_SUB, k, nb0, bzb);
-            else
+            else if constexpr (!WR)
               tma_load_3d(&mapB, &full[s], b_dst + j * C::B_SUB, k, nb0, bzb);
           }
           if (rank == 0) {
@@ -332,6 +353,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
       volatile int dummy = 0;
       for (int st = 0; st < STAGES; ++st)
         if (armed & (1u << st)) mbar_wait(&full[st], (armed_ph >> st) & 1, &dummy, kDrainNs);
+      if (w_issued) mbar_wait(wfull, 0, &dummy, kDrainNs);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -351,6 +373,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
         const uint32_t aph = (it / C::NACC) & 1;
         const int kb0 = (p.batch > 1 ? 0 : u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
         if (!warp_wait(&tempty[b], aph ^ 1, abort_flag, kTimeoutNs)) break;
+        if (WR && it == 0 && !warp_wait(wfull, 0, abort_flag, kTimeoutNs)) break;  // resident weights
         tc_fence_after();
         const uint32_t d = tmem_base + b * (BN * MS);
         bool ok = true;
@@ -361,7 +384,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
           }
           tc_fence_after();
           if (lane == 0) {
-            const uint64_t as = adesc0 + ((s * C::A_STAGE) >> 4), bs = bdesc0 + ((s * C::B_STAGE) >> 4);
+            // resident weights are indexed by the k-block, the ring by the stage
+            const uint64_t as = adesc0 + ((s * C::A_STAGE) >> 4),
+                           bs = bdesc0 + (((WR ? (uint32_t)kb : (uint32_t)s) * C::B_STAGE) >> 4);
 #pragma unroll
             for (int j = 0; j < C::KSTEPS; ++j) {
               const uint64_t ad = as + (kslice_offset<CB>(j, C::A_SUB) >> 4);
@@ -538,7 +563,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_>::THREADS, 1)
               for (int i = 0; i < 32; ++i) v[i] = v[i] < 0.0f ? 0.0f : v[i];
             } else if (p.act == 3) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = v[i] / (1.0f + expf(-v[i]));
+              for (int i = 0; i < 32; ++i) v[i] = silu_fast(v[i]);
             }
             if (p.round_out) {
 #pragma unroll
@@ -636,7 +661,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (act == 1 || act == 5) v[j] = v[j] < 0.0f ? 0.0f : v[j];
-      else if (act == 3) v[j] = v[j] / (1.0f + expf(-v[j]));
+      else if (act == 3) v[j] = silu_fast(v[j]);
       if (round_out) v[j] = round_tf32_bits(v[j]);
     }
     float* dst = y + (size_t)m * ldy + n;
@@ -678,11 +703,15 @@ int pair_clusters(K kern, uint32_t smem, int threads, int sms) {
   return n;
 }
 
-template <int BN, int CB, int MODE, bool RES, int PAIR, int BK, int MS = 1>
+template <int BN, int CB, int MODE, bool RES, int PAIR, int BK, int MS = 1, bool WR = false>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr,
                    const TcParams& p, int sms, cudaStream_t stream) {
-  using C = Cfg<BN, CB, RES, PAIR, BK, MS>;
-  auto kern = tc_gemm_kernel<BN, CB, MODE, RES, PAIR, BK, MS>;
+  using C = Cfg<BN, CB, RES, PAIR, BK, MS, WR>;
+  auto kern = tc_gemm_kernel<BN, CB, MODE, RES, PAIR, BK, MS, WR>;
+  if (WR && (p.tiles_n != 1 || (uint32_t)p.num_kb * C::B_STAGE > C::W_BYTES)) {
+    set_error("tcgen05 gemm: resident weights need one N tile and at most %u bytes of W", C::W_BYTES);
+    return SPINN_CUDA_EINVAL;
+  }
   // The opt-in shared-memory size is a per-device function attribute: set it once per device.
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -738,20 +767,24 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
 }
 
 template <int MODE, bool RES>
-int dispatch_bn_cb(int bn, int cb, int pair, int bk, int ms, const CUtensorMap& ma, const CUtensorMap& mb,
+int dispatch_bn_cb(int bn, int cb, int pair, int bk, int ms, int wr, const CUtensorMap& ma, const CUtensorMap& mb,
                    const CUtensorMap& my, const CUtensorMap& mr, const TcParams& p, int sms, cudaStream_t s) {
-#define SPINN_TC_CASE(BNV, CBV, PV, BKV)                                  \
-  if (bn == BNV && cb == CBV && pair == PV && bk == BKV && ms == 1) \
+#define SPINN_TC_CASE(BNV, CBV, PV, BKV)                                             \
+  if (bn == BNV && cb == CBV && pair == PV && bk == BKV && ms == 1 && !wr) \
     return launch_variant<BNV, CBV, MODE, RES, PV, BKV>(ma, mb, my, mr, p, sms, s);
-#define SPINN_TC_CASE2(BNV, CBV, BKV)                                    \
-  if (bn == BNV && cb == CBV && pair == 1 && bk == BKV && ms == 2) \
+#define SPINN_TC_CASE2(BNV, CBV, BKV)                                               \
+  if (bn == BNV && cb == CBV && pair == 1 && bk == BKV && ms == 2 && !wr) \
     return launch_variant<BNV, CBV, MODE, RES, 1, BKV, 2>(ma, mb, my, mr, p, sms, s);
+#define SPINN_TC_CASE2W(BNV, CBV, BKV)                                             \
+  if (bn == BNV && cb == CBV && pair == 1 && bk == BKV && ms == 2 && wr) \
+    return launch_variant<BNV, CBV, MODE, RES, 1, BKV, 2, true>(ma, mb, my, mr, p, sms, s);
   SPINN_TC_CASE(256, 32, 1, 32) SPINN_TC_CASE(128, 32, 1, 32) SPINN_TC_CASE(64, 32, 1, 32)
   SPINN_TC_CASE2(128, 32, 32) SPINN_TC_CASE2(64, 32, 32)
   if constexpr (!RES) {
     SPINN_TC_CASE(128, 32, 1, 64) SPINN_TC_CASE(64, 32, 1, 64)
     SPINN_TC_CASE(256, 32, 2, 64) SPINN_TC_CASE(128, 32, 2, 64)
     SPINN_TC_CASE2(128, 32, 64) SPINN_TC_CASE2(64, 32, 64)
+    SPINN_TC_CASE2W(64, 32, 32) SPINN_TC_CASE2W(64, 32, 64)
   }
   if constexpr (MODE == kIm2col) {
     SPINN_TC_CASE(256, 16, 1, 32) SPINN_TC_CASE(128, 16, 1, 32) SPINN_TC_CASE(64, 16, 1, 32)
@@ -762,11 +795,14 @@ int dispatch_bn_cb(int bn, int cb, int pair, int bk, int ms, const CUtensorMap& 
       SPINN_TC_CASE(128, 16, 1, 64) SPINN_TC_CASE(64, 16, 1, 64)
       SPINN_TC_CASE(256, 16, 2, 64) SPINN_TC_CASE(128, 16, 2, 64)
       SPINN_TC_CASE2(128, 16, 64) SPINN_TC_CASE2(64, 16, 64)
+      SPINN_TC_CASE2W(64, 16, 32) SPINN_TC_CASE2W(64, 16, 64)
     }
   }
 #undef SPINN_TC_CASE
 #undef SPINN_TC_CASE2
-  set_error("tcgen05 gemm: no variant for BN=%d CB=%d pair=%d BK=%d MS=%d mode=%d", bn, cb, pair, bk, ms, MODE);
+#undef SPINN_TC_CASE2W
+  set_error("tcgen05 gemm: no variant for BN=%d CB=%d pair=%d BK=%d MS=%d WR=%d mode=%d", bn, cb, pair, bk, ms, wr,
+            MODE);
   return SPINN_CUDA_EUNSUPPORTED;
 }
 
@@ -799,22 +835,25 @@ struct TilePlan {
   int bn = 256;
   int pair = 1;  // 2: CTA pairs with 256-row tiles (cta_group::2)
   int ms = 1;    // 2: one CTA, 256-row tiles as two 128-row sub-tiles
+  int wr = 0;    // 1: W resident in shared memory (one N tile, small K)
   int bk = 32;   // K depth of a pipeline stage
   int ksplit = 1;
   int kb_per = 1;
   size_t ws_bytes = 0;
 };
 
-// Optional override for tuning sweeps: SPINN_TC_TILES="bn,ksplit[,pair[,bk[,ms]]]" (read at
-// each launch; a captured graph keeps the choice made when it was captured).
-void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms) {
+// Optional override for tuning sweeps: SPINN_TC_TILES="bn,ksplit[,pair[,bk[,ms[,wr]]]]" (read
+// at each launch; a captured graph keeps the choice made when it was captured; wr: -1 = no,
+// 1 = yes, 0 = planner's choice).
+void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms, int* wr) {
   *bn = -1;
   *ks = 0;
   *pair = 0;
   *bk = 0;
   *ms = 0;
+  *wr = 0;
   const char* e = getenv("SPINN_TC_TILES");
-  if (e && sscanf(e, "%d,%d,%d,%d,%d", bn, ks, pair, bk, ms) < 1) *bn = -1;
+  if (e && sscanf(e, "%d,%d,%d,%d,%d,%d", bn, ks, pair, bk, ms, wr) < 1) *bn = -1;
 }
 
 // Chooses the tile shape (BN, single CTA or CTA pair, stage depth) and the K split from a
@@ -829,18 +868,23 @@ void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms) {
 // boxes, one W box per two MMAs) pay off.  A split adds the finish pass: (ksplit + 2) x M x N
 // floats at 8 TB/s (the partials are L2-resident).  64-deep stages and sub-tiles need channel
 // blocks of 16 or 32 and no fused residual (the residual ring would leave too few stages).
-TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t ws_limit, int force_bn) {
-  int fbn, fks, fpair, fbk, fms;
-  forced_tiles(&fbn, &fks, &fpair, &fbk, &fms);
+TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t ws_limit, int force_bn,
+                    bool allow_wr) {
+  int fbn, fks, fpair, fbk, fms, fwr;
+  forced_tiles(&fbn, &fks, &fpair, &fbk, &fms, &fwr);
   if (force_bn <= 0 && (fbn == 64 || fbn == 128 || fbn == 256)) force_bn = fbn;
   struct Shape {
-    int bn, pair, bk, ms;
+    int bn, pair, bk, ms, wr;
     double per_stage;
   };
-  const Shape shapes[11] = {{256, 1, 32, 1, 0.332}, {128, 1, 32, 1, 0.266}, {64, 1, 32, 1, 0.237},
-                            {128, 1, 64, 1, 0.405}, {64, 1, 64, 1, 0.319},  {256, 2, 64, 1, 0.617},
-                            {128, 2, 64, 1, 0.456}, {128, 1, 32, 2, 0.46},  {64, 1, 32, 2, 0.38},
-                            {128, 1, 64, 2, 0.86},  {64, 1, 64, 2, 0.67}};
+  // Resident-weight shapes come first: when the epilogue term dominates a narrow tile both
+  // kinds cost the same in the model, and the measured stems favour resident weights
+  // (the 3->16-channel 640x640 stem at batch 32: 121 vs 199 us).
+  const Shape shapes[13] = {{64, 1, 64, 2, 1, 0.45},   {64, 1, 32, 2, 1, 0.25},   {256, 1, 32, 1, 0, 0.332},
+                            {128, 1, 32, 1, 0, 0.266}, {64, 1, 32, 1, 0, 0.237},  {128, 1, 64, 1, 0, 0.405},
+                            {64, 1, 64, 1, 0, 0.319},  {256, 2, 64, 1, 0, 0.617}, {128, 2, 64, 1, 0, 0.456},
+                            {128, 1, 32, 2, 0, 0.46},  {64, 1, 32, 2, 0, 0.38},   {128, 1, 64, 2, 0, 0.86},
+                            {64, 1, 64, 2, 0, 0.67}};
   const size_t ldw = (size_t)((N + 3) & ~3);
   TilePlan best;
   double best_cost = 1e300;
@@ -850,6 +894,11 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
     if (fpair > 0 && sh.pair != fpair) continue;
     if (fbk > 0 && sh.bk != fbk) continue;
     if (fms > 0 && sh.ms != fms) continue;
+    if ((fwr > 0 && !sh.wr) || (fwr < 0 && sh.wr)) continue;
+    // resident weights: one N tile, all of W within the resident region, no residual
+    if (sh.wr && (!allow_wr || has_res || N > sh.bn || (cb != 32 && cb != 16) ||
+                  (size_t)((K + sh.bk - 1) / sh.bk) * sh.bn * sh.bk * 4 > kWresBytes))
+      continue;
     if (sh.bk == 64 && ((cb != 32 && cb != 16) || has_res)) continue;
     // sub-tiles with a fused residual: correct (forced shapes) but measured no faster than
     // 256-wide single tiles, and the model cannot tell them apart, so not chosen by default
@@ -880,6 +929,7 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
         best.pair = sh.pair;
         best.bk = sh.bk;
         best.ms = sh.ms;
+        best.wr = sh.wr;
         best.ksplit = ks;
         best.kb_per = kb_per;
         best.ws_bytes = ws;
@@ -891,6 +941,7 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
     best.pair = 1;
     best.bk = 32;
     best.ms = 1;
+    best.wr = 0;
     best.ksplit = 1;
     best.kb_per = (K + 31) / 32;
     best.ws_bytes = 0;
@@ -907,7 +958,8 @@ size_t tc_gemm_workspace_bytes(const TcGemmArgs& a) {
   if (!tc_gemm_supported(a, nullptr) || a.batch > 1) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  return plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), kWsCap, a.bn).ws_bytes;
+  return plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), kWsCap, a.bn, true)
+      .ws_bytes;
 }
 
 bool tc_gemm_supported(const TcGemmArgs& a, std::string* why) {
@@ -960,7 +1012,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     return SPINN_CUDA_EINVAL;
   }
   const size_t ws_limit = (a.ws && a.batch == 1) ? std::min(a.ws_bytes, kWsCap) : 0;  // batched: no split
-  const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn);
+  const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn, a.batch == 1);
   const int arows = kBM * tp.ms;  // A rows per box
   CUtensorMap ma, mb, my, mr;
   int rc;
@@ -1033,13 +1085,13 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   p.alpha = a.alpha;
   p.bias = a.bias;
   p.err = a.err ? a.err : device_error_flag(dev);
-  const int pr = tp.pair, ms = tp.ms;
+  const int pr = tp.pair, ms = tp.ms, wr = tp.wr;
   if (a.a_mode == 0)
-    rc = p.has_res ? dispatch_bn_cb<kIm2col, true>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream)
-                   : dispatch_bn_cb<kIm2col, false>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream);
+    rc = p.has_res ? dispatch_bn_cb<kIm2col, true>(bn, cb, pr, tp.bk, ms, wr, ma, mb, my, mr, p, sms, stream)
+                   : dispatch_bn_cb<kIm2col, false>(bn, cb, pr, tp.bk, ms, wr, ma, mb, my, mr, p, sms, stream);
   else
-    rc = p.has_res ? dispatch_bn_cb<kTiled, true>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream)
-                   : dispatch_bn_cb<kTiled, false>(bn, cb, pr, tp.bk, ms, ma, mb, my, mr, p, sms, stream);
+    rc = p.has_res ? dispatch_bn_cb<kTiled, true>(bn, cb, pr, tp.bk, ms, wr, ma, mb, my, mr, p, sms, stream)
+                   : dispatch_bn_cb<kTiled, false>(bn, cb, pr, tp.bk, ms, wr, ma, mb, my, mr, p, sms, stream);
   if (rc || !split) return rc;
   const long groups = (long)a.M * ((a.N + 3) / 4);
   const int fgrid = (int)std::min<long>((groups + 255) / 256, (long)sms * 8);

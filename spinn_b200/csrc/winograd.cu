@@ -141,7 +141,7 @@ __global__ void wino_output_kernel(const float* __restrict__ m, const float* __r
         if (act == 1 || act == 5)
           v = v < 0.0f ? 0.0f : v;
         else if (act == 3)
-          v = v / (1.0f + expf(-v));
+          v = silu_fast(v);
         y[idx] = round_out ? to_tf32_rna(v) : v;
       }
   }

@@ -37,6 +37,8 @@ CONV_CASES = [
     (3, 512, 7, 7, 2048, 1, 1, 0, 1, 3, True, False),    # split-K, SiLU applied after the reduction
     (1, 32, 40, 40, 32, 3, 1, 1, 32, 3, True, False),    # depthwise (CUDA cores)
     (1, 32, 10, 10, 64, 3, 1, 1, 4, 1, True, False),     # grouped (CUDA cores)
+    (2, 16, 20, 20, 64, 3, 1, 1, 1, 1, True, False),     # C=16, N=64, K=144: resident-weight shapes fit
+    (2, 64, 9, 11, 40, 1, 1, 0, 1, 3, True, False),      # 1x1, N=40 < 64, K=64, ragged everything
 ]
 
 
@@ -148,10 +150,12 @@ def test_split_k_is_deterministic(cuda_lib):
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
 
 
-# bn,ksplit,pair[,bk,ms]: CTA pairs (cta_group::2) and single CTAs with two 128-row M sub-tiles,
-# each with and without split-K
+# bn,ksplit,pair[,bk,ms[,wr]]: CTA pairs (cta_group::2), single CTAs with two 128-row M sub-tiles
+# and the same with resident weights (wr=1; where infeasible the planner falls back), each with
+# and without split-K
 PAIR_SHAPES = ["256,1,2", "128,1,2", "256,3,2", "128,2,2",
-               "64,1,1,32,2", "128,1,1,64,2", "64,2,1,64,2", "128,3,1,32,2"]
+               "64,1,1,32,2", "128,1,1,64,2", "64,2,1,64,2", "128,3,1,32,2",
+               "64,1,1,32,2,1", "64,1,1,64,2,1", "64,2,1,32,2,1"]
 TC_CASES = [c for c in CONV_CASES if c[8] == 1]
 
 
