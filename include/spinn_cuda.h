@@ -73,6 +73,12 @@ int spinn_cuda_init(int device, size_t scratch_bytes);
 /* Waits for all work queued by this thread's session; returns the first deferred error. */
 int spinn_cuda_sync(void);
 
+/* Diagnostic: runs a one-thread kernel whose bounded mbarrier wait -- the primitive every
+ * tcgen05 kernel waits with -- expires after timeout_ns (at most 1 s), and reports it.  Returns
+ * SPINN_CUDA_ETIMEOUT when the expiry was detected and cleared (the expected result); the
+ * context stays usable. */
+int spinn_cuda_selftest_wait_expiry(uint64_t timeout_ns);
+
 /* Releases the calling thread's session (stream, scratch, cached weights). */
 void spinn_cuda_shutdown(void);
 

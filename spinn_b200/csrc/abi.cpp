@@ -311,6 +311,16 @@ __attribute__((visibility("default"))) int spinn_cuda_sync(void) {
   return check_device_error_flag(S.device, S.stream);
 }
 
+__attribute__((visibility("default"))) int spinn_cuda_selftest_wait_expiry(uint64_t timeout_ns) {
+  int rc = ensure_session();
+  if (rc) return rc;
+  Session& S = g_sess;
+  rc = launch_wait_expiry_selftest(device_error_flag(S.device), timeout_ns, S.stream);
+  if (rc) return rc;
+  SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));
+  return check_device_error_flag(S.device, S.stream);
+}
+
 __attribute__((visibility("default"))) void spinn_cuda_shutdown(void) {
   Session& S = g_sess;
   if (!S.ready) return;

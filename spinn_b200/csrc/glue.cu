@@ -178,6 +178,21 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool3s2_tile_kernel(const flo
   }
 }
 
+// Self-test of the bounded-wait path every tcgen05 kernel relies on: one thread waits on an
+// mbarrier that nothing arrives at, with the same mbar_wait the GEMM uses, gives up after
+// `timeout_ns` and raises the device error flag (code 2).  Nothing faults or hangs.
+__global__ void wait_expiry_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ volatile int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait(&bar, 0, &abort_flag, timeout_ns)) atomicExch(err, 2);
+}
+
 // TopK (SPINN/run_time/ops/tensor/topk.c:20-87): for every row of the last axis, the k largest
 // values in descending order and their int64 indices.  One CTA sorts a row in shared memory
 // (bitonic network over 64-bit keys: order-preserving bits of the value, inverted, above the
@@ -577,6 +592,13 @@ int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad,
     maxpool_nhwc_kernel<long><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
         reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow, kh, kw, sh, sw, ph,
         pw);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_wait_expiry_selftest(int* err, uint64_t timeout_ns, cudaStream_t s) {
+  SPINN_CHECK_ARG(err != nullptr && timeout_ns > 0 && timeout_ns <= 1000000000ull,
+                  "wait self-test: timeout %llu ns outside (0, 1 s]", (unsigned long long)timeout_ns);
+  wait_expiry_kernel<<<1, 32, 0, s>>>(err, (unsigned long long)timeout_ns);
   SPINN_LAUNCH_CHECK();
 }
 

@@ -54,6 +54,8 @@ int sm_count(int device);
 int* device_error_flag(int device);
 // Reads and clears the flag; SPINN_CUDA_ETIMEOUT if it was set.
 int check_device_error_flag(int device, cudaStream_t stream);
+// One-thread kernel whose mbarrier wait expires after timeout_ns (<= 1 s) and raises *err.
+int launch_wait_expiry_selftest(int* err, uint64_t timeout_ns, cudaStream_t s);
 
 // ------------------------------------------------------------------ tcgen05 GEMM / conv
 // Y[M][ldy] = epilogue( A * W^T ), W stored K-major [N][kpad].
