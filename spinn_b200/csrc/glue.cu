@@ -346,15 +346,17 @@ __global__ void channel_affine_kernel(const float* __restrict__ x, float* __rest
 }
 
 // Depthwise convolution, NHWC, four channels per thread (16-B loads along C).
-// w is [kh*kw][cpad]; bias [cpad]; residual NHWC like y.
+// w is [kh*kw][cpad]; bias [cpad]; residual NHWC like y.  Idx = int when the element count
+// fits: the 64-bit divisions of the index decomposition would otherwise dominate.
+template <typename Idx>
 __global__ void depthwise_kernel(const float4* __restrict__ x, const float4* __restrict__ w,
                                  const float4* __restrict__ bias, const float4* __restrict__ res,
                                  float4* __restrict__ y, int n, int h, int wd, int c4, int oh, int ow, int kh, int kw,
                                  int sh, int sw, int ph, int pw, int dh, int dw, int act, int round_out) {
-  const long total = (long)n * oh * ow * c4;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+  const Idx total = (Idx)n * oh * ow * c4;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
     const int cq = (int)(i % c4);
-    long t = i / c4;
+    Idx t = i / c4;
     const int ox = (int)(t % ow);
     t /= ow;
     const int oy = (int)(t % oh);
@@ -441,12 +443,13 @@ __global__ void grouped_kernel(const float* __restrict__ x, const float* __restr
   }
 }
 
+template <typename Idx>
 __global__ void resize_nearest_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
                                       int c4, int oh, int ow) {
-  const long total = (long)n * oh * ow * c4;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+  const Idx total = (Idx)n * oh * ow * c4;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
     const int cq = (int)(i % c4);
-    long t = i / c4;
+    Idx t = i / c4;
     const int ox = (int)(t % ow);
     t /= ow;
     const int oy = (int)(t % oh);
@@ -681,10 +684,17 @@ int launch_depthwise_nhwc(const float* x, const float* w, const float* bias, con
                           int dw, int act, int round_out, cudaStream_t s) {
   SPINN_CHECK_ARG(cpad % 4 == 0, "depthwise: channel stride %d not a multiple of 4", cpad);
   const long work = (long)n * oh * ow * (cpad / 4);
-  depthwise_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
-      reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(w), reinterpret_cast<const float4*>(bias),
-      reinterpret_cast<const float4*>(res), reinterpret_cast<float4*>(y), n, h, wd, cpad / 4, oh, ow, kh, kw, sh, sw, ph,
-      pw, dh, dw, act, round_out);
+  const long span = (long)grid_for(work, kEltThreads) * kEltThreads;  // the loop index reaches work + span
+  if (work < (1l << 31) - span)
+    depthwise_kernel<int><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(w), reinterpret_cast<const float4*>(bias),
+        reinterpret_cast<const float4*>(res), reinterpret_cast<float4*>(y), n, h, wd, cpad / 4, oh, ow, kh, kw, sh, sw,
+        ph, pw, dh, dw, act, round_out);
+  else
+    depthwise_kernel<long><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(w), reinterpret_cast<const float4*>(bias),
+        reinterpret_cast<const float4*>(res), reinterpret_cast<float4*>(y), n, h, wd, cpad / 4, oh, ow, kh, kw, sh, sw,
+        ph, pw, dh, dw, act, round_out);
   SPINN_LAUNCH_CHECK();
 }
 
@@ -703,8 +713,13 @@ int launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, in
                                cudaStream_t s) {
   SPINN_CHECK_ARG(cpad % 4 == 0, "resize: channel stride %d not a multiple of 4", cpad);
   const long work = (long)n * oh * ow * (cpad / 4);
-  resize_nearest_kernel<<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
-      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow);
+  const long span = (long)grid_for(work, kEltThreads) * kEltThreads;  // the loop index reaches work + span
+  if (work < (1l << 31) - span)
+    resize_nearest_kernel<int><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow);
+  else
+    resize_nearest_kernel<long><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow);
   SPINN_LAUNCH_CHECK();
 }
 
