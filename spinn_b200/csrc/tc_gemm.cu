@@ -11,8 +11,9 @@
 //
 // Structure (one persistent CTA per SM, 384 threads):
 //   warp 0      TMA producer: STAGES-deep ring of (A 128xBK, W BNxBK) tiles in shared memory
-//   warp 1      MMA issuer: BK/8 x tcgen05.mma (128 x BN x 8) per stage into TMEM
-//   warp 2      TMEM allocator (2 accumulators x BN columns)
+//               (resident-weight variants: W loaded once, the ring carries A only)
+//   warp 1      MMA issuer: BK/8 x tcgen05.mma (128 x BN x 8) per stage and M sub-tile into TMEM
+//   warp 2      TMEM allocator (all 512 columns)
 //   warp 3      residual producer (fused residual variants)
 //   warps 4..11 epilogue: tcgen05.ld -> bias / residual / activation / tf32 rounding ->
 //               swizzled shared staging -> TMA store; warps w and w+4 share the 32
