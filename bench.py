@@ -18,6 +18,9 @@ forward pass of every rank's shard.  Rank 0 prints one JSON line:
             synchronous spinn_cuda_run (copy, run, copy back, one after another).
 * roofline  the tcgen05 convolution kernel: algorithmic conv FLOPs / its device time, both
             taken from one profiled replay (CUDA events between the graph's kernels).
+            `layer_roofline` adds the per-layer view of the same replay: every convolution's
+            floor is max(FLOPs / tf32 peak, algorithmic bytes / copy bandwidth), and `frac`
+            is the sum of the floors over the measured convolution time.
 * cpu_baseline  the reference's own CPU runtime (oracle/_ref, built unmodified from the
             reference sources, epilogue fixed) on a bounded sample, rank 0 at N=1 only.
 
@@ -142,6 +145,37 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def layer_roofline(img: bytes, prof, kinds, tf32_tflops: float, hbm_gbs: float):
+    """Per-layer roofline of the convolutions of one profiled replay.  Each layer's floor is
+    the larger of its algorithmic FLOPs at the tf32 peak and its algorithmic bytes (input,
+    weights, output and fused residual, each touched once) at the copy bandwidth; `frac` is
+    the sum of the floors over the measured convolution time."""
+    from spinn_b200 import ennf
+    em = ennf.read(img)
+    convs = [n for n in em.nodes if n.op_type == ennf.OP["Conv"]]
+    steps = [(ms, fl) for (op, ms, fl), k in zip(prof, kinds) if k == 1]
+    if len(convs) != len(steps):
+        return None
+    floor = conv_ms = 0.0
+    n_tensor = n_hbm = 0
+    for n, (ms, fl) in zip(convs, steps):
+        dims = [em.tensors[t].dims for t in (n.inputs[0], n.inputs[1], n.outputs[0])]
+        x, w, y = (float(np.prod(d)) for d in dims)
+        res = ennf.ConvParams.unpack(n.params).fused_act in (4, 5)
+        byts = 4.0 * (x + w + y * (2 if res else 1))
+        t_c = fl / (tf32_tflops * 1e12) * 1e3
+        t_m = byts / (hbm_gbs * 1e9) * 1e3
+        floor += max(t_c, t_m)
+        conv_ms += ms
+        if t_c >= t_m:
+            n_tensor += 1
+        else:
+            n_hbm += 1
+    return {"floor_ms": floor, "conv_ms": conv_ms, "frac": floor / conv_ms if conv_ms > 0 else None,
+            "tensor_bound_layers": n_tensor, "hbm_bound_layers": n_hbm,
+            "peaks": {"tf32_tflops": tf32_tflops, "hbm_gbs": hbm_gbs}}
 
 
 def build_model_image(batch: int, depth: int):
@@ -328,6 +362,7 @@ def main():
 
     peaks, peak_src = measured_peaks()
     tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    layers = layer_roofline(img, prof, kinds, tf32_peak, peaks["hbm_gbs"])
     achieved = conv_fl / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
 
     cpu = None
@@ -359,6 +394,7 @@ def main():
                          "launches_per_step": conv_launches,
                          "flops_per_launch_avg": conv_fl / max(conv_launches, 1),
                          "ms_per_launch_avg": conv_ms / max(conv_launches, 1)},
+            "layer_roofline": layers,
             "model_tflops": flops_per_step * world / (dev_ms_max / args.steps / 1e3) / 1e12,
             "breakdown_ms_per_step": breakdown,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(in_bytes) * world,
