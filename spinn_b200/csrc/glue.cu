@@ -257,6 +257,26 @@ __global__ void copy_rows_kernel(const float* __restrict__ src, int src_ld, floa
   }
 }
 
+// Concat of up to kCatMaxParts parts along the last (row-contiguous) axis in one launch: one
+// thread per float4 of a destination row finds its part by offset; the destination's pad lanes
+// past the last part are written as zeros.  Offsets and widths are multiples of 4 floats.
+template <typename Idx>
+__global__ void concat_rows_kernel(CatParts parts, float* __restrict__ dst, int dst_ld, Idx rows, int fill_to) {
+  const int q = fill_to / 4;
+  const Idx total = rows * q;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
+    const Idx r = i / q;
+    const int c = (int)(i - r * q) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < kCatMaxParts; ++k) {
+      if (k < parts.n && c >= parts.off[k] && c < parts.off[k] + parts.width[k])
+        v = __ldg(reinterpret_cast<const float4*>(parts.src[k] + (size_t)r * parts.ld[k] + (c - parts.off[k])));
+    }
+    *reinterpret_cast<float4*>(dst + (size_t)r * dst_ld + c) = v;
+  }
+}
+
 // AveragePool (SPINN/run_time/ops/pool/avgpool.c): divisor = window taps inside the image,
 // or the full window when count_include_pad.
 __global__ void avgpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
@@ -643,6 +663,25 @@ int launch_copy_rows(const float* src, int src_ld, float* dst, int dst_ld, long 
     copy_rows_kernel<1, int><<<grid, kEltThreads, 0, s>>>(src, src_ld, dst, dst_ld, (int)rows, width, fill_to);
   else
     copy_rows_kernel<1, long><<<grid, kEltThreads, 0, s>>>(src, src_ld, dst, dst_ld, rows, width, fill_to);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_concat_rows(const CatParts& parts, float* dst, int dst_ld, long rows, int fill_to, cudaStream_t s) {
+  SPINN_CHECK_ARG(parts.n >= 1 && parts.n <= kCatMaxParts && fill_to % 4 == 0 && dst_ld >= fill_to && dst_ld % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(dst) & 15) == 0,
+                  "concat_rows: %d parts, fill %d, ld %d", parts.n, fill_to, dst_ld);
+  for (int k = 0; k < parts.n; ++k)
+    SPINN_CHECK_ARG(parts.off[k] % 4 == 0 && parts.width[k] % 4 == 0 && parts.ld[k] % 4 == 0 &&
+                        parts.ld[k] >= parts.width[k] && parts.off[k] + parts.width[k] <= fill_to &&
+                        (reinterpret_cast<uintptr_t>(parts.src[k]) & 15) == 0,
+                    "concat_rows: part %d misaligned", k);
+  if (rows == 0 || fill_to == 0) return 0;
+  const long work = rows * (fill_to / 4);
+  const int grid = grid_for(work, kEltThreads);
+  if (work < (1l << 31) - (long)grid * kEltThreads)
+    concat_rows_kernel<int><<<grid, kEltThreads, 0, s>>>(parts, dst, dst_ld, (int)rows, fill_to);
+  else
+    concat_rows_kernel<long><<<grid, kEltThreads, 0, s>>>(parts, dst, dst_ld, rows, fill_to);
   SPINN_LAUNCH_CHECK();
 }
 

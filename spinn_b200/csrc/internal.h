@@ -177,6 +177,14 @@ int launch_split_tf32(const float* src, float* dst, long rows, int cols, int src
 // dst[r][0..fill_to) = src[r][0..width) followed by zeros, for r < rows (pitches in floats).
 int launch_copy_rows(const float* src, int src_ld, float* dst, int dst_ld, long rows, int width, int fill_to,
                      cudaStream_t s);
+// Concat parts along the row-contiguous axis in one launch (offsets, widths multiples of 4).
+constexpr int kCatMaxParts = 8;
+struct CatParts {
+  int n;
+  const float* src[kCatMaxParts];
+  int ld[kCatMaxParts], off[kCatMaxParts], width[kCatMaxParts];
+};
+int launch_concat_rows(const CatParts& parts, float* dst, int dst_ld, long rows, int fill_to, cudaStream_t s);
 // TopK over the last axis of a row-major [rows][n] tensor (n <= kTopkMaxN): k largest values
 // (descending, ties by ascending index) and their int64 indices, each [rows][k].
 constexpr int kTopkMaxN = 16384;

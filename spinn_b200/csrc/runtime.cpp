@@ -1141,6 +1141,23 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             int off = 0;
             const long rows = nhwc ? (long)w->n * w->h * w->w : outer;
             const int wld = nhwc ? w->cpad : (int)(w->bytes / 4 / outer);
+            if (is_cat && (int)pp.size() <= kCatMaxParts && wld % 4 == 0) {
+              // float4-aligned parts: the whole destination row in one launch
+              CatParts cp{};
+              cp.n = (int)pp.size();
+              bool ok = true;
+              for (size_t i = 0; i < pp.size(); ++i) {
+                const int width = nhwc ? sizes[i] : (int)(sizes[i] * inner);
+                cp.src[i] = pp[i]->ptr;
+                cp.ld[i] = nhwc ? pp[i]->cpad : width;
+                cp.off[i] = off;
+                cp.width[i] = width;
+                ok &= width % 4 == 0 && off % 4 == 0 && cp.ld[i] % 4 == 0;
+                off += width;
+              }
+              if (ok) return launch_concat_rows(cp, w->ptr, wld, rows, wld, st);
+              off = 0;
+            }
             for (size_t i = 0; i < pp.size(); ++i) {
               const Buf* p = pp[i];
               const int width = nhwc ? sizes[i] : (int)(sizes[i] * inner);

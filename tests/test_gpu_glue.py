@@ -111,3 +111,14 @@ def test_maxpool_3x3_s2(cuda_lib, ref_oracle, tmp_path, shape):
     g.mark_output(y)
     out, ref = _run_both(ref_oracle, tmp_path, g, xv)
     assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
+
+
+def test_concat_aligned_parts_one_launch(cuda_lib, ref_oracle, tmp_path):
+    """NHWC channel concat whose parts are all multiples of 4 channels (the one-launch path),
+    five parts, the destination's channel count padded to a multiple of 4 by nothing."""
+    g, b, x, xv = _builder((2, 8, 9, 7))
+    parts = [b.conv_bn(x, c, 1, 1) for c in (8, 16, 4, 12, 8)]
+    y = b.conv_bn(b.concat(parts), 12, 3, 1)
+    g.mark_output(y)
+    out, ref = _run_both(ref_oracle, tmp_path, g, xv)
+    assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
