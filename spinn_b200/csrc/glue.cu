@@ -277,6 +277,23 @@ __global__ void concat_rows_kernel(CatParts parts, float* __restrict__ dst, int 
   }
 }
 
+// The inverse: one thread per float4 of a source row writes it to the part that owns it.
+template <typename Idx>
+__global__ void split_rows_kernel(SplitParts parts, const float* __restrict__ src, int src_ld, Idx rows, int width) {
+  const int q = width / 4;
+  const Idx total = rows * q;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
+    const Idx r = i / q;
+    const int c = (int)(i - r * q) * 4;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(src + (size_t)r * src_ld + c));
+#pragma unroll
+    for (int k = 0; k < kCatMaxParts; ++k) {
+      if (k < parts.n && c >= parts.off[k] && c < parts.off[k] + parts.width[k])
+        *reinterpret_cast<float4*>(parts.dst[k] + (size_t)r * parts.ld[k] + (c - parts.off[k])) = v;
+    }
+  }
+}
+
 // AveragePool (SPINN/run_time/ops/pool/avgpool.c): divisor = window taps inside the image,
 // or the full window when count_include_pad.
 __global__ void avgpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
@@ -682,6 +699,27 @@ int launch_concat_rows(const CatParts& parts, float* dst, int dst_ld, long rows,
     concat_rows_kernel<int><<<grid, kEltThreads, 0, s>>>(parts, dst, dst_ld, (int)rows, fill_to);
   else
     concat_rows_kernel<long><<<grid, kEltThreads, 0, s>>>(parts, dst, dst_ld, rows, fill_to);
+  SPINN_LAUNCH_CHECK();
+}
+
+int launch_split_rows(const SplitParts& parts, const float* src, int src_ld, long rows, cudaStream_t s) {
+  SPINN_CHECK_ARG(parts.n >= 1 && parts.n <= kCatMaxParts && src_ld % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0,
+                  "split_rows: %d parts, ld %d", parts.n, src_ld);
+  int width = 0;
+  for (int k = 0; k < parts.n; ++k) {
+    SPINN_CHECK_ARG(parts.off[k] == width && parts.width[k] % 4 == 0 && parts.ld[k] == parts.width[k] &&
+                        (reinterpret_cast<uintptr_t>(parts.dst[k]) & 15) == 0,
+                    "split_rows: part %d not dense and float4-aligned", k);
+    width += parts.width[k];
+  }
+  SPINN_CHECK_ARG(width <= src_ld, "split_rows: parts wider than the source row");
+  if (rows == 0 || width == 0) return 0;
+  const long work = rows * (width / 4);
+  const int grid = grid_for(work, kEltThreads);
+  if (work < (1l << 31) - (long)grid * kEltThreads)
+    split_rows_kernel<int><<<grid, kEltThreads, 0, s>>>(parts, src, src_ld, (int)rows, width);
+  else
+    split_rows_kernel<long><<<grid, kEltThreads, 0, s>>>(parts, src, src_ld, rows, width);
   SPINN_LAUNCH_CHECK();
 }
 

@@ -185,6 +185,14 @@ struct CatParts {
   int ld[kCatMaxParts], off[kCatMaxParts], width[kCatMaxParts];
 };
 int launch_concat_rows(const CatParts& parts, float* dst, int dst_ld, long rows, int fill_to, cudaStream_t s);
+// Split of a row-contiguous axis into dense parts (each part's pitch = its width, widths
+// multiples of 4, consecutive offsets) in one launch.
+struct SplitParts {
+  int n;
+  float* dst[kCatMaxParts];
+  int ld[kCatMaxParts], off[kCatMaxParts], width[kCatMaxParts];
+};
+int launch_split_rows(const SplitParts& parts, const float* src, int src_ld, long rows, cudaStream_t s);
 // TopK over the last axis of a row-major [rows][n] tensor (n <= kTopkMaxN): k largest values
 // (descending, ties by ascending index) and their int64 indices, each [rows][k].
 constexpr int kTopkMaxN = 16384;

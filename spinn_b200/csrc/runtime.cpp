@@ -1158,6 +1158,24 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
               if (ok) return launch_concat_rows(cp, w->ptr, wld, rows, wld, st);
               off = 0;
             }
+            if (!is_cat && (int)pp.size() <= kCatMaxParts && wld % 4 == 0) {
+              // dense float4-aligned parts (no pad lanes to zero): one launch
+              SplitParts sp{};
+              sp.n = (int)pp.size();
+              bool ok = true;
+              for (size_t i = 0; i < pp.size(); ++i) {
+                const int width = nhwc ? sizes[i] : (int)(sizes[i] * inner);
+                const int pld = nhwc ? pp[i]->cpad : width;
+                sp.dst[i] = pp[i]->ptr;
+                sp.ld[i] = pld;
+                sp.off[i] = off;
+                sp.width[i] = width;
+                ok &= width % 4 == 0 && pld == width;
+                off += width;
+              }
+              if (ok) return launch_split_rows(sp, w->ptr, wld, rows, st);
+              off = 0;
+            }
             for (size_t i = 0; i < pp.size(); ++i) {
               const Buf* p = pp[i];
               const int width = nhwc ? sizes[i] : (int)(sizes[i] * inner);
