@@ -1,0 +1,35 @@
+"""bench.py's host-side helpers (no GPU): the per-layer roofline classification."""
+import importlib.util
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_layer_roofline_floors():
+    from spinn_b200 import ennf, netdef
+    bench = _bench()
+    g = netdef.conv_bn_proj_add_relu(batch=4, c=16, hw=8, oc=32)[0]
+    img = ennf.convert(g)
+    m = ennf.read(img)
+    convs = [n for n in m.nodes if n.op_type == ennf.OP["Conv"]]
+    assert len(convs) == 2
+    fl = 2.0 * 4 * 32 * 8 * 8 * 16  # 1x1 16 -> 32 at 8x8, batch 4
+    prof = [(60, 0.010, fl), (60, 0.020, fl)]
+    r = bench.layer_roofline(img, prof, [1, 1], tf32_tflops=100.0, hbm_gbs=1000.0)
+    # bytes: x 4*16*64, w 32*16, y 4*32*64 (+ the residual for the second conv), 4 B each
+    x, w, y = 4 * 16 * 64, 32 * 16, 4 * 32 * 64
+    floors = [max(fl / 100e12, 4.0 * (x + w + y) / 1e12) * 1e3,
+              max(fl / 100e12, 4.0 * (x + w + 2 * y) / 1e12) * 1e3]
+    assert np.isclose(r["floor_ms"], sum(floors))
+    assert np.isclose(r["conv_ms"], 0.030)
+    assert r["hbm_bound_layers"] == 2 and r["tensor_bound_layers"] == 0
+    assert bench.layer_roofline(img, prof[:1], [1], 100.0, 1000.0) is None  # step/node mismatch
