@@ -167,3 +167,21 @@ def test_submit_pipeline_matches_run(cuda_lib, graph):
         for r, o in zip(ref, outs):
             assert np.array_equal(o.numpy(), r)
     m.close()
+
+
+@pytest.mark.parametrize("case", [(2, 224, 64, 7, 3, "Relu"), (3, 96, 64, 7, 3, "Relu"), (2, 64, 16, 3, 1, "SiLU"),
+                                  (1, 100, 64, 7, 3, "Relu")],
+                         ids=["resnet-stem", "96px", "yolo-like-3to16", "50px-output-generic-path"])
+def test_space_to_depth_stem(cuda_lib, ref_oracle, tmp_path, case):
+    """The stride-2 stem over a 3-channel input: the 16x16-patch kernel (output sides that are
+    multiples of 16) or the generic implicit GEMM, against the reference runtime."""
+    from spinn_b200 import ennf, netdef, runtime
+    batch, hw, oc, k, pad, act = case
+    g, x = netdef.conv_bn_relu(batch=batch, c=3, hw=hw, oc=oc, k=k, stride=2, pad=pad, act=act)
+    img = ennf.convert(g)
+    p = tmp_path / "stem.ennf"
+    p.write_bytes(img)
+    ref = list(ref_oracle.run_model(str(p), x).values())[0]
+    y = runtime.Model(img).run(x)
+    assert np.isfinite(y).all()
+    assert rel_l2(y.ravel(), ref.ravel()) <= 2e-3, rel_l2(y.ravel(), ref.ravel())
