@@ -79,6 +79,13 @@ int spinn_cuda_sync(void);
  * context stays usable. */
 int spinn_cuda_selftest_wait_expiry(uint64_t timeout_ns);
 
+/* Diagnostic: per-SM cost in cycles of one tcgen05 kind::tf32 MMA of m x n x 8 (m 64 or 128,
+ * n 16..256 in steps of 16) with both operands resident in shared memory in `layout`
+ * (0 no swizzle, 1/2/3 = 32/64/128-byte swizzle), issued back to back `iters` times
+ * (1..2^20) on every SM at once.  Writes the slowest SM's cycles per MMA.  No reference
+ * counterpart; it backs the tile planner's cost model. */
+int spinn_cuda_diag_mma_rate(int m, int n, int layout, int iters, double *cycles_per_mma);
+
 /* Releases the calling thread's session (stream, scratch, cached weights). */
 void spinn_cuda_shutdown(void);
 

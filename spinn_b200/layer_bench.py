@@ -3,10 +3,12 @@ runtime -- a unit for tuning and for profiling a single kernel.
 
     python -m spinn_b200.layer_bench --batch 512 --c 256 --hw 14 --oc 256 --k 3 [--residual]
     python -m spinn_b200.layer_bench --batch 128 --c 256 --hw 14 --oc 1024 --k 1 --projection
+    python -m spinn_b200.layer_bench --mma-rate
 
 Prints one JSON line: device ms per run (CUDA events around the planned step list, inputs
 resident), algorithmic TFLOP/s of the layer and algorithmic GB/s (input + output
-[+ residual] + weights, each touched once).
+[+ residual] + weights, each touched once).  --mma-rate instead prints one line per tf32 MMA
+shape and shared-memory layout with its per-SM cost in cycles (spinn_cuda_diag_mma_rate).
 """
 from __future__ import annotations
 
@@ -29,7 +31,11 @@ def main(argv=None):
     ap.add_argument("--winograd", action="store_true", help="plan with Winograd F(4x4,3x3)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--mma-rate", action="store_true",
+                    help="print the per-SM cycles of one tcgen05 tf32 MMA per shape and layout")
     a = ap.parse_args(argv)
+    if a.mma_rate:
+        return mma_rate()
 
     import numpy as np
     import torch
@@ -69,6 +75,29 @@ def main(argv=None):
     print(json.dumps({"layer": vars(a), "ms_per_run": ms, "tflops": flops / ms / 1e9, "gbs": byts / ms / 1e6,
                       "steps": model.plan_info()["steps"]}))
     model.close()
+    return 0
+
+
+MMA_SHAPES = ((128, 32), (128, 64), (128, 128), (128, 256), (64, 64), (64, 128), (64, 256))
+LAYOUTS = ("none", "sw32", "sw64", "sw128")
+
+
+def mma_rate(iters: int = 4096) -> int:
+    """Cycles per kind::tf32 MMA by shape and layout; MAC/cycle relative to the 2048 MAC/cycle
+    that a 128 x 256 x 8 instruction every 128 cycles delivers."""
+    import ctypes
+
+    from spinn_b200 import lib
+
+    L = lib.lib()
+    for layout, name in enumerate(LAYOUTS):
+        for m, n in MMA_SHAPES:
+            cyc = ctypes.c_double(0.0)
+            L.spinn_cuda_diag_mma_rate(m, n, layout, iters, ctypes.byref(cyc))  # warm-up
+            lib.check(L.spinn_cuda_diag_mma_rate(m, n, layout, iters, ctypes.byref(cyc)), "spinn_cuda_diag_mma_rate")
+            mac = m * n * 8 / cyc.value if cyc.value > 0 else None
+            print(json.dumps({"m": m, "n": n, "k": 8, "layout": name, "cycles_per_mma": cyc.value,
+                              "mac_per_cycle": mac}))
     return 0
 
 
