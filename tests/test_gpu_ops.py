@@ -27,6 +27,7 @@ CONV_CASES = [
     (1, 64, 56, 56, 64, 3, 1, 1, 1, 1, True, False),     # benchmark configuration 0
     (2, 32, 9, 11, 48, 3, 1, 1, 1, 0, True, False),      # ragged M tile, OC not a multiple of 32
     (1, 64, 14, 14, 256, 1, 1, 0, 1, 5, True, True),     # 1x1 + residual + ReLU
+    (2, 64, 20, 20, 512, 1, 1, 0, 1, 5, True, True),     # 1x1 + residual, several M and N tiles
     (2, 128, 15, 15, 128, 3, 2, 1, 1, 1, True, False),   # stride 2, odd spatial size
     (1, 3, 32, 32, 64, 7, 2, 3, 1, 1, True, False),      # stem: C=3 (padded to 4), 7x7/s2
     (1, 16, 20, 20, 32, 3, 1, 1, 1, 3, True, False),     # C=16 (64-B swizzle), SiLU
