@@ -149,6 +149,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
+def min_profile(prev, cur):
+    """Per-step minimum of two profiles [(op, ms, flops), ...] of the same step list (prev may
+    be None); raises if the step lists differ."""
+    if prev is None:
+        return list(cur)
+    if len(prev) != len(cur) or any(a[0] != b[0] for a, b in zip(prev, cur)):
+        raise ValueError("profiles of different step lists")
+    return [(op, min(ms, pms), fl) for (op, ms, fl), (_, pms, _) in zip(cur, prev)]
+
+
 def layer_roofline(img: bytes, prof, kinds, tf32_tflops: float, hbm_gbs: float):
     """Per-layer roofline of the convolutions' profiled times.  Each layer's floor is
     the larger of its algorithmic FLOPs at the tf32 peak and its algorithmic bytes (input,
@@ -336,7 +346,7 @@ def main():
         flush.zero_()
         model.run_profiled(sid)
         cur = model.profile()
-        prof = cur if prof is None else [(op, min(ms, pms), fl) for (op, ms, fl), (_, pms, _) in zip(cur, prof)]
+        prof = min_profile(prof, cur)
     conv_ms = sum(ms for (op, ms, fl), k in zip(prof, kinds) if k == 1)
     conv_fl = sum(fl for (op, ms, fl), k in zip(prof, kinds) if k == 1)
     conv_launches = sum(1 for k in kinds if k == 1)

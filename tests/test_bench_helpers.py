@@ -1,4 +1,5 @@
-"""bench.py's host-side helpers (no GPU): the per-layer roofline classification."""
+"""bench.py's host-side helpers (no GPU): the per-layer roofline classification and the
+per-step minimum over profiled replays."""
 import importlib.util
 import os
 
@@ -33,3 +34,25 @@ def test_layer_roofline_floors():
     assert np.isclose(r["conv_ms"], 0.030)
     assert r["hbm_bound_layers"] == 2 and r["tensor_bound_layers"] == 0
     assert bench.layer_roofline(img, prof[:1], [1], 100.0, 1000.0) is None  # step/node mismatch
+
+
+def test_min_profile_keeps_each_steps_minimum():
+    bench = _bench()
+    a = [(60, 0.30, 1e9), (5, 0.10, 0.0), (60, 0.50, 2e9)]
+    b = [(60, 0.25, 1e9), (5, 0.12, 0.0), (60, 0.55, 2e9)]
+    assert bench.min_profile(None, a) == a
+    m = bench.min_profile(a, b)
+    assert m == [(60, 0.25, 1e9), (5, 0.10, 0.0), (60, 0.50, 2e9)]
+    assert bench.min_profile(m, a) == m
+    try:
+        bench.min_profile(a, a[:2])
+    except ValueError:
+        pass
+    else:
+        raise AssertionError("step lists of different length accepted")
+    try:
+        bench.min_profile(a, [(61, 0.3, 1e9)] + a[1:])
+    except ValueError:
+        pass
+    else:
+        raise AssertionError("different operators accepted")
