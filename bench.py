@@ -18,12 +18,20 @@ forward pass of every rank's shard.  Rank 0 prints one JSON line:
             synchronous spinn_cuda_run (copy, run, copy back, one after another).
 * roofline  the tcgen05 convolution kernel: algorithmic conv FLOPs / its device time, both
             taken from profiled replays (CUDA events between the graph's kernels; each
-            kernel's minimum over PROFILE_REPLAYS replays).
+            kernel's minimum over PROFILE_REPLAYS replays).  The peak is the dense tf32
+            tensor rate, 2048 MAC per cycle per SM (one 128x256x8 kind::tf32 MMA every 128
+            cycles) x 2 FLOP x SMs x the median SM clock sampled during the timed region;
+            `frac_of_measured_burst` divides by half the measured bf16 cuBLAS burst instead.
             `layer_roofline` adds the per-layer view of the same times: every convolution's
             floor is max(FLOPs / tf32 peak, algorithmic bytes / copy bandwidth), and `frac`
             is the sum of the floors over the measured convolution time.
 * cpu_baseline  the reference's own CPU runtime (oracle/_ref, built unmodified from the
-            reference sources, epilogue fixed) on a bounded sample, rank 0 at N=1 only.
+            reference sources, epilogue fixed) on one 64-image micro-batch of the timed batch
+            (images 0..63), rank 0 at N=1 only.
+* parity    the checker, run after every timed region: the logits of sampled images of the
+            timed batch (the 64 images of the CPU baseline at N=1; the first two and last two
+            of rank 0's shard at N>1) against the same reference CPU runtime on those images:
+            relative L2, max |error| relative to max |reference|, and argmax agreement.
 
 ``--impl reference`` times that reference CPU runtime alone (rank 0; other ranks exit 0).
 """
@@ -50,12 +58,10 @@ DEPTH = 101
 SEED = 3
 METRIC = "resnet101_images_per_sec"
 UNIT = "images/s"
-CPU_SAMPLE_BATCH = 2
+CPU_SAMPLE_BATCH = 64   # one micro-batch of the reference CPU runtime (its arena clamp allows it)
+PARITY_IMAGES_MULTI = 4  # images checked by rank 0 at N > 1
 PROFILE_REPLAYS = 3  # profiled replays whose per-kernel minimum feeds the roofline
-# DRAM bytes per convolution launch of the batch-256 ResNet-101 step, measured with ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum over the 104 conv launches, 1 pass); the
-# algorithmic bytes of the same launches are 405.3 MB.
-CONV_DRAM_BYTES_PER_LAUNCH = 355.1e6
+TF32_MAC_PER_CLK_SM = 2048  # dense kind::tf32: one 128 x 256 x 8 MMA per 128 cycles per SM
 
 
 def parse():
@@ -105,21 +111,36 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def physical_gpu(local: int) -> str:
+    """nvidia-smi's id of this process's GPU: entry `local` of CUDA_VISIBLE_DEVICES (an index
+    or a UUID) when it is set, else `local` itself."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids):
+            return ids[local]
+    return str(local)
+
+
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons, sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons of one GPU, sampled every 100 ms while running."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
+    def __init__(self, gpu: str = "0"):
+        self.gpu = gpu
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.p = None
 
+    def command(self):
+        return ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                "-lms", "100"]
+
     def start(self):
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+            self.p = subprocess.Popen(self.command(), stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
 
@@ -145,8 +166,36 @@ class ClockSampler:
             for i, n in enumerate(names):
                 if r[5 + i].strip() == "Active":
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        return {"gpu": self.gpu, "sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def tf32_peak_tflops(sms: int, clocks) -> tuple:
+    """Dense tf32 tensor peak (TFLOP/s) at the median SM clock sampled during the timed region
+    (the maximum clock when no sample was taken), and a description of it."""
+    mhz, how = None, "median SM clock sampled during the timed region"
+    if clocks and clocks.get("sm_mhz"):
+        mhz = float(clocks["sm_mhz"])
+    elif clocks and clocks.get("sm_max_mhz"):
+        mhz, how = float(clocks["sm_max_mhz"]), "maximum SM clock (no sample under load)"
+    else:
+        mhz, how = 1965.0, "B200 maximum SM clock 1965 MHz (no clock sample)"
+    peak = TF32_MAC_PER_CLK_SM * 2.0 * sms * mhz * 1e6 / 1e12
+    return peak, f"{TF32_MAC_PER_CLK_SM} MAC/cycle/SM x 2 x {sms} SMs x {mhz:.0f} MHz ({how})"
+
+
+def parity_stats(y, ref) -> dict:
+    """Relative L2, max |error| over max |reference|, and argmax agreement of logits [n, classes]."""
+    y = np.asarray(y, np.float64).reshape(ref.shape[0], -1)
+    ref = np.asarray(ref, np.float64).reshape(ref.shape[0], -1)
+    d = float(np.linalg.norm(ref))
+    rel = float(np.linalg.norm(y - ref) / (d if d > 0 else 1.0))
+    scale = float(np.abs(ref).max())
+    max_abs = float(np.abs(y - ref).max())
+    agree = int((y.argmax(1) == ref.argmax(1)).sum())
+    return {"rel_l2": rel, "max_abs": max_abs, "max_abs_over_range": max_abs / scale if scale > 0 else None,
+            "argmax_agree": agree, "images": int(ref.shape[0]),
+            "ok": bool(rel <= 2e-3 and agree == ref.shape[0] and max_abs <= 1e-2 * scale)}
 
 
 def min_profile(prev, cur):
@@ -196,31 +245,44 @@ def build_model_image(batch: int, depth: int):
     return ennf.convert(g), g.flops()
 
 
-def cpu_reference_rate(depth: int, seconds: float, warmup: int = 1, min_runs: int = 2):
-    """Reference CPU runtime (oracle/_ref, O-fix) on ResNet-`depth` batch CPU_SAMPLE_BATCH."""
+def _reference_model_file(batch: int, depth: int) -> str:
+    """The benchmark network at `batch` (weights depend on SEED only) as a temporary .ennf file."""
+    img, _ = build_model_image(batch, depth)
+    with tempfile.NamedTemporaryFile(suffix=".ennf", delete=False) as f:
+        f.write(img)
+        return f.name
+
+
+def reference_leg(depth: int, images: np.ndarray, seconds: float = 0.0, min_runs: int = 2):
+    """The reference CPU runtime (oracle/_ref, O-fix build) on `images` (one micro-batch of the
+    timed batch), with all host threads: its logits (the checker's answer for those images)
+    and, when `seconds` > 0, its rate timed over at least `min_runs` further spinn_run calls
+    (about `seconds` of CPU work).  Returns (logits or None, cpu_baseline dict or None)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     if not oracle.ref_available():
-        return None
-    img, _ = build_model_image(CPU_SAMPLE_BATCH, depth)
-    from spinn_b200 import netdef
-    x = netdef.resnet_input(CPU_SAMPLE_BATCH, IMAGE, seed=SEED)
+        return None, None
+    n = images.shape[0]
     ref = oracle.RefOracle(fix=True)
     threads = os.cpu_count() or 1
     ref.set_threads(threads)
-    with tempfile.NamedTemporaryFile(suffix=".ennf", delete=False) as f:
-        f.write(img)
-        path = f.name
+    path = _reference_model_file(n, depth)
     try:
-        ts = ref.time_model(path, x, steps=1, warmup=warmup)
-        n = max(min_runs, int(seconds / max(ts[0], 1e-3)))
-        ts += ref.time_model(path, x, steps=n - 1, warmup=0)
+        t0 = time.perf_counter()
+        logits = list(ref.run_model(path, images).values())[0].reshape(n, -1)  # also the warm-up run
+        first = time.perf_counter() - t0
+        cpu = None
+        if seconds > 0:
+            runs = max(min_runs, int(seconds / max(first, 1e-3)))
+            ts = ref.time_model(path, images, steps=runs, warmup=0)
+            per = statistics.median(ts)
+            cpu = {"value": n / per, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": f"ResNet-{depth} micro-batch of {n} images (images 0..{n - 1} of the timed batch), "
+                             f"3x224x224, {len(ts)} spinn_run calls after 1 warm-up, median {per * 1e3:.0f} ms/call, "
+                             f"O-fix build of the reference sources, OMP threads={threads}"}
     finally:
         os.unlink(path)
-    per = statistics.median(ts)
-    return {"value": CPU_SAMPLE_BATCH / per, "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": f"ResNet-{depth} batch {CPU_SAMPLE_BATCH} 3x224x224, {len(ts)} spinn_run calls after {warmup} "
-                      f"warm-up, median {per * 1e3:.1f} ms/call, OMP threads={threads}"}
+    return logits, cpu
 
 
 def run_reference_arm(args, rank: int, world: int):
@@ -233,31 +295,29 @@ def run_reference_arm(args, rank: int, world: int):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libspinn_ref.so was not built"}))
         return 0
     from spinn_b200 import netdef
-    img, _ = build_model_image(CPU_SAMPLE_BATCH, args.depth)
-    x = netdef.resnet_input(CPU_SAMPLE_BATCH, IMAGE, seed=SEED)
+    sample = min(CPU_SAMPLE_BATCH, args.batch)
+    x = netdef.image_batch(0, sample, IMAGE, seed=SEED)
     ref = oracle.RefOracle(fix=True)
     threads = os.cpu_count() or 1
     ref.set_threads(threads)
-    with tempfile.NamedTemporaryFile(suffix=".ennf", delete=False) as f:
-        f.write(img)
-        path = f.name
+    path = _reference_model_file(sample, args.depth)
     try:
         ts = ref.time_model(path, x, steps=args.steps, warmup=args.warmup)
     finally:
         os.unlink(path)
     total = sum(ts)
-    value = CPU_SAMPLE_BATCH * args.steps / total
+    value = sample * args.steps / total
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (He-init weights, N(0,1) input)",
-        "config": {"workload": f"ResNet-{args.depth} 3x224x224 (benchmark configuration 3); each step a "
-                               f"bounded sample of {CPU_SAMPLE_BATCH} images", "global_batch": args.batch,
-                   "image": IMAGE, "sample_batch": CPU_SAMPLE_BATCH},
+        "config": {"workload": f"ResNet-{args.depth} batch {args.batch} 3x224x224 (benchmark configuration 3); "
+                               f"each step one micro-batch of {sample} images (images 0..{sample - 1} of the batch)",
+                   "global_batch": args.batch, "image": IMAGE, "sample_batch": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": f"{args.steps} spinn_run calls of batch {CPU_SAMPLE_BATCH} after "
-                                   f"{args.warmup} warm-up, O-fix build, OMP threads={threads}"},
+                         "sample": f"{args.steps} spinn_run calls of a {sample}-image micro-batch after "
+                                   f"{args.warmup} warm-up, O-fix build of the reference sources, OMP threads={threads}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.time() - t0,
     }
@@ -319,7 +379,7 @@ def main():
         flush.zero_()
     barrier()
 
-    sampler = ClockSampler() if rank == 0 else None
+    sampler = ClockSampler(physical_gpu(local)) if rank == 0 else None
     if sampler:
         sampler.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -379,16 +439,36 @@ def main():
     sync_value = args.batch * args.steps / sync_s
 
     peaks, peak_src = measured_peaks()
-    tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    tf32_peak, tf32_peak_how = tf32_peak_tflops(sms, clocks if rank == 0 else None)
+    tf32_peak = reduce_max(tf32_peak, pg, f"cuda:{local}")  # rank 0's sampled clock on every rank
+    burst_tf32 = peaks["bf16_tflops"] / 2.0
     layers = layer_roofline(img, prof, kinds, tf32_peak, peaks["hbm_gbs"])
     achieved = conv_fl / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    # The checker, after every timed region: logits of sampled images of the timed batch (the
+    # last submission above left this shard's logits in out_pin) against the reference CPU
+    # runtime on the same images; at N = 1 the same micro-batch is also timed as the CPU baseline.
+    cpu = parity = None
+    if rank == 0 and not args.no_cpu_baseline:
+        logits = out_pin.numpy().reshape(shard, -1)
+        if world == 1:
+            idx = list(range(min(CPU_SAMPLE_BATCH, shard)))
+        else:
+            h = PARITY_IMAGES_MULTI // 2
+            idx = list(range(h)) + list(range(shard - h, shard))
         try:
-            cpu = cpu_reference_rate(args.depth, args.cpu_seconds)
+            ref_logits, cpu = reference_leg(args.depth, x.numpy()[idx], args.cpu_seconds if world == 1 else 0.0)
+            if ref_logits is not None:
+                parity = parity_stats(logits[idx], ref_logits)
+                parity["image_ids"] = f"{start + idx[0]}..{start + idx[-1]}" if world == 1 else \
+                    [start + i for i in idx]
+                parity["oracle"] = "reference CPU runtime (oracle/_ref O-fix) on the same images"
+                parity["tolerance"] = "rel_l2 <= 2e-3, argmax identical, max_abs <= 1e-2 x max|ref|"
         except Exception as e:  # reported, not fatal
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference", "sample": f"failed: {e}"}
+        if world > 1:
+            cpu = None
 
     if rank == 0:
         line = {
@@ -403,12 +483,14 @@ def main():
                        "graph": "CUDA graph of the planned step list"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
                          "frac": achieved / tf32_peak if tf32_peak else None,
-                         "traffic": CONV_DRAM_BYTES_PER_LAUNCH if (shard, args.depth) == (256, 101) else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the 104 "
-                                           "conv launches of one batch-256 step "
-                                           "(profiles/resnet101_b256_launch_list.md)",
+                         "traffic": None,
+                         "traffic_source": "per-launch DRAM bytes come from single-kernel ncu captures of "
+                                           "small cases, listed with the kernel summaries",
                          "kernel": "tc_gemm_kernel (implicit-GEMM conv, tcgen05 kind::tf32)",
-                         "peak_source": f"{peak_src}: bf16_tflops_sustained / 2 (dense tf32)",
+                         "peak_source": f"dense tf32 tensor rate: {tf32_peak_how}",
+                         "peak_measured_burst": burst_tf32,
+                         "frac_of_measured_burst": achieved / burst_tf32 if burst_tf32 else None,
+                         "peak_measured_burst_source": f"{peak_src}: bf16_tflops / 2 (cuBLAS bf16 burst, halved)",
                          "launches_per_step": conv_launches,
                          "flops_per_launch_avg": conv_fl / max(conv_launches, 1),
                          "ms_per_launch_avg": conv_ms / max(conv_launches, 1)},
@@ -420,8 +502,10 @@ def main():
                     "api": "spinn_cuda_submit per step + spinn_cuda_wait (input copy overlaps the previous run)",
                     "sync_value": sync_value},
             "gpu_launches": info["kernels"] * args.steps * world,
+            "gpu_launches_per_step_per_gpu": info["kernels"],
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "parity": parity,
             "plan": {"arena_bytes": info["arena_bytes"], "weight_bytes": info["weight_bytes"],
                      "steps": info["steps"], "build_s": round(build_s, 1)},
             "wall_s_timed_region": wall,

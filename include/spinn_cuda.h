@@ -79,13 +79,6 @@ int spinn_cuda_sync(void);
  * context stays usable. */
 int spinn_cuda_selftest_wait_expiry(uint64_t timeout_ns);
 
-/* Diagnostic: per-SM cost in cycles of one tcgen05 kind::tf32 MMA of m x n x 8 (m 64 or 128,
- * n 16..256 in steps of 16) with both operands resident in shared memory in `layout`
- * (0 no swizzle, 1/2/3 = 32/64/128-byte swizzle), issued back to back `iters` times
- * (1..2^20) on every SM at once.  Writes the slowest SM's cycles per MMA.  No reference
- * counterpart; it backs the tile planner's cost model. */
-int spinn_cuda_diag_mma_rate(int m, int n, int layout, int iters, double *cycles_per_mma);
-
 /* Releases the calling thread's session (stream, scratch, cached weights). */
 void spinn_cuda_shutdown(void);
 
@@ -94,8 +87,10 @@ const char *spinn_cuda_last_error(void);
 
 /* Installs spinn_cuda_conv2d / _gemm / _matmul into a registry through `register_op`
  * (op_type: ENNF_OpType value; Conv=60, Gemm=160, MatMul=161, SPINN/ennf_op_types.h:79,134,135).
- * The reference registry is a file-static array (SPINN/run_time/spinn_ops.c:17); the
- * setter it needs is shown in INTEGRATION.md.  Returns the number of operators installed. */
+ * The reference registry is a file-static array (SPINN/run_time/spinn_ops.c:17), so the
+ * reference needs a one-function setter, e.g. `int spinn_register_op(uint16_t op,
+ * SpinnOpKernel fn) { g_op_registry[op] = fn; return 0; }` beside init_registry.
+ * Returns the number of operators installed. */
 int spinn_cuda_register(int (*register_op)(uint16_t op_type, SpinnOpKernel fn));
 
 /* ------------------------------------------------------------------ operator level */
@@ -124,9 +119,15 @@ int spinn_cuda_matmul(SpinnTensor **in, int n_in, void *params, uint16_t params_
  * up front -- this variant of spinn_cuda_conv2d keeps every temporary in one fixed 32 MiB
  * device array that each GPU loading the library holds until exit.  Arguments are device
  * pointers (NCHW fp32 x, OIHW w, optional bias[oc], residual like y when fused_act is 4/5)
- * and the geometry; group 1.  Larger problems return SPINN_CUDA_EINVAL.  The first call on a
- * device resolves the array's address (make it before any stream capture); calls overlapping
- * on the GPU share the array and race; the call waits for `stream` before returning. */
+ * and the geometry; group 1.  Refused with SPINN_CUDA_EINVAL before any GPU work: problems
+ * whose temporaries exceed the 32 MiB, batch n > 65535, stride > 8, padding that puts the
+ * im2col corners outside [-128, 127], and a `stream` of a device other than the current one.
+ * The first call on a device resolves the array's address; under lazy module loading (the
+ * CUDA default) the first call of each shape also loads kernel code, which allocates, so make
+ * those calls during set-up (or set CUDA_MODULE_LOADING=EAGER).  Never call it while its
+ * stream, or any stream under a global-mode capture, is capturing: it reads an error word back
+ * to the host and waits for `stream` before returning.  Calls overlapping on the GPU share the
+ * array and race. */
 int spinn_cuda_conv2d_noalloc(const float *x, const float *w, const float *bias, const float *residual,
                               float *y, int n, int c, int h, int w_, int oc, int kh, int kw,
                               int stride_h, int stride_w, int pad_h, int pad_w, int fused_act,
@@ -147,11 +148,14 @@ SpinnCudaModel *spinn_cuda_load_buffer(const void *data, size_t size);
  * flags: bit 0 = do not capture a CUDA graph; bit 1 = also prepare a profiled variant
  *        (spinn_cuda_run_profiled);
  *        bit 2 = keep activations fp32 on store (no tf32 rounding of conv outputs);
- *        bit 3 = Winograd F(4x4,3x3) for 3x3 stride-1 group-1 convolutions. */
+ *        bit 3 = Winograd F(4x4,3x3) for 3x3 stride-1 group-1 convolutions;
+ *        bit 4 = keep every intermediate tensor after a run (each gets its own arena range). */
 #define SPINN_CUDA_PLAN_NO_GRAPH 1
 #define SPINN_CUDA_PLAN_PROFILE 2
 #define SPINN_CUDA_PLAN_NO_ROUND 4
 #define SPINN_CUDA_PLAN_WINOGRAD 8 /* run 3x3 stride-1 convolutions with Winograd F(4x4,3x3) */
+#define SPINN_CUDA_PLAN_KEEP 16    /* keep every intermediate tensor (no arena reuse) for
+                                      spinn_cuda_copy_tensor; same kernels and tile plans */
 int spinn_cuda_plan(SpinnCudaModel *m, int device, uint64_t max_arena_bytes, int flags);
 
 /* Stage 3: run one inference.  Copies input 0 (NCHW fp32, host memory) to the device, runs
@@ -195,7 +199,18 @@ int spinn_cuda_io_dtype(SpinnCudaModel *m, int is_output, int index);
  * the output's size (spinn_cuda_io_ptr). */
 int spinn_cuda_copy_output(SpinnCudaModel *m, int index, void *host, size_t bytes);
 
-/* Planned sizes: device arena bytes and pre-transformed weight bytes. */
+/* Synchronous copy of items [first, first + count) along dim 0 (the images of an NCHW
+ * tensor) of ENNF tensor `tensor_id` after a run, in the .ennf's own layout (NCHW fp32 for
+ * 4-D tensors), into `host`; `bytes` must be exactly their size.  Graph outputs can always be
+ * read; any other activation needs plan flag SPINN_CUDA_PLAN_KEEP (otherwise its arena range
+ * has been reused).  Weights and tensors fused away by the converter return EINVAL.  The
+ * reference keeps intermediates in its host arena (SPINN/run_time/spinn_runtime.c:147-152);
+ * this is how a caller inspects them here, e.g. for per-layer checks. */
+int spinn_cuda_copy_tensor(SpinnCudaModel *m, int tensor_id, int first, int count, void *host, size_t bytes);
+
+/* Planned sizes: device arena bytes and pre-transformed weight bytes; the number of steps and
+ * the kernels one run launches (the captured graph's kernel nodes; without a graph, the steps
+ * that launch a kernel). */
 int spinn_cuda_plan_info(SpinnCudaModel *m, uint64_t *arena_bytes, uint64_t *weight_bytes,
                          int *num_steps, int *num_kernels);
 

@@ -45,12 +45,24 @@ def _fp(a: Optional[np.ndarray]):
     return a.ctypes.data_as(_f32p) if a is not None else None
 
 
+def reference_dir() -> Optional[str]:
+    """The reference's ``SPINN/`` source directory: ``$REF_DIR`` when set, else a ``reference``
+    checkout beside this repository; None when neither exists (the GPU box has only the
+    prebuilt ``_ref`` files)."""
+    cands = [os.environ.get("REF_DIR"), os.path.join(os.path.dirname(ROOT), "reference", "SPINN")]
+    for c in cands:
+        if c and os.path.isfile(os.path.join(c, "run_time", "spinn_runtime.c")):
+            return os.path.abspath(c)
+    return None
+
+
 def build(ref: bool = True) -> None:
     """Builds the port (always) and the reference library (when the reference tree exists)."""
     targets = ["port"]
-    if ref and os.path.isdir(os.environ.get("REF_DIR", "/root/reference/SPINN")):
+    rd = reference_dir() if ref else None
+    if rd:
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    subprocess.run(["make", "-s", "-C", HERE] + targets + ([f"REF_DIR={rd}"] if rd else []), check=True)
 
 
 def ref_available() -> bool:

@@ -9,6 +9,10 @@
   (M=256, K=2048, N=1000, transB 0/1).
 * cfg2 -- ResNet-50, batch 1 and 64.
 * cfg4 -- the YOLOv10n-shaped network (``netdef.yolo_shaped``), 640x640, batch 1 and 32.
+* layer -- one fused convolution (Conv+BN+ReLU, optionally +residual or a projection shortcut)
+  of a chosen shape, the unit the single-kernel ncu summaries capture:
+
+    python -m spinn_b200.config_bench --layer --batch 128 --c 256 --hw 14 --oc 1024 --k 1 --projection
 
 Every case is planned once (weights uploaded, graph captured), its input staged on the device,
 and the captured step list replayed: ``ms`` is the mean device time per run from CUDA events on
@@ -51,12 +55,62 @@ def _case(name, graph, x, iters, warmup, flags=0, per_item=None, **extra):
     print(json.dumps(line), flush=True)
 
 
+def layer(a) -> int:
+    """Times one fused convolution layer through the device runtime: device ms per run (CUDA
+    events around the planned step list, inputs resident), algorithmic TFLOP/s and algorithmic
+    GB/s (input + output [+ residual] + weights, each touched once)."""
+    from spinn_b200 import lib, netdef
+
+    pad = a.k // 2
+    if a.projection:
+        g, x = netdef.conv_bn_proj_add_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k)
+    elif a.residual:
+        g, x = netdef.conv_bn_add_relu(batch=a.batch, c=a.c, hw=a.hw)
+    else:
+        g, x = netdef.conv_bn_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k, stride=a.stride, pad=pad,
+                                   group=a.group)
+    from spinn_b200 import ennf, runtime
+    model = runtime.Model(ennf.convert(g), flags=lib.PLAN_WINOGRAD if a.winograd else 0)
+    model.run(x)  # stages the input on the device
+    ms = _time(model, a.iters, a.warmup)
+    oc = a.c if a.residual else a.oc
+    oh = a.hw if a.projection else (a.hw + 2 * pad - a.k) // a.stride + 1
+    cin = a.c // a.group
+    # --projection: both convolutions (the shortcut 1x1 and the fused-residual one)
+    flops = 2.0 * a.batch * oc * oh * oh * cin * (a.k * a.k + (1 if a.projection else 0))
+    cpad = (a.c + 3) // 4 * 4
+    res = a.residual or a.projection
+    byts = 4.0 * (a.batch * a.hw * a.hw * cpad * (2 if a.projection else 1)
+                  + a.batch * oh * oh * oc * ((3 if a.projection else 2) if res else 1)
+                  + oc * cin * (a.k * a.k + (1 if a.projection else 0)))
+    print(json.dumps({"layer": {k: v for k, v in vars(a).items() if k != "only"}, "ms_per_run": ms,
+                      "tflops": flops / ms / 1e9, "gbs": byts / ms / 1e6, "steps": model.plan_info()["steps"],
+                      "kinds": model.step_kinds()}), flush=True)
+    model.close()
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="cfg0,cfg1,cfg2,cfg4")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--layer", action="store_true", help="time one convolution layer (shape below)")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--c", type=int, default=256)
+    ap.add_argument("--hw", type=int, default=14)
+    ap.add_argument("--oc", type=int, default=256)
+    ap.add_argument("--k", type=int, default=3)
+    ap.add_argument("--stride", type=int, default=1)
+    ap.add_argument("--group", type=int, default=1)
+    ap.add_argument("--residual", action="store_true", help="conv+BN+Add+ReLU (needs c == oc, stride 1)")
+    ap.add_argument("--projection", action="store_true",
+                    help="bottleneck end with a projection shortcut: ReLU(BN(conv(x)) + BN(conv1x1(x))); "
+                         "the second conv (c -> oc) carries the fused residual")
+    ap.add_argument("--winograd", action="store_true", help="plan with Winograd F(4x4,3x3)")
     a = ap.parse_args(argv)
+    if a.layer:
+        return layer(a)
     which = set(a.only.split(","))
 
     from spinn_b200 import lib, netdef

@@ -321,16 +321,6 @@ __attribute__((visibility("default"))) int spinn_cuda_selftest_wait_expiry(uint6
   return check_device_error_flag(S.device, S.stream);
 }
 
-__attribute__((visibility("default"))) int spinn_cuda_diag_mma_rate(int m, int n, int layout, int iters,
-                                                                   double* cycles_per_mma) {
-  int rc = ensure_session();
-  if (rc) return rc;
-  Session& S = g_sess;
-  rc = run_mma_rate_probe(S.device, m, n, layout, iters, device_error_flag(S.device), S.stream, cycles_per_mma);
-  if (rc) return rc;
-  return check_device_error_flag(S.device, S.stream);
-}
-
 __attribute__((visibility("default"))) void spinn_cuda_shutdown(void) {
   Session& S = g_sess;
   if (!S.ready) return;

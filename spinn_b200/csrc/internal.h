@@ -56,10 +56,6 @@ int* device_error_flag(int device);
 int check_device_error_flag(int device, cudaStream_t stream);
 // One-thread kernel whose mbarrier wait expires after timeout_ns (<= 1 s) and raises *err.
 int launch_wait_expiry_selftest(int* err, uint64_t timeout_ns, cudaStream_t s);
-// Per-SM cost of one kind::tf32 MMA (M x N x 8, operands resident in shared memory, given
-// layout), measured on every SM at once: the slowest CTA's cycles / iters.  -1 if a wait expired.
-int run_mma_rate_probe(int device, int m, int n, int layout, int iters, int* err, cudaStream_t s,
-                       double* cycles_per_mma);
 
 // ------------------------------------------------------------------ tcgen05 GEMM / conv
 // Y[M][ldy] = epilogue( A * W^T ), W stored K-major [N][kpad].

@@ -13,15 +13,27 @@
 //  * x, w, bias, residual and y are device pointers supplied by the caller (NCHW fp32, weights
 //    OIHW), group 1.  The problem's scratch need must fit kNoAllocScratchBytes; larger
 //    problems are rejected with SPINN_CUDA_EINVAL before any GPU work.
+//  * Every unsupported problem is refused with SPINN_CUDA_EINVAL before any GPU work is
+//    queued: scratch need above kNoAllocScratchBytes, a batch above 65535 (the layout
+//    kernels put the image index in grid.z), a geometry the tensor-core kernel does not take
+//    (stride above 8, im2col corners outside [-128, 127]), or a stream of another device.
+//  * `stream` must belong to the current device (NULL: that device's legacy default stream).
 //  * The first call on a device resolves the array's device address with
-//    cudaGetSymbolAddress (with that device current); make that first call before any stream
-//    capture.
+//    cudaGetSymbolAddress (with that device current).  Under lazy module loading (the CUDA
+//    default since 12.2) that first call, and the first call that needs a kernel variant not
+//    launched before, also loads code onto the GPU, which allocates device memory.  A host
+//    that must not allocate at inference time therefore makes one call per device, of each
+//    shape it will use, during its setup, or runs with CUDA_MODULE_LOADING=EAGER.
+//  * Never call it while its stream (or any stream, under a global-mode capture) is being
+//    captured: every call copies the device error word into host memory and waits for the
+//    stream, and neither may happen inside a capture.
 //  * Every call shares the array and overwrites it.  Calls that overlap on the GPU (other
 //    streams, other host threads, the same device) race on it: serialize them.
 //  * The call is synchronous: it waits for its stream and reports a kernel timeout as
 //    SPINN_CUDA_ETIMEOUT.
 #include <algorithm>
 #include <mutex>
+#include <string>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -102,12 +114,18 @@ extern "C" __attribute__((visibility("default"))) int spinn_cuda_conv2d_noalloc(
               kNoAllocScratchBytes);
     return SPINN_CUDA_EINVAL;
   }
+  SPINN_CHECK_ARG(n <= 65535, "conv2d_noalloc: batch %d above 65535", n);
   int dev = 0;
   SPINN_CUDA_TRY(cudaGetDevice(&dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (st) {
+    int sdev = -1;
+    SPINN_CUDA_TRY(cudaStreamGetDevice(st, &sdev));
+    SPINN_CHECK_ARG(sdev == dev, "conv2d_noalloc: stream belongs to device %d, the current device is %d", sdev, dev);
+  }
   unsigned char* base = nullptr;
   int rc = scratch_address(dev, &base);
   if (rc) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   int* err = reinterpret_cast<int*>(base);
   float* xs = reinterpret_cast<float*>(base + kErrSlot);
   float* ws = reinterpret_cast<float*>(base + kErrSlot + xb);
@@ -115,19 +133,6 @@ extern "C" __attribute__((visibility("default"))) int spinn_cuda_conv2d_noalloc(
   float* ys = reinterpret_cast<float*>(base + kErrSlot + xb + wb + bb);
   float* rs = has_res ? reinterpret_cast<float*>(base + kErrSlot + xb + wb + bb + yb) : nullptr;
 
-  SPINN_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
-  rc = launch_nchw_to_nhwc(x, xs, n, c, h, wd, cpad, st, /*round_tf32=*/1);
-  if (rc) return rc;
-  const long wtotal = (long)ocpad * kpad;
-  weight_km_kernel<<<(int)std::min<long>((wtotal + 255) / 256, 148 * 8), 256, 0, st>>>(w, ws, oc, c, kh, kw, cpad,
-                                                                                       ocpad, kpad);
-  SPINN_CUDA_TRY(cudaGetLastError());
-  SPINN_CUDA_TRY(cudaMemsetAsync(bs, 0, (size_t)ocpad * 4, st));
-  if (bias) SPINN_CUDA_TRY(cudaMemcpyAsync(bs, bias, (size_t)oc * 4, cudaMemcpyDeviceToDevice, st));
-  if (has_res) {
-    rc = launch_nchw_to_nhwc(residual, rs, n, oc, oh, ow, ocpad, st);
-    if (rc) return rc;
-  }
   TcGemmArgs a;
   a.a_mode = 0;
   a.x = xs;
@@ -155,6 +160,26 @@ extern "C" __attribute__((visibility("default"))) int spinn_cuda_conv2d_noalloc(
   a.ldy = ocpad;
   a.act = fused_act;
   a.err = err;
+  std::string why;
+  if (!tc_gemm_supported(a, &why)) {
+    set_error("conv2d_noalloc: %s", why.c_str());
+    return SPINN_CUDA_EINVAL;
+  }
+
+  // from here on GPU work is queued
+  SPINN_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+  rc = launch_nchw_to_nhwc(x, xs, n, c, h, wd, cpad, st, /*round_tf32=*/1);
+  if (rc) return rc;
+  const long wtotal = (long)ocpad * kpad;
+  weight_km_kernel<<<(int)std::min<long>((wtotal + 255) / 256, 148 * 8), 256, 0, st>>>(w, ws, oc, c, kh, kw, cpad,
+                                                                                       ocpad, kpad);
+  SPINN_CUDA_TRY(cudaGetLastError());
+  SPINN_CUDA_TRY(cudaMemsetAsync(bs, 0, (size_t)ocpad * 4, st));
+  if (bias) SPINN_CUDA_TRY(cudaMemcpyAsync(bs, bias, (size_t)oc * 4, cudaMemcpyDeviceToDevice, st));
+  if (has_res) {
+    rc = launch_nchw_to_nhwc(residual, rs, n, oc, oh, ow, ocpad, st);
+    if (rc) return rc;
+  }
   rc = tc_gemm_launch(a, st);
   if (rc) return rc;
   rc = launch_nhwc_to_nchw(ys, y, n, oc, oh, ow, ocpad, st);

@@ -332,11 +332,14 @@ int plan_arena(SpinnCudaModel* m, int nsteps, uint64_t budget) {
   std::vector<Blk> freel{{0, budget ? budget : ~0ull >> 1}};
   uint64_t peak = 0;
   std::vector<std::vector<int>> born(nsteps + 1), dies(nsteps + 1);
+  // SPINN_CUDA_PLAN_KEEP: no buffer is released, so every intermediate keeps its value from
+  // the last run (spinn_cuda_copy_tensor); the kernels and their tile plans do not change
+  const bool keep = (m->flags & SPINN_CUDA_PLAN_KEEP) != 0;
   for (int i = 0; i < (int)m->bufs.size(); ++i) {
     Buf& b = m->bufs[i];
     if (b.alias >= 0 || b.external || b.bytes == 0 || b.first < 0) continue;
     born[b.first].push_back(i);
-    dies[b.last].push_back(i);
+    dies[keep ? nsteps : b.last].push_back(i);
   }
   auto alloc = [&](uint64_t size, uint64_t* off) {
     size = align_up(size, 256);
@@ -1643,6 +1646,19 @@ __attribute__((visibility("default"))) int spinn_cuda_plan(SpinnCudaModel* m, in
       if (pass == 0) {
         m->graph = g;
         m->gexec = ge;
+        // kernels launched per run: the captured graph's kernel nodes (a split-K step, for
+        // instance, is two kernels)
+        size_t nn = 0;
+        SPINN_CUDA_TRY(cudaGraphGetNodes(g, nullptr, &nn));
+        std::vector<cudaGraphNode_t> nodes(nn);
+        SPINN_CUDA_TRY(cudaGraphGetNodes(g, nodes.data(), &nn));
+        int kern = 0;
+        for (size_t i = 0; i < nn; ++i) {
+          cudaGraphNodeType t;
+          SPINN_CUDA_TRY(cudaGraphNodeGetType(nodes[i], &t));
+          if (t == cudaGraphNodeTypeKernel) ++kern;
+        }
+        m->kernels = kern;
       } else {
         m->pgraph = g;
         m->pgexec = ge;
@@ -1849,6 +1865,61 @@ __attribute__((visibility("default"))) int spinn_cuda_copy_output(SpinnCudaModel
   SPINN_CUDA_TRY(cudaSetDevice(m->device));
   SPINN_CUDA_TRY(cudaMemcpyAsync(host, b.ptr, bytes, cudaMemcpyDeviceToHost, m->stream));
   SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_copy_tensor(SpinnCudaModel* m, int tensor_id, int first,
+                                                                  int count, void* host, size_t bytes) {
+  if (!m || !m->planned || !host) {
+    set_error("spinn_cuda_copy_tensor: model not planned or no host buffer");
+    return SPINN_CUDA_ESTATE;
+  }
+  if (tensor_id < 0 || tensor_id >= (int)m->tensors.size() || tensor_id >= (int)m->bufs.size()) {
+    set_error("spinn_cuda_copy_tensor: no tensor %d", tensor_id);
+    return SPINN_CUDA_EINVAL;
+  }
+  const TensorRec& t = m->tensors[tensor_id];
+  const bool is_output = std::find(m->outputs.begin(), m->outputs.end(), (uint16_t)tensor_id) != m->outputs.end();
+  if (!(m->flags & SPINN_CUDA_PLAN_KEEP) && !is_output) {
+    set_error("spinn_cuda_copy_tensor: tensor %d is not a graph output; plan with SPINN_CUDA_PLAN_KEEP", tensor_id);
+    return SPINN_CUDA_ESTATE;
+  }
+  int r = tensor_id;
+  while (m->bufs[r].alias >= 0) r = m->bufs[r].alias;
+  const Buf& b = m->bufs[tensor_id];
+  const float* base = m->bufs[r].ptr;
+  if (t.is_weight || !base || b.lay == LAY_NONE || t.ndim < 1 || t.dims[0] == 0) {
+    set_error("spinn_cuda_copy_tensor: tensor %d has no device buffer (weight, fused away or unused)", tensor_id);
+    return SPINN_CUDA_EINVAL;
+  }
+  const uint64_t d0 = t.dims[0];
+  if (first < 0 || count < 1 || (uint64_t)first + (uint64_t)count > d0) {
+    set_error("spinn_cuda_copy_tensor: items [%d, %d) outside dim 0 = %llu", first, first + count,
+              (unsigned long long)d0);
+    return SPINN_CUDA_EINVAL;
+  }
+  const uint64_t esz = elem_bytes(t);
+  const uint64_t item_elems = t.elems / d0;
+  if (bytes != (uint64_t)count * item_elems * esz) {
+    set_error("spinn_cuda_copy_tensor: %d items of tensor %d are %llu bytes, not %zu", count, tensor_id,
+              (unsigned long long)((uint64_t)count * item_elems * esz), bytes);
+    return SPINN_CUDA_EINVAL;
+  }
+  SPINN_CUDA_TRY(cudaSetDevice(m->device));
+  SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  if (b.lay == LAY_NHWC) {
+    // NHWC with padded channels on the device -> NCHW on the host
+    const uint64_t hw = (uint64_t)b.h * b.w, img = hw * b.cpad;
+    std::vector<float> tmp((size_t)(count * img));
+    SPINN_CUDA_TRY(cudaMemcpy(tmp.data(), base + (uint64_t)first * img, tmp.size() * 4, cudaMemcpyDeviceToHost));
+    float* dst = static_cast<float*>(host);
+    for (int n = 0; n < count; ++n)
+      for (int c = 0; c < b.c; ++c)
+        for (uint64_t p = 0; p < hw; ++p) dst[((uint64_t)n * b.c + c) * hw + p] = tmp[n * img + p * b.cpad + c];
+  } else {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(base) + (uint64_t)first * item_elems * esz;
+    SPINN_CUDA_TRY(cudaMemcpy(host, src, bytes, cudaMemcpyDeviceToHost));
+  }
   return 0;
 }
 

@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(HERE, "libspinn_cuda.so")
 
 # Status codes (include/spinn_cuda.h)
 OK, EINVAL, ENOMEM, ECUDA, EUNSUPPORTED, ETIMEOUT, EFORMAT, ESTATE = 0, -1, -2, -3, -4, -5, -6, -7
-PLAN_NO_GRAPH, PLAN_PROFILE, PLAN_NO_ROUND, PLAN_WINOGRAD = 1, 2, 4, 8
+PLAN_NO_GRAPH, PLAN_PROFILE, PLAN_NO_ROUND, PLAN_WINOGRAD, PLAN_KEEP = 1, 2, 4, 8, 16
 
 # ENNF operator codes (SPINN/ennf_op_types.h:79,134,135)
 OP_CONV, OP_GEMM, OP_MATMUL = 60, 160, 161
@@ -69,8 +69,6 @@ _SIGS = {
     "spinn_cuda_run_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_submit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_selftest_wait_expiry": (ctypes.c_int, [ctypes.c_uint64]),
-    "spinn_cuda_diag_mma_rate": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                                 ctypes.POINTER(ctypes.c_double)]),
     "spinn_cuda_wait": (ctypes.c_int, [ctypes.c_void_p]),
     "spinn_cuda_run_profiled": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_io_ptr": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
@@ -78,6 +76,8 @@ _SIGS = {
     "spinn_cuda_io_count": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "spinn_cuda_io_dtype": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
     "spinn_cuda_copy_output": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t]),
+    "spinn_cuda_copy_tensor": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_void_p, ctypes.c_size_t]),
     "spinn_cuda_io_dims": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_uint32)]),
     "spinn_cuda_plan_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64),

@@ -263,9 +263,10 @@ class _Builder:
 
 # ---------------------------------------------------------------------- models
 def conv_bn_relu(batch: int = 1, c: int = 64, hw: int = 56, oc: int = 64, k: int = 3,
-                 stride: int = 1, pad: int = 1, seed: int = 0, act: str = "Relu"
+                 stride: int = 1, pad: int = 1, seed: int = 0, act: str = "Relu", group: int = 1
                  ) -> Tuple[Graph, np.ndarray]:
-    """Single Conv+BatchNorm(+act) layer (the benchmark's first configuration).
+    """Single Conv+BatchNorm(+act) layer (the benchmark's first configuration; ``group`` > 1
+    gives grouped / depthwise layers).
 
     Draw order from ``default_rng(seed)``: input X~U(-1,1), W~N(0,sqrt(2/fan_in)),
     gamma, beta, mean, var.  Returns the graph and the input tensor.
@@ -275,7 +276,7 @@ def conv_bn_relu(batch: int = 1, c: int = 64, hw: int = 56, oc: int = 64, k: int
     g = Graph("conv_bn_relu")
     b = _Builder(g, rng)
     x = g.add_input("input", (batch, c, hw, hw))
-    y = b.bn(b.conv(x, oc, k, stride, pad))
+    y = b.bn(b.conv(x, oc, k, stride, pad, group=group))
     if act == "Relu":
         y = b.unary("Relu", y)
     elif act == "SiLU":

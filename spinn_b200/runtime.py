@@ -167,6 +167,17 @@ class Model:
         check(lib().spinn_cuda_copy_output(self._h, index, out.ctypes.data, out.nbytes), "spinn_cuda_copy_output")
         return out
 
+    def tensor(self, tensor_id: int, dims: Sequence[int], first: int = 0, count: Optional[int] = None,
+               dtype=np.float32) -> np.ndarray:
+        """Items ``first .. first+count-1`` (dim 0) of ENNF tensor `tensor_id` after a run, in the
+        .ennf layout (``dims`` as the .ennf declares them; ``spinn_cuda_copy_tensor``).  Any
+        activation when planned with ``PLAN_KEEP``, otherwise graph outputs only."""
+        count = int(dims[0]) - first if count is None else count
+        out = np.empty((count,) + tuple(int(d) for d in dims[1:]), dtype)
+        check(lib().spinn_cuda_copy_tensor(self._h, int(tensor_id), int(first), int(count), out.ctypes.data,
+                                           out.nbytes), "spinn_cuda_copy_tensor")
+        return out
+
     def run(self, x: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
         """Host input -> host output 0 (``spinn_run``)."""
         x = np.ascontiguousarray(x, dtype=np.float32)

@@ -56,3 +56,36 @@ def test_min_profile_keeps_each_steps_minimum():
         pass
     else:
         raise AssertionError("different operators accepted")
+
+
+def test_clock_sampler_queries_only_its_own_gpu(monkeypatch):
+    bench = _bench()
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "4,5,6,7")
+    assert bench.physical_gpu(1) == "5"
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "GPU-aaaa, GPU-bbbb")
+    assert bench.physical_gpu(1) == "GPU-bbbb"
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench.physical_gpu(3) == "3"
+    cmd = bench.ClockSampler("5").command()
+    assert cmd[:3] == ["nvidia-smi", "-i", "5"]
+
+
+def test_tf32_peak_from_sampled_clock():
+    bench = _bench()
+    peak, how = bench.tf32_peak_tflops(148, {"sm_mhz": 1920.0, "sm_max_mhz": 1965.0})
+    assert np.isclose(peak, 2048 * 2 * 148 * 1920e6 / 1e12)  # ~1164 TFLOP/s
+    assert "1920 MHz" in how
+    peak2, how2 = bench.tf32_peak_tflops(148, None)
+    assert np.isclose(peak2, 2048 * 2 * 148 * 1965e6 / 1e12) and "no clock sample" in how2
+
+
+def test_parity_stats():
+    bench = _bench()
+    rng = np.random.default_rng(0)
+    ref = rng.standard_normal((4, 10)) * 1e4
+    p = bench.parity_stats(ref * (1 + 1e-5), ref)
+    assert p["ok"] and p["argmax_agree"] == 4 and p["rel_l2"] < 2e-5
+    bad = ref.copy()
+    bad[0, ref[0].argmax()] -= 1e6
+    q = bench.parity_stats(bad, ref)
+    assert not q["ok"] and q["argmax_agree"] == 3
