@@ -74,8 +74,6 @@ def parse():
     ap.add_argument("--depth", type=int, default=DEPTH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--serial", action="store_true",
-                    help="plan flag SERIAL: run the layers one after another instead of overlapping them")
     return ap.parse_args()
 
 
@@ -348,7 +346,7 @@ def main():
 
     t_build = time.time()
     img, flops_per_step = build_model_image(shard, args.depth)
-    model = runtime.Model(img, device=local, flags=lib.PLAN_PROFILE | (lib.PLAN_SERIAL if args.serial else 0))
+    model = runtime.Model(img, device=local, flags=lib.PLAN_PROFILE)
     info = model.plan_info()
     kinds = model.step_kinds()
     build_s = time.time() - t_build
@@ -482,9 +480,7 @@ def main():
                        "global_batch": args.batch, "per_gpu_batch": shard, "image": IMAGE,
                        "parallelism": f"batch sharded over {world} GPU(s), weight replica per GPU, no collectives",
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
-                       "graph": "CUDA graph of the planned step list",
-                       "layers": "serialized" if args.serial else
-                                 "overlapped (programmatic dependent launches + row-tile readiness counters)"},
+                       "graph": "CUDA graph of the planned step list"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
                          "frac": achieved / tf32_peak if tf32_peak else None,
                          "traffic": None,

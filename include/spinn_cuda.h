@@ -149,19 +149,13 @@ SpinnCudaModel *spinn_cuda_load_buffer(const void *data, size_t size);
  *        (spinn_cuda_run_profiled);
  *        bit 2 = keep activations fp32 on store (no tf32 rounding of conv outputs);
  *        bit 3 = Winograd F(4x4,3x3) for 3x3 stride-1 group-1 convolutions;
- *        bit 4 = keep every intermediate tensor after a run (each gets its own arena range);
- *        bit 5 = serialize the layers.  By default consecutive tensor-core convolutions
- *        overlap: each starts while its producer finishes and waits for the producer's row
- *        tiles through readiness counters; that needs an arena without reuse, so when it would
- *        take more than three quarters of the free device memory (or max_arena_bytes) the plan
- *        falls back to serialized layers with arena reuse on its own. */
+ *        bit 4 = keep every intermediate tensor after a run (each gets its own arena range). */
 #define SPINN_CUDA_PLAN_NO_GRAPH 1
 #define SPINN_CUDA_PLAN_PROFILE 2
 #define SPINN_CUDA_PLAN_NO_ROUND 4
 #define SPINN_CUDA_PLAN_WINOGRAD 8 /* run 3x3 stride-1 convolutions with Winograd F(4x4,3x3) */
 #define SPINN_CUDA_PLAN_KEEP 16    /* keep every intermediate tensor (no arena reuse) for
                                       spinn_cuda_copy_tensor; same kernels and tile plans */
-#define SPINN_CUDA_PLAN_SERIAL 32  /* run layers one after another (see below) */
 int spinn_cuda_plan(SpinnCudaModel *m, int device, uint64_t max_arena_bytes, int flags);
 
 /* Stage 3: run one inference.  Copies input 0 (NCHW fp32, host memory) to the device, runs

@@ -193,23 +193,6 @@ __global__ void wait_expiry_kernel(int* err, unsigned long long timeout_ns) {
   if (threadIdx.x == 0 && !mbar_wait(&bar, 0, &abort_flag, timeout_ns)) atomicExch(err, 2);
 }
 
-// Join of overlapped layers: waits until every readiness counter has reached its target, so
-// that the kernels after it (which wait only for their predecessor in the stream) see every
-// earlier layer complete.  One CTA; bounded by `timeout_ns`, after which it raises the device
-// error flag (code 3) and returns.
-__global__ void __launch_bounds__(256) counters_join_kernel(const int* __restrict__ counters,
-                                                            const int* __restrict__ targets, int n, int* err,
-                                                            unsigned long long timeout_ns) {
-  __shared__ volatile int abort_flag;
-  if (threadIdx.x == 0) abort_flag = 0;
-  __syncthreads();
-  bool ok = true;
-  for (int i = threadIdx.x; i < n && ok; i += blockDim.x) ok = counters_wait(counters, i, i, targets[i], &abort_flag,
-                                                                           timeout_ns);
-  __syncthreads();
-  if (threadIdx.x == 0 && abort_flag) atomicExch(err, 3);
-}
-
 // TopK (SPINN/run_time/ops/tensor/topk.c:20-87): for every row of the last axis, the k largest
 // values in descending order and their int64 indices.  One CTA sorts a row in shared memory
 // (bitonic network over 64-bit keys: order-preserving bits of the value, inverted, above the
@@ -656,13 +639,6 @@ int launch_wait_expiry_selftest(int* err, uint64_t timeout_ns, cudaStream_t s) {
   SPINN_CHECK_ARG(err != nullptr && timeout_ns > 0 && timeout_ns <= 1000000000ull,
                   "wait self-test: timeout %llu ns outside (0, 1 s]", (unsigned long long)timeout_ns);
   wait_expiry_kernel<<<1, 32, 0, s>>>(err, (unsigned long long)timeout_ns);
-  SPINN_LAUNCH_CHECK();
-}
-
-int launch_counters_join(const int* counters, const int* targets, int n, int* err, cudaStream_t s) {
-  SPINN_CHECK_ARG(n >= 0 && (n == 0 || (counters && targets && err)), "counters join: bad arguments");
-  if (n == 0) return 0;
-  counters_join_kernel<<<1, 256, 0, s>>>(counters, targets, n, err, 4000000000ull);
   SPINN_LAUNCH_CHECK();
 }
 

@@ -54,8 +54,6 @@ int sm_count(int device);
 int* device_error_flag(int device);
 // Reads and clears the flag; SPINN_CUDA_ETIMEOUT if it was set.
 int check_device_error_flag(int device, cudaStream_t stream);
-// Waits (one CTA, bounded at 4 s, then *err = 3) until counters[i] >= targets[i] for all i < n.
-int launch_counters_join(const int* counters, const int* targets, int n, int* err, cudaStream_t s);
 // One-thread kernel whose mbarrier wait expires after timeout_ns (<= 1 s) and raises *err.
 int launch_wait_expiry_selftest(int* err, uint64_t timeout_ns, cudaStream_t s);
 
@@ -97,35 +95,7 @@ struct TcGemmArgs {
   // that applies the epilogue; results stay deterministic.
   float* ws = nullptr;
   size_t ws_bytes = 0;
-  // Layer overlap.  The kernels that produced x and res may still be running when this one
-  // starts: they publish finished row tiles in readiness counters (dep_x / dep_res: counters,
-  // rows per counter, value that means "done"), which this launch waits for per work unit.
-  // full_wait = 1 additionally waits for the previous kernel in the stream to complete (inputs
-  // from kernels that publish nothing).  out_flags: counters this launch publishes its own row
-  // tiles in (tc_gemm_plan gives their count, rows per counter and target; not with split-K).
-  const int* dep_x = nullptr;
-  int dep_x_tm = 0, dep_x_target = 0;
-  const int* dep_res = nullptr;
-  int dep_res_tm = 0, dep_res_target = 0;
-  int* out_flags = nullptr;
-  int full_wait = 1;
-  // split-K finish pass: let the next kernel launch before it ends (only when that kernel
-  // waits for it in full)
-  int finish_early_trigger = 1;
 };
-// Tile plan of a launch, as far as a scheduler needs it.
-struct TcPlanInfo {
-  int ksplit = 1;
-  int tm = 128;      // output rows per readiness counter (rows of one work unit)
-  int tiles_m = 0;   // readiness counters the launch publishes (when ksplit == 1)
-  int target = 0;    // counter value once all N tiles of a row tile are stored
-  size_t ws_bytes = 0;
-};
-// The plan a launch of `a` makes, assuming the caller provides the split-K workspace that
-// tc_gemm_workspace_bytes(a) asks for.
-int tc_gemm_plan(const TcGemmArgs& a, TcPlanInfo* info);
-// Layer overlap needs programmatic dependent launch (off with SPINN_NO_PDL).
-bool tc_overlap_available();
 // Workspace a launch of `a` would use (0 when it would not split), for planners.
 size_t tc_gemm_workspace_bytes(const TcGemmArgs& a);
 // Checks whether the tcgen05 path accepts the problem (alignment, corner ranges ...).

@@ -139,51 +139,6 @@ __device__ __forceinline__ void tma_store_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
-// Waits until at most N committed store groups are incomplete (their global writes done).
-template <int N>
-__device__ __forceinline__ void tma_store_wait() {
-  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// ------------------------------------------------------------------ cross-kernel readiness counters
-// A layer whose kernel may still be running publishes finished row tiles through counters in
-// global memory.  Producer: its TMA stores complete (tma_store_wait), then a proxy fence
-// (async-proxy writes before generic-proxy operations), then a release add.  Consumer: an
-// acquire load that sees the target, then a proxy fence before its TMA loads (generic-proxy
-// acquire before async-proxy reads).
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
-  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Bounded wait until counters[t] >= target for every t in [t0, t1]; false (and `abort`
-// raised) after timeout_ns, or when `abort` is raised elsewhere.
-__device__ __forceinline__ bool counters_wait(const int* counters, int t0, int t1, int target, volatile int* abort,
-                                              uint64_t timeout_ns) {
-  uint64_t start = 0;
-  for (int t = t0; t <= t1; ++t) {
-    while (ld_acquire_gpu(counters + t) < target) {
-      if (*abort) return false;
-      const uint64_t now = globaltimer_ns();
-      if (start == 0) {
-        start = now;
-      } else if (now - start > timeout_ns) {
-        *abort = 1;
-        return false;
-      }
-      __nanosleep(64);
-    }
-  }
-  fence_proxy_async_global();
-  return true;
-}
-
 // ------------------------------------------------------------------ programmatic dependent launch
 // A kernel launched with the programmatic-serialization attribute may start while the
 // previous kernel in the stream is finishing; griddep_wait() blocks until that kernel has

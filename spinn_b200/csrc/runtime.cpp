@@ -112,7 +112,6 @@ struct Buf {
   int64_t offset = -1;
   float* ptr = nullptr;
   int first = -1, last = -1;  // step interval of use
-  int flag_step = -1;         // layer overlap: the step that publishes this buffer's row tiles
 };
 
 struct StepRec {
@@ -121,12 +120,6 @@ struct StepRec {
   uint16_t op = 0;
   double flops = 0;
   std::function<int(cudaStream_t)> run;
-  // layer overlap: readiness counters this step publishes ([flag_off, flag_off + flag_count)
-  // of the model's counter buffer, flag_tm rows each, done at flag_target), and the counters
-  // a join before this step waits for ([join_lo, join_hi))
-  int flag_off = -1, flag_count = 0, flag_tm = 0, flag_target = 0;
-  int join_lo = 0, join_hi = 0;
-  bool overlapped = false;  // a tcgen05 conv that waits for its inputs through counters
 };
 
 struct SpinnCudaModel {
@@ -147,15 +140,6 @@ struct SpinnCudaModel {
   float* wdev = nullptr;
   uint64_t wbytes = 0;
   int tc_layers = 0;               // tensor-core conv steps planned so far (tile walk direction)
-  // Layer overlap (default; plan flag SERIAL turns it off): consecutive tcgen05 convolutions
-  // run as programmatic dependents that start while their producer is finishing and wait for
-  // its row tiles through readiness counters.  Needs an arena without reuse (a later layer may
-  // write while an earlier one still reads) and joins before every other kernel.
-  bool overlap = false;
-  int* flagbuf = nullptr;          // [nflags] counters, zeroed at the start of every run
-  int* flag_targets = nullptr;     // [nflags] value of each counter once its row tile is done
-  int nflags = 0;
-  std::vector<int> flag_target_host;
   float* splitk_ws = nullptr;      // split-K partial sums, shared by all steps (one stream)
   size_t splitk_bytes = 0;
   std::vector<float> whost;        // pre-transformed weights before upload
@@ -350,7 +334,7 @@ int plan_arena(SpinnCudaModel* m, int nsteps, uint64_t budget) {
   std::vector<std::vector<int>> born(nsteps + 1), dies(nsteps + 1);
   // SPINN_CUDA_PLAN_KEEP: no buffer is released, so every intermediate keeps its value from
   // the last run (spinn_cuda_copy_tensor); the kernels and their tile plans do not change
-  const bool keep = (m->flags & SPINN_CUDA_PLAN_KEEP) != 0 || m->overlap;
+  const bool keep = (m->flags & SPINN_CUDA_PLAN_KEEP) != 0;
   for (int i = 0; i < (int)m->bufs.size(); ++i) {
     Buf& b = m->bufs[i];
     if (b.alias >= 0 || b.external || b.bytes == 0 || b.first < 0) continue;
@@ -712,52 +696,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             const Buf* ybp = &m->bufs[yb];
             const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
             note_ws(m, a);
-            // layer overlap: wait for the inputs through their producers' readiness counters
-            // (griddepcontrol.wait for inputs from kernels that publish none) and publish this
-            // layer's row tiles, unless it splits K (its finish pass publishes nothing)
-            int xoff = -1, roff = -1, foff = -1;
-            if (m->overlap) {
-              a.x = xbp->ptr;
-              a.y = ybp->ptr;
-              a.res = rbp ? rbp->ptr : nullptr;
-              a.wt = m->wdev + woff;
-              a.bias = boff != ~0ull ? m->wdev + boff : nullptr;
-              TcPlanInfo pi;
-              const int prc = tc_gemm_plan(a, &pi);
-              if (prc) return prc;
-              a.reverse = 0;  // consumers start on the rows their producer finished first
-              a.full_wait = 0;
-              a.finish_early_trigger = 0;
-              const int px = xbp->flag_step;
-              if (px >= 0) {
-                xoff = m->steps[px].flag_off;
-                a.dep_x_tm = m->steps[px].flag_tm;
-                a.dep_x_target = m->steps[px].flag_target;
-              } else {
-                a.full_wait = 1;
-              }
-              if (rbp) {
-                const int pr = rbp->flag_step;
-                if (pr >= 0) {
-                  roff = m->steps[pr].flag_off;
-                  a.dep_res_tm = m->steps[pr].flag_tm;
-                  a.dep_res_target = m->steps[pr].flag_target;
-                } else {
-                  a.full_wait = 1;
-                }
-              }
-              if (pi.ksplit == 1) {
-                r.flag_off = foff = m->nflags;
-                r.flag_count = pi.tiles_m;
-                r.flag_tm = pi.tm;
-                r.flag_target = pi.target;
-                m->nflags += pi.tiles_m;
-                m->flag_target_host.resize(m->nflags, pi.target);
-                m->bufs[yb].flag_step = (int)(&r - m->steps.data());
-              }
-              r.overlapped = true;
-            }
-            r.run = [m, a, xbp, ybp, rbp, woff, boff, xoff, roff, foff](cudaStream_t st) mutable {
+            r.run = [m, a, xbp, ybp, rbp, woff, boff](cudaStream_t st) mutable {
               a.ws = m->splitk_ws;
               a.ws_bytes = m->splitk_bytes;
               a.x = xbp->ptr;
@@ -765,9 +704,6 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
               a.res = rbp ? rbp->ptr : nullptr;
               a.wt = m->wdev + woff;
               a.bias = boff != ~0ull ? m->wdev + boff : nullptr;
-              a.dep_x = xoff >= 0 ? m->flagbuf + xoff : nullptr;
-              a.dep_res = roff >= 0 ? m->flagbuf + roff : nullptr;
-              a.out_flags = foff >= 0 ? m->flagbuf + foff : nullptr;
               return tc_gemm_launch(a, st);
             };
             return 0;
@@ -1557,20 +1493,9 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     P.touch(src, s);
   }
 
-  // arena: without reuse when layers overlap, if that fits the budget (else, or when the device
-  // would be left with less than a quarter of its memory, layers run serialized with reuse)
+  // arena
   const int nsteps = (int)m->steps.size();
-  int rc;
-  if (m->overlap) {
-    size_t free_b = 0, total_b = 0;
-    SPINN_CUDA_TRY(cudaMemGetInfo(&free_b, &total_b));
-    rc = plan_arena(m, nsteps, budget);
-    if (rc || m->arena_bytes > free_b / 4 * 3) {
-      m->overlap = false;
-      for (auto& b : m->bufs) b.offset = -1;
-    }
-  }
-  rc = m->overlap ? 0 : plan_arena(m, nsteps, budget);
+  int rc = plan_arena(m, nsteps, budget);
   if (rc) return rc;
   if (m->arena_bytes) SPINN_CUDA_TRY(cudaMalloc(&m->arena, m->arena_bytes));
   for (auto& b : m->bufs) {
@@ -1594,51 +1519,23 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     SPINN_CUDA_TRY(cudaMemcpy(m->wdev, m->whost.data(), m->wbytes, cudaMemcpyHostToDevice));
   }
   std::vector<float>().swap(m->whost);
-  // closures (in step order: a consumer's builder reads its producers' counter layout)
+  // closures
   m->kernels = 0;
-  int joined = 0;  // counters [0, joined) are covered by an earlier join
   for (int i = 0; i < nsteps; ++i) {
     rc = builders[i](m->steps[i]);
     if (rc) return rc;
     if (m->steps[i].kind != 0) ++m->kernels;
-    if (m->overlap && !m->steps[i].overlapped && m->steps[i].kind != 0) {
-      // any other kernel waits only for its predecessor: join every earlier counter first
-      m->steps[i].join_lo = joined;
-      m->steps[i].join_hi = joined = m->nflags;
-    }
   }
   if (m->splitk_bytes) SPINN_CUDA_TRY(cudaMalloc(&m->splitk_ws, m->splitk_bytes));
-  if (m->nflags) {
-    SPINN_CUDA_TRY(cudaMalloc(&m->flagbuf, (size_t)m->nflags * 4 * 2));
-    m->flag_targets = m->flagbuf + m->nflags;
-    SPINN_CUDA_TRY(cudaMemcpy(m->flag_targets, m->flag_target_host.data(), (size_t)m->nflags * 4,
-                              cudaMemcpyHostToDevice));
-    SPINN_CUDA_TRY(cudaMemset(m->flagbuf, 0, (size_t)m->nflags * 4));
-  }
   return 0;
 }
 
 static int run_steps(SpinnCudaModel* m, cudaStream_t st, bool prof) {
-  // readiness counters start every run at zero
-  if (m->flagbuf) SPINN_CUDA_TRY(cudaMemsetAsync(m->flagbuf, 0, (size_t)m->nflags * 4, st));
-  int* err = device_error_flag(m->device);
-  int joined = 0;
   // External records become real event nodes when captured into a graph (a plain record
   // inside a capture is only an intra-graph dependency marker and is never timestamped).
   for (size_t i = 0; i < m->steps.size(); ++i) {
     if (prof) SPINN_CUDA_TRY(cudaEventRecordWithFlags(m->events[i], st, cudaEventRecordExternal));
-    const StepRec& sr = m->steps[i];
-    if (sr.join_hi > sr.join_lo) {
-      int rc = launch_counters_join(m->flagbuf + sr.join_lo, m->flag_targets + sr.join_lo, sr.join_hi - sr.join_lo,
-                                    err, st);
-      if (rc) return rc;
-      joined = sr.join_hi;
-    }
-    int rc = sr.run(st);
-    if (rc) return rc;
-  }
-  if (joined < m->nflags) {  // the run ends with overlapped layers: nothing may outlive it
-    int rc = launch_counters_join(m->flagbuf + joined, m->flag_targets + joined, m->nflags - joined, err, st);
+    int rc = m->steps[i].run(st);
     if (rc) return rc;
   }
   if (prof) SPINN_CUDA_TRY(cudaEventRecordWithFlags(m->events[m->steps.size()], st, cudaEventRecordExternal));
@@ -1658,7 +1555,6 @@ static void release_model(SpinnCudaModel* m) {
   if (m->arena) cudaFree(m->arena);
   if (m->wdev) cudaFree(m->wdev);
   if (m->splitk_ws) cudaFree(m->splitk_ws);
-  if (m->flagbuf) cudaFree(m->flagbuf);
   if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
   if (m->gexec_alt) cudaGraphExecDestroy(m->gexec_alt);
   if (m->graph_alt) cudaGraphDestroy(m->graph_alt);
@@ -1721,7 +1617,6 @@ __attribute__((visibility("default"))) int spinn_cuda_plan(SpinnCudaModel* m, in
   SPINN_CUDA_TRY(cudaSetDevice(device));
   m->device = device;
   m->flags = flags;
-  m->overlap = !(flags & SPINN_CUDA_PLAN_SERIAL) && tc_overlap_available();
   SPINN_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
   int rc = compile_model(m, max_arena_bytes);
   if (rc) return rc;

@@ -65,37 +65,7 @@ struct TcParams {
   float alpha;
   const float* bias;
   int* err;
-  // Layer overlap: the kernels that produced A and the residual may still be running.  Their
-  // finished row tiles are published in per-tile counters (dep_*: nullptr = none); this
-  // launch publishes its own in out_flags (one counter per TM-row tile of units).
-  const int* dep_a;
-  int dep_a_tm, dep_a_target;
-  const int* dep_r;
-  int dep_r_tm, dep_r_target;
-  // split launches with a residual: the finish pass reads it, so the producer warp waits for
-  // the residual rows of each unit (the unit's own output rows) before its first load
-  const int* dep_o;
-  int dep_o_tm, dep_o_target;
-  int in_h, in_w, kh;  // A's image geometry (im2col mode): input rows a unit reads
-  int* out_flags;
-  int full_wait;  // griddepcontrol.wait before the first access (inputs of non-publishing kernels)
 };
-
-// Input rows [*lo, *hi] (flattened NHWC pixels of A) that output rows [m_first, m_last] read.
-__device__ __forceinline__ void a_input_rows(const TcParams& p, int mode, int m_first, int m_last, long* lo,
-                                             long* hi) {
-  if (mode != kIm2col) {
-    *lo = m_first;
-    *hi = m_last;
-    return;
-  }
-  const int img0 = m_first / p.ohw, oh0 = (m_first - img0 * p.ohw) / p.ow;
-  const int img1 = m_last / p.ohw, oh1 = (m_last - img1 * p.ohw) / p.ow;
-  const int hlo = min(max(oh0 * p.stride_h - p.pad_h, 0), p.in_h - 1);
-  const int hhi = max(min(oh1 * p.stride_h - p.pad_h + (p.kh - 1) * p.dil_h, p.in_h - 1), 0);
-  *lo = ((long)img0 * p.in_h + hlo) * p.in_w;
-  *hi = ((long)img1 * p.in_h + hhi) * p.in_w + p.in_w - 1;
-}
 
 // BK: K depth of one pipeline stage, 32 or 64.  Deeper stages halve the barrier handoffs per
 // K (each handoff costs a few hundred cycles of single-thread latency); CTA pairs use 64 (one
@@ -275,11 +245,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
   if constexpr (PAIR == 2) cluster_sync();  // the peer's barriers are initialised before use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Everything above overlapped the previous kernel's tail.  With full_wait, from here on its
-  // outputs are visible; without it, this launch reads only inputs published through the
-  // readiness counters (dep_a / dep_r), waited for per unit, and its outputs go to memory no
-  // earlier kernel still uses.
-  if (p.full_wait) griddep_wait();
+  // Everything above overlapped the previous kernel's tail; from here on its outputs (our
+  // activations, residual) are visible and the buffers it read may be overwritten.
+  griddep_wait();
   griddep_launch_dependents();
 
   // Work units of this CTA: unit0, unit0 + unit_step, ...  (A dynamic schedule -- units
@@ -322,24 +290,6 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
       if (m0 >= p.M) m0 = tm * TM;  // a pair's second half past the end: load valid rows, store none
       const int nb0 = tn * BN + (int)rank * C::BNC;
       const int kb0 = ks * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
-      if (do_a && p.dep_a) {
-        // the producer kernel may still be running: wait for the input rows these A boxes read
-        long lo, hi;
-        a_input_rows(p, MODE, m0, min(m0 + C::AROWS, p.M) - 1, &lo, &hi);
-        bool ok = true;
-        if (lane == 0)
-          ok = counters_wait(p.dep_a, (int)(lo / p.dep_a_tm), (int)(hi / p.dep_a_tm), p.dep_a_target, abort_flag,
-                             kTimeoutNs);
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      }
-      if (do_a && p.dep_o) {
-        const int r0 = tm * TM;
-        bool ok = true;
-        if (lane == 0 && r0 < p.M)
-          ok = counters_wait(p.dep_o, r0 / p.dep_o_tm, (min(r0 + TM, p.M) - 1) / p.dep_o_tm, p.dep_o_target,
-                             abort_flag, kTimeoutNs);
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      }
       int w0 = 0, h0 = 0, img = 0;
       // im2col walk state for the next box: channel offset c0 inside tap (r, q)
       int c0 = 0, r = 0, q = 0, tap = 0;
@@ -515,10 +465,6 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
           const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
           const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
           bool ok = true;
-          if (p.dep_r && m0 < p.M &&
-              !counters_wait(p.dep_r, m0 / p.dep_r_tm, (min(m0 + kBM * MS, p.M) - 1) / p.dep_r_tm, p.dep_r_target,
-                             abort_flag, kTimeoutNs))
-            break;
           // chunk c goes to group (c + it) % EPI_GROUPS; with two M sub-tiles every chunk
           // goes to both groups, each its own sub-tile's 128 rows
           for (int c = 0; ok && c < BN / 32 && n0 + c * 32 < p.N; ++c) {
@@ -557,13 +503,6 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
     // the finish kernel applies the epilogue after reducing the planes.
     const bool partial = p.ksplit > 1;
     const bool unit_alpha = p.alpha == 1.0f;
-    // Readiness counters (out_flags): each warp commits exactly MYCH store groups per unit
-    // (empty ones where it stores less), so that after a unit, waiting until at most MYCH
-    // groups are incomplete means the previous unit's stores are done; that unit's row tile
-    // is published then, one unit late, without stalling on the stores just issued.
-    constexpr int MYCH = MS == 2 ? BN / 32 : BN / 32 / C::EPI_GROUPS;
-    int prev_tile = -1;
-    bool aborted = false;
     for (;; ++it) {
       const int u = take_unit(it);
       if (u < 0) break;
@@ -579,18 +518,15 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
       // This warp's bias values for the unit (lane l: column n0 + 32 c + l of each chunk c it
       // owns), fetched before the accumulator wait so the load latency is hidden behind it.
       // With two M sub-tiles a group owns every chunk of its sub-tile.
+      constexpr int MYCH = MS == 2 ? BN / 32 : BN / 32 / C::EPI_GROUPS;
       float bias_reg[MYCH];
 #pragma unroll
       for (int i = 0; i < MYCH; ++i) {
         const int col = n0 + 32 * (MS == 2 ? i : i * C::EPI_GROUPS + eo) + lane;
         bias_reg[i] = (!partial && p.bias && col < p.N) ? __ldg(p.bias + col) : 0.0f;
       }
-      if (!warp_wait_backoff(&tfull[b], aph, abort_flag, kTimeoutNs)) {
-        aborted = true;
-        break;
-      }
+      if (!warp_wait_backoff(&tfull[b], aph, abort_flag, kTimeoutNs)) break;
       tc_fence_after();
-      int ncommit = 0;
       const int row0 = m0 + (MS == 2 ? eg * kBM : 0) + wq * 32;
       const bool rows_live = row0 < p.M;
       const uint32_t acc_col = b * (BN * MS) + (MS == 2 ? eg * BN : 0);
@@ -601,10 +537,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
         const float* res_row = nullptr;
         const int rslot = C::RES_G > 0 ? eg * C::RES_G + rcount % C::RES_G : 0;
         if constexpr (RES) {
-          if (!warp_wait(&rfull[rslot], (rcount / C::RES_G) & 1, abort_flag, kTimeoutNs)) {
-            aborted = true;
-            break;
-          }
+          if (!warp_wait(&rfull[rslot], (rcount / C::RES_G) & 1, abort_flag, kTimeoutNs)) break;
           res_row = reinterpret_cast<const float*>(sRes + rslot * C::RES_SLOT) + (wq * 32 + lane) * 32;
         }
         if (rows_live) {
@@ -668,7 +601,6 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
             tma_store_commit();
           }
           ++nstore;
-          ++ncommit;
         }
         if constexpr (RES) {
           __syncwarp();
@@ -676,7 +608,6 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
           ++rcount;
         }
       }
-      if (aborted) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -685,25 +616,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
         else
           mbar_arrive(&tempty[b]);
       }
-      if (p.out_flags) {
-        if (lane == 0) {
-          for (int i = ncommit; i < MYCH; ++i) tma_store_commit();  // empty groups
-          tma_store_wait<MYCH>();  // the previous unit's stores are complete
-          if (prev_tile >= 0) {
-            fence_proxy_async_global();
-            red_release_gpu_add(p.out_flags + prev_tile, 1);
-          }
-        }
-        prev_tile = tm;
-      }
     }
-    if (lane == 0) {
-      tma_store_wait0();
-      if (p.out_flags && prev_tile >= 0 && !aborted && !*abort_flag) {
-        fence_proxy_async_global();
-        red_release_gpu_add(p.out_flags + prev_tile, 1);
-      }
-    }
+    if (lane == 0) tma_store_wait0();
     __syncwarp();
   }
 
@@ -726,13 +640,11 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
 __global__ void __launch_bounds__(256)
     splitk_finish_kernel(const float* __restrict__ ws, int ksplit, int M, int N, int ldw, float alpha,
                          const float* __restrict__ bias, const float* __restrict__ res, int ldr, int act,
-                         int round_out, float* __restrict__ y, int ldy, int early_trigger) {
+                         int round_out, float* __restrict__ y, int ldy) {
   // launched as a programmatic dependent of the split GEMM: its CTAs may be resident before
-  // the partials are complete, and wait here until they are.  The next kernel may start its
-  // prologue early only when it waits for this pass in full (layers serialized); otherwise
-  // it starts when this pass ends.
+  // the partials are complete, and wait here until they are
   griddep_wait();
-  if (early_trigger) griddep_launch_dependents();
+  griddep_launch_dependents();
   const int groups = (N + 3) >> 2;
   const long total = (long)M * groups;
   const size_t plane = (size_t)M * ldw;
@@ -1056,31 +968,6 @@ int problem_cb(const TcGemmArgs& a) { return a.a_mode == 0 ? channel_block(a.cpa
 
 }  // namespace
 
-bool tc_overlap_available() { return pdl_enabled(); }
-
-int tc_gemm_plan(const TcGemmArgs& a, TcPlanInfo* info) {
-  std::string why;
-  if (!tc_gemm_supported(a, &why)) {
-    set_error("tcgen05 gemm: %s", why.c_str());
-    return SPINN_CUDA_EINVAL;
-  }
-  int dev = 0;
-  SPINN_CUDA_TRY(cudaGetDevice(&dev));
-  // the plan a launch makes when its caller provides the workspace tc_gemm_workspace_bytes
-  // asks for (any larger workspace leads to the same plan)
-  const size_t ws_limit = a.batch == 1 ? kWsCap : 0;
-  const TilePlan tp =
-      plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), ws_limit, a.bn, a.batch == 1);
-  info->ksplit = tp.ksplit;
-  info->tm = kBM * tp.pair * tp.ms;
-  info->tiles_m = (a.M + info->tm - 1) / info->tm;
-  const int tiles_n = (a.N + tp.bn - 1) / tp.bn;
-  const int epi_warps = (a.res && tp.bn == 256) ? 4 : 8;  // Cfg::EPI_WARPS
-  info->target = tiles_n * epi_warps * tp.pair;
-  info->ws_bytes = tp.ws_bytes;
-  return 0;
-}
-
 size_t tc_gemm_workspace_bytes(const TcGemmArgs& a) {
   if (!tc_gemm_supported(a, nullptr) || a.batch > 1) return 0;
   int dev = 0;
@@ -1212,25 +1099,6 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   p.alpha = a.alpha;
   p.bias = a.bias;
   p.err = a.err ? a.err : device_error_flag(dev);
-  p.dep_a = a.dep_x;
-  p.dep_a_tm = a.dep_x_tm;
-  p.dep_a_target = a.dep_x_target;
-  p.dep_r = p.has_res ? a.dep_res : nullptr;
-  p.dep_r_tm = a.dep_res_tm;
-  p.dep_r_target = a.dep_res_target;
-  p.dep_o = (a.res && split) ? a.dep_res : nullptr;
-  p.dep_o_tm = a.dep_res_tm;
-  p.dep_o_target = a.dep_res_target;
-  p.in_h = a.h;
-  p.in_w = a.w;
-  p.kh = a.kh;
-  // a split launch publishes nothing: its consumers wait for the finish pass in full
-  p.out_flags = split ? nullptr : a.out_flags;
-  p.full_wait = a.full_wait ? 1 : 0;
-  if ((p.dep_a && p.dep_a_tm <= 0) || (a.dep_res && a.dep_res_tm <= 0)) {
-    set_error("tcgen05 gemm: readiness counters without a row-tile size");
-    return SPINN_CUDA_EINVAL;
-  }
   const int pr = tp.pair, ms = tp.ms, wr = tp.wr;
   if (a.a_mode == 0)
     rc = p.has_res ? dispatch_bn_cb<kIm2col, true>(bn, cb, pr, tp.bk, ms, wr, ma, mb, my, mr, p, sms, stream)
@@ -1251,7 +1119,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   cfg.attrs = &attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   SPINN_CUDA_TRY(cudaLaunchKernelEx(&cfg, splitk_finish_kernel, (const float*)a.ws, tp.ksplit, a.M, a.N, ldw, a.alpha,
-                                    a.bias, a.res, a.ldr, a.act, a.round_out, a.y, a.ldy, a.finish_early_trigger));
+                                    a.bias, a.res, a.ldr, a.act, a.round_out, a.y, a.ldy));
   SPINN_CUDA_TRY(cudaGetLastError());
   return 0;
 }

@@ -163,27 +163,3 @@ def test_copy_tensor_needs_keep_for_intermediates(cuda_lib):
     with pytest.raises(lib.SpinnCudaError):
         k.tensor(conv_out, em.tensors[conv_out].dims, 2, 1)  # past the batch
     k.close()
-
-
-@pytest.mark.parametrize("case", ["resnet101-b32", "resnet50-b3-96px", "yolo-b2-320"])
-def test_layer_overlap_matches_serialized_layers(cuda_lib, case):
-    """The default plan overlaps consecutive tensor-core convolutions (each waits for its
-    producer's row tiles through readiness counters); plan flag SERIAL runs the same kernels
-    one after another.  Every element is computed by the same instructions in both, so the
-    outputs must be bit-identical, run after run."""
-    from spinn_b200 import ennf, lib, netdef, runtime
-    if case == "resnet101-b32":
-        img, x = _bench_model_image(32), netdef.image_batch(224, 32, IMAGE, seed=SEED)
-    elif case == "resnet50-b3-96px":
-        img, x = ennf.convert(netdef.resnet(50, batch=3, image=96, seed=5)), netdef.resnet_input(3, 96, seed=5)
-    else:
-        img, x = ennf.convert(netdef.yolo_shaped(batch=2, image=320)), netdef.yolo_input(2, 320)
-    serial = runtime.Model(img, flags=lib.PLAN_SERIAL)
-    ref = serial.run(x)
-    serial.close()
-    for flags in (0, lib.PLAN_NO_GRAPH):
-        m = runtime.Model(img, flags=flags)
-        for _ in range(3):
-            y = m.run(x)
-            assert np.array_equal(y, ref), float(np.abs(y - ref).max())
-        m.close()
