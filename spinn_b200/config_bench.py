@@ -70,9 +70,19 @@ def layer(a) -> int:
         g, x = netdef.conv_bn_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k, stride=a.stride, pad=pad,
                                    group=a.group)
     from spinn_b200 import ennf, runtime
-    model = runtime.Model(ennf.convert(g), flags=lib.PLAN_WINOGRAD if a.winograd else 0)
+    model = runtime.Model(ennf.convert(g), flags=(lib.PLAN_WINOGRAD if a.winograd else 0) | lib.PLAN_PROFILE)
     model.run(x)  # stages the input on the device
     ms = _time(model, a.iters, a.warmup)
+    # the convolution steps alone (the model also converts layouts at its input and output):
+    # each step's minimum over profiled replays
+    import torch
+    stream = torch.cuda.Stream()
+    prof = None
+    for _ in range(max(3, a.warmup)):
+        model.run_profiled(stream.cuda_stream)
+        cur = model.profile()
+        prof = cur if prof is None else [(o, min(t, pt), f) for (o, t, f), (_, pt, _) in zip(cur, prof)]
+    conv_ms = sum(t for (o, t, f), k in zip(prof, model.step_kinds()) if o == ennf.OP["Conv"])
     oc = a.c if a.residual else a.oc
     oh = a.hw if a.projection else (a.hw + 2 * pad - a.k) // a.stride + 1
     cin = a.c // a.group
@@ -84,7 +94,8 @@ def layer(a) -> int:
                   + a.batch * oh * oh * oc * ((3 if a.projection else 2) if res else 1)
                   + oc * cin * (a.k * a.k + (1 if a.projection else 0)))
     print(json.dumps({"layer": {k: v for k, v in vars(a).items() if k != "only"}, "ms_per_run": ms,
-                      "tflops": flops / ms / 1e9, "gbs": byts / ms / 1e6, "steps": model.plan_info()["steps"],
+                      "conv_ms": conv_ms, "tflops": flops / conv_ms / 1e9, "gbs": byts / conv_ms / 1e6,
+                      "algorithmic_mb": byts / 1e6, "steps": model.plan_info()["steps"],
                       "kinds": model.step_kinds()}), flush=True)
     model.close()
     return 0

@@ -441,6 +441,144 @@ __global__ void depthwise_kernel(const float4* __restrict__ x, const float4* __r
   }
 }
 
+// Depthwise 3x3 convolution (dilation 1, stride S = 1 or 2), NHWC, persistent CTAs.  A work
+// unit is a tile of 8 x TW output pixels (TW = 16 at stride 1, 8 at stride 2) x 32 channels of
+// one image.  One thread per CTA loads the unit's input window (its halo included) with a
+// single 4-D TMA box -- each pixel's 32-channel slice is one 128-B line, out-of-range pixels
+// and channels arrive as zeros, which is the convolution's zero padding -- into one of two
+// shared-memory buffers, so the next unit's window is in flight while the CTA computes the
+// current one: HBM sees each input byte about once, the halo comes from L2.  Thread (p, q)
+// computes channel quad q of output pixels p, p + 32, ... with the taps in the order r, then s,
+// and applies the epilogue of depthwise_kernel (bias, residual, activation, tf32 rounding).
+// w is [9][cpad], bias [cpad], residual NHWC like y.  Waits are bounded; on expiry the CTA
+// raises *err (code 4) and stops.
+constexpr int kDwThreads = 256;
+template <int S>
+struct DwTile {
+  static constexpr int TH = 8, TW = S == 1 ? 16 : 8;
+  static constexpr int IH = (TH - 1) * S + 3, IW = (TW - 1) * S + 3;
+  static constexpr uint32_t BYTES = IH * IW * 128;  // one window: IH x IW pixels x 32 channels
+  static constexpr int PIX = TH * TW / (kDwThreads / 8);  // output pixels per thread
+};
+
+template <int S>
+__global__ void __launch_bounds__(kDwThreads) depthwise3x3_tma_kernel(
+    const __grid_constant__ CUtensorMap mx, const float4* __restrict__ w, const float4* __restrict__ bias,
+    const float4* __restrict__ res, float4* __restrict__ y, int n, int c4, int oh, int ow, int ph, int pw,
+    int tiles_x, int tiles_y, int groups, int act, int round_out, int* err) {
+  using T = DwTile<S>;
+  extern __shared__ uint8_t dw_raw[];
+  float4* buf = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(dw_raw) + 127) & ~uintptr_t(127));
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ volatile int abort_flag;
+  const long units = (long)groups * n * tiles_y * tiles_x;
+  auto unit_coords = [&](long u, int* g, int* b, int* ty, int* tx) {
+    *tx = (int)(u % tiles_x);
+    long r = u / tiles_x;
+    *ty = (int)(r % tiles_y);
+    r /= tiles_y;
+    *b = (int)(r % n);
+    *g = (int)(r / n);
+  };
+  auto issue = [&](long u, int slot) {
+    int g, b, ty, tx;
+    unit_coords(u, &g, &b, &ty, &tx);
+    mbar_arrive_expect_tx(&full[slot], T::BYTES);
+    tma_load_4d(&mx, &full[slot], buf + (size_t)slot * (T::BYTES / 16), g * 32, tx * T::TW * S - pw,
+                ty * T::TH * S - ph, b);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && (long)blockIdx.x < units) {
+    prefetch_tmap(&mx);
+    issue(blockIdx.x, 0);
+  }
+  const int q = threadIdx.x & 7, slot_p = threadIdx.x >> 3;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  // thread 0's record of loads in flight: bit s set while buffer s awaits the phase in bit s of armed_ph
+  uint32_t armed = (long)blockIdx.x < units ? 1u : 0u, armed_ph = 0;
+  int it = 0;
+  for (long u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    const int cur = it & 1;
+    const long nu = u + gridDim.x;
+    if (threadIdx.x == 0 && nu < units) {  // the other buffer was released by the last iteration's barrier
+      issue(nu, cur ^ 1);
+      armed |= 1u << (cur ^ 1);
+      armed_ph = (armed_ph & ~(1u << (cur ^ 1))) | ((uint32_t)(((it + 1) >> 1) & 1) << (cur ^ 1));
+    }
+    bool ok = mbar_wait(&full[cur], (it >> 1) & 1, &abort_flag, 4000000000ull);
+    if (!__syncthreads_and(ok)) break;
+    if (threadIdx.x == 0) armed &= ~(1u << cur);
+    int g, b, ty, tx;
+    unit_coords(u, &g, &b, &ty, &tx);
+    const int qq = g * 8 + q;  // channel quad
+    if (qq < c4) {
+      float4 k[9];
+#pragma unroll
+      for (int t = 0; t < 9; ++t) k[t] = __ldg(w + (size_t)t * c4 + qq);
+      const float4 bb = bias ? __ldg(bias + qq) : zero;
+      const float4* win = buf + (size_t)cur * (T::BYTES / 16);
+#pragma unroll
+      for (int j = 0; j < T::PIX; ++j) {
+        const int p = slot_p + j * (kDwThreads / 8);
+        const int ly = p / T::TW, lx = p - ly * T::TW;
+        const int oy = ty * T::TH + ly, ox = tx * T::TW + lx;
+        if (oy >= oh || ox >= ow) continue;
+        float4 acc = zero;
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+          for (int s = 0; s < 3; ++s) {
+            const float4 v = win[((ly * S + r) * T::IW + lx * S + s) * 8 + q];
+            const float4 kk = k[r * 3 + s];
+            acc.x = fmaf(v.x, kk.x, acc.x);
+            acc.y = fmaf(v.y, kk.y, acc.y);
+            acc.z = fmaf(v.z, kk.z, acc.z);
+            acc.w = fmaf(v.w, kk.w, acc.w);
+          }
+        if (bias) {
+          acc.x += bb.x;
+          acc.y += bb.y;
+          acc.z += bb.z;
+          acc.w += bb.w;
+        }
+        const size_t o = (((size_t)b * oh + oy) * ow + ox) * c4 + qq;
+        if (res && (act == 4 || act == 5)) {
+          const float4 rr = res[o];
+          acc.x += rr.x;
+          acc.y += rr.y;
+          acc.z += rr.z;
+          acc.w += rr.w;
+        }
+        acc.x = apply_act(acc.x, act);
+        acc.y = apply_act(acc.y, act);
+        acc.z = apply_act(acc.z, act);
+        acc.w = apply_act(acc.w, act);
+        if (round_out) {
+          acc.x = to_tf32_rna(acc.x);
+          acc.y = to_tf32_rna(acc.y);
+          acc.z = to_tf32_rna(acc.z);
+          acc.w = to_tf32_rna(acc.w);
+        }
+        y[o] = acc;
+      }
+    }
+    __syncthreads();  // every thread is done with buffer `cur`; the next iteration may refill it
+  }
+  if (threadIdx.x == 0 && abort_flag) {
+    // let any window still in flight land before the CTA's shared memory goes away
+    volatile int dummy = 0;
+    for (int sl = 0; sl < 2; ++sl)
+      if (armed & (1u << sl)) mbar_wait(&full[sl], (armed_ph >> sl) & 1, &dummy, 200000000ull);
+    atomicExch(err, 4);
+  }
+}
+
 // Generic grouped direct convolution, NHWC, one output element per thread (CUDA cores).
 // w is [oc][kh][kw][c/group].
 __global__ void grouped_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -756,10 +894,48 @@ int launch_channel_affine_nhwc(const float* x, float* y, long pixels, int cpad, 
   SPINN_LAUNCH_CHECK();
 }
 
+template <int S>
+int launch_depthwise3x3_tma(const float* x, const float* w, const float* bias, const float* res, float* y, int n,
+                            int h, int wd, int cpad, int oh, int ow, int ph, int pw, int act, int round_out, int dev,
+                            cudaStream_t s) {
+  using T = DwTile<S>;
+  CUtensorMap mx;
+  int rc = encode_nhwc_window(&mx, x, n, h, wd, cpad, 32, T::IW, T::IH);
+  if (rc) return rc;
+  const int tiles_x = (ow + T::TW - 1) / T::TW, tiles_y = (oh + T::TH - 1) / T::TH;
+  const int groups = (cpad / 4 + 7) / 8;
+  const long units = (long)groups * n * tiles_y * tiles_x;
+  const int smem = (int)(2 * T::BYTES + 128);
+  static std::atomic<uint64_t> configured{0};
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    SPINN_CUDA_TRY(cudaFuncSetAttribute(depthwise3x3_tma_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured.fetch_or(bit);
+  }
+  int per_sm = 0;
+  SPINN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, depthwise3x3_tma_kernel<S>, kDwThreads, smem));
+  const long grid = std::min<long>(units, (long)sm_count(dev) * std::max(per_sm, 1));
+  if (grid <= 0) return 0;
+  depthwise3x3_tma_kernel<S><<<(int)grid, kDwThreads, smem, s>>>(
+      mx, reinterpret_cast<const float4*>(w), reinterpret_cast<const float4*>(bias),
+      reinterpret_cast<const float4*>(res), reinterpret_cast<float4*>(y), n, cpad / 4, oh, ow, ph, pw, tiles_x,
+      tiles_y, groups, act, round_out, device_error_flag(dev));
+  SPINN_LAUNCH_CHECK();
+}
+
 int launch_depthwise_nhwc(const float* x, const float* w, const float* bias, const float* res, float* y, int n, int h,
                           int wd, int cpad, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int dh,
                           int dw, int act, int round_out, cudaStream_t s) {
   SPINN_CHECK_ARG(cpad % 4 == 0, "depthwise: channel stride %d not a multiple of 4", cpad);
+  if (kh == 3 && kw == 3 && dh == 1 && dw == 1 && sh == sw && (sh == 1 || sh == 2) && ph >= 0 && pw >= 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    int dev = 0;
+    SPINN_CUDA_TRY(cudaGetDevice(&dev));
+    return sh == 1 ? launch_depthwise3x3_tma<1>(x, w, bias, res, y, n, h, wd, cpad, oh, ow, ph, pw, act, round_out,
+                                                 dev, s)
+                   : launch_depthwise3x3_tma<2>(x, w, bias, res, y, n, h, wd, cpad, oh, ow, ph, pw, act, round_out,
+                                                 dev, s);
+  }
   const long work = (long)n * oh * ow * (cpad / 4);
   const long span = (long)grid_for(work, kEltThreads) * kEltThreads;  // the loop index reaches work + span
   if (work < (1l << 31) - span)

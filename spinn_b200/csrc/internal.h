@@ -43,6 +43,10 @@ int encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
 // 3-D tiled map of `planes` row-major [outer][inner] matrices stored back to back.
 int encode_tiled_3d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t planes,
                     uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+// 4-D tiled map of an NHWC tensor [n][h][w][cpad] whose boxes are windows of box_h x box_w
+// pixels x box_c channels (no swizzle; out-of-range pixels and channels read as zeros).
+int encode_nhwc_window(CUtensorMap* map, const void* base, int n, int h, int w, int cpad, uint32_t box_c,
+                       uint32_t box_w, uint32_t box_h);
 int encode_im2col_4d(CUtensorMap* map, const void* base, int n, int h, int w, int c,
                      int lower_w, int lower_h, int upper_w, int upper_h, int channels_per_pixel,
                      int pixels_per_column, int stride_w, int stride_h, CUtensorMapSwizzle swizzle);

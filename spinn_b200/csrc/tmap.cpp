@@ -106,6 +106,31 @@ int encode_tiled_3d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   return 0;
 }
 
+int encode_nhwc_window(CUtensorMap* map, const void* base, int n, int h, int w, int cpad, uint32_t box_c,
+                       uint32_t box_w, uint32_t box_h) {
+  std::call_once(g_once, load_entry_points);
+  if (!g_tiled) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return SPINN_CUDA_ECUDA;
+  }
+  SPINN_CHECK_ARG((reinterpret_cast<uintptr_t>(base) & 15) == 0, "tensor map base %p not 16-B aligned", base);
+  SPINN_CHECK_ARG(cpad % 4 == 0 && (box_c * 4) % 16 == 0, "NHWC window: channel stride %d / box %u", cpad, box_c);
+  cuuint64_t dims[4] = {(cuuint64_t)cpad, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
+  cuuint64_t strides[3] = {(cuuint64_t)cpad * 4, (cuuint64_t)cpad * 4 * w, (cuuint64_t)cpad * 4 * w * h};
+  cuuint32_t box[4] = {box_c, box_w, box_h, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (NHWC window) failed (%d): nhwc %d %d %d %d box %u %u %u", (int)r, n, h, w,
+              cpad, box_c, box_w, box_h);
+    return SPINN_CUDA_ECUDA;
+  }
+  small_tensor_fixup(map, (uint64_t)cpad * 4 * w * h * n);
+  return 0;
+}
+
 int encode_im2col_4d(CUtensorMap* map, const void* base, int n, int h, int w, int c, int lower_w, int lower_h,
                      int upper_w, int upper_h, int channels_per_pixel, int pixels_per_column, int stride_w,
                      int stride_h, CUtensorMapSwizzle swizzle) {

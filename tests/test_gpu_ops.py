@@ -36,7 +36,12 @@ CONV_CASES = [
     (1, 1024, 14, 14, 256, 1, 1, 0, 1, 1, True, False),  # deep K
     (1, 256, 7, 7, 256, 3, 1, 1, 1, 5, True, True),      # split-K (2 tiles, 72 K blocks) + residual in the finish
     (3, 512, 7, 7, 2048, 1, 1, 0, 1, 3, True, False),    # split-K, SiLU applied after the reduction
-    (1, 32, 40, 40, 32, 3, 1, 1, 32, 3, True, False),    # depthwise (CUDA cores)
+    (1, 32, 40, 40, 32, 3, 1, 1, 32, 3, True, False),    # depthwise (shared-memory spatial tiles)
+    (2, 36, 17, 23, 36, 3, 2, 1, 36, 1, True, False),    # depthwise, stride 2, a partial 32-channel group
+    (1, 64, 31, 29, 64, 5, 1, 2, 64, 3, True, False),    # depthwise 5x5, ragged tiles, SiLU
+    (2, 96, 20, 20, 96, 3, 1, 1, 96, 5, True, True),     # depthwise + residual + ReLU
+    (1, 128, 9, 40, 128, 3, 2, 1, 128, 0, False, False),  # depthwise, stride 2, no bias
+    (4, 128, 80, 80, 128, 3, 2, 1, 128, 3, True, False),  # depthwise, YOLO-shaped downsampling
     (1, 32, 10, 10, 64, 3, 1, 1, 4, 1, True, False),     # grouped (CUDA cores)
     (2, 16, 20, 20, 64, 3, 1, 1, 1, 1, True, False),     # C=16, N=64, K=144: resident-weight shapes fit
     (2, 64, 9, 11, 40, 1, 1, 0, 1, 3, True, False),      # 1x1, N=40 < 64, K=64, ragged everything
