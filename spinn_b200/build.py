@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libspinn_cuda.so")
-SOURCES = ["tmap.cpp", "tc_gemm.cu", "glue.cu", "runtime.cpp", "abi.cpp", "noalloc.cu", "winograd.cu"]
+SOURCES = ["tmap.cpp", "tc_gemm.cu", "glue.cu", "runtime.cpp", "abi.cpp", "noalloc.cu", "winograd.cu", "tail.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",

@@ -108,6 +108,28 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);
 // Number of K blocks (32 wide) and padded K the weight matrix must have.
 inline int tc_num_kb(int K) { return (K + 31) / 32; }
 
+// ------------------------------------------------------------------ bottleneck tail (tail.cu)
+// One launch for a 1x1 expand with a fused residual followed by a 1x1 reduce of its output:
+//   y = act_e(t2 * W3^T + b3 + x),  t = act_r(y * W1^T + b1)
+// over M rows (pixels, NHWC), t2 [M][k1], x and y [M][n1], t [M][n2]; weights K-major
+// W3 [n1][kpad3], W1 [n2][kpad1] (tf32-rounded), act_e 4 (+residual) or 5 (+residual, ReLU),
+// act_r 0 or 1 (ReLU).  y is written once and reused from shared memory by the reduce.
+struct TailArgs {
+  const float* t2 = nullptr;
+  const float* x = nullptr;
+  const float* w3 = nullptr;
+  const float* b3 = nullptr;
+  const float* w1 = nullptr;
+  const float* b1 = nullptr;
+  float* y = nullptr;
+  float* t = nullptr;
+  int M = 0, k1 = 0, n1 = 0, n2 = 0, kpad3 = 0, kpad1 = 0;
+  int act_e = 5, act_r = 1, round_out = 1;
+  int* err = nullptr;  // device error word; nullptr = the per-device flag
+};
+bool tail_fused_supported(const TailArgs& a, std::string* why);
+int tail_fused_launch(const TailArgs& a, cudaStream_t stream);
+
 // ------------------------------------------------------------------ Winograd F(4x4,3x3) (winograd.cu)
 // 3x3 stride-1 convolution of NHWC x[n][h][w][cpad] into y[n][oh][ow][ocpad] through the
 // transform buffers v [36][tiles][3*cpad] and m [36][tiles][ocpad]

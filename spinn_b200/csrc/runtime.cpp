@@ -589,6 +589,92 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         const int rnd = P.round_out;
         const bool wino = (m->flags & SPINN_CUDA_PLAN_WINOGRAD) && G == 1 && !s2d && KH == 3 && KW == 3 && SH == 1 &&
                           SW == 1 && DH == 1 && DW == 1;
+        // Bottleneck tail: this 1x1 expand with a fused residual, followed by a 1x1 reduce of
+        // its output (the next block's first convolution), runs as one kernel that keeps y's
+        // chunks in shared memory for the reduce (tail.cu) -- when there are rows enough for
+        // two waves of 128-row tiles (with fewer, the separate launches spread over more SMs).
+        const NodeRec* nb = ni + 1 < (int)m->nodes.size() ? &m->nodes[ni + 1] : nullptr;
+        int oc2 = 0, act2 = 0;
+        const TensorRec* W2 = nullptr;
+        const TensorRec* B2 = nullptr;
+        bool tail = false;
+        if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && !wino && !s2d && G == 1 && KH == 1 && KW == 1 && SH == 1 &&
+            SW == 1 && PH == 0 && PW == 0 && OH == H && OW == Wd && has_res && n_real == 3 && C % 32 == 0 &&
+            OC % 128 == 0 && nb && nb->op == OP_CONV && nb->in.size() == 3 && nb->out.size() == 1 &&
+            nb->in[0] == nd.out[0] && (long)N * H * Wd >= 2L * 128 * sm_count(m->device)) {
+          ConvParams c2{};
+          if (nb->params.size() >= sizeof(ConvParams)) std::memcpy(&c2, nb->params.data(), sizeof(c2));
+          W2 = &m->tensors[nb->in[1]];
+          B2 = &m->tensors[nb->in[2]];
+          const TensorRec& Y2 = m->tensors[nb->out[0]];
+          act2 = c2.fused_act;
+          const int g2 = c2.group > 0 ? c2.group : 1;
+          oc2 = W2->ndim == 4 ? (int)W2->dims[0] : 0;
+          tail = (act2 == 0 || act2 == 1) && g2 == 1 && W2->ndim == 4 && W2->host && B2->host && W2->dims[1] == (uint32_t)OC &&
+                 W2->dims[2] == 1 && W2->dims[3] == 1 && (c2.kernel_shape[0] <= 1) && (c2.kernel_shape[1] <= 1) &&
+                 (c2.strides[0] <= 1) && (c2.strides[1] <= 1) && c2.pads[0] == 0 && c2.pads[1] == 0 &&
+                 c2.pads[2] == 0 && c2.pads[3] == 0 && c2.auto_pad == 0 && oc2 % 32 == 0 && oc2 >= 32 &&
+                 oc2 <= 256 && Y2.ndim == 4 && Y2.dims[1] == (uint32_t)oc2 && Y2.dims[2] == (uint32_t)OH &&
+                 Y2.dims[3] == (uint32_t)OW;
+        }
+        if (tail) {
+          const TensorRec* B = (n_real > 2 && m->tensors[nd.in[2]].host) ? &m->tensors[nd.in[2]] : nullptr;
+          const int xb = ensure_nhwc(nd.in[0], ni);
+          const int rb = ensure_nhwc(nd.in.back(), ni);
+          if (xb < 0 || rb < 0) {
+            set_error("plan: Conv node %d inputs are not 4-D", ni);
+            return SPINN_CUDA_EUNSUPPORTED;
+          }
+          const int yb = nd.out[0], tb = nb->out[0];
+          set_nhwc(m->bufs[yb], Y);
+          set_nhwc(m->bufs[tb], m->tensors[tb]);
+          // weights K-major, tf32-rounded: W3 [OC][C], W1 [oc2][OC]
+          const uint64_t w3 = P.wreserve((uint64_t)OC * C), w1 = P.wreserve((uint64_t)oc2 * OC);
+          for (uint64_t i = 0; i < (uint64_t)OC * C; ++i) m->whost[w3 + i] = host_round_tf32(W.host[i]);
+          for (uint64_t i = 0; i < (uint64_t)oc2 * OC; ++i) m->whost[w1 + i] = host_round_tf32(W2->host[i]);
+          const uint64_t b3 = P.wreserve(OC), b1 = P.wreserve(oc2);
+          for (int o = 0; o < OC; ++o) m->whost[b3 + o] = B ? B->host[o] : 0.0f;
+          for (int o = 0; o < oc2; ++o) m->whost[b1 + o] = B2->host[o];
+          const double fl = conv_flops(W, Y) + conv_flops(*W2, m->tensors[tb]);
+          const int rnd = P.round_out, M = N * H * Wd, n1 = OC, k1 = C, n2 = oc2, ae = act, ar = act2;
+          const int s = add_step(ni, OP_CONV, 9, fl, [=](StepRec& r) {
+            const Buf* xbp = &m->bufs[xb];
+            const Buf* rbp = &m->bufs[rb];
+            const Buf* ybp = &m->bufs[yb];
+            const Buf* tbp = &m->bufs[tb];
+            m->tc_layers |= 1;  // the next layer walks its tiles from the end, where this one stopped
+            r.run = [=](cudaStream_t st) {
+              TailArgs a;
+              a.t2 = xbp->ptr;
+              a.x = rbp->ptr;
+              a.w3 = m->wdev + w3;
+              a.w1 = m->wdev + w1;
+              a.b3 = m->wdev + b3;
+              a.b1 = m->wdev + b1;
+              a.y = ybp->ptr;
+              a.t = tbp->ptr;
+              a.M = M;
+              a.k1 = k1;
+              a.n1 = n1;
+              a.n2 = n2;
+              a.kpad3 = k1;
+              a.kpad1 = n1;
+              a.act_e = ae;
+              a.act_r = ar;
+              a.round_out = rnd;
+              return tail_fused_launch(a, st);
+            };
+            return 0;
+          });
+          P.touch(xb, s);
+          P.touch(rb, s);
+          P.touch(yb, s);
+          P.touch(tb, s);
+          produced[yb] = 1;
+          produced[tb] = 1;
+          ++ni;  // the reduce node is part of this step
+          break;
+        }
         if (wino) {
           // Winograd F(4x4,3x3): transforms in HBM, 36 tcgen05 GEMMs (winograd.cu)
           const int kpad = tc_num_kb(3 * cpad) * 32;

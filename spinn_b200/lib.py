@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(HERE, "libspinn_cuda.so")
 
 # Status codes (include/spinn_cuda.h)
 OK, EINVAL, ENOMEM, ECUDA, EUNSUPPORTED, ETIMEOUT, EFORMAT, ESTATE = 0, -1, -2, -3, -4, -5, -6, -7
-PLAN_NO_GRAPH, PLAN_PROFILE, PLAN_NO_ROUND, PLAN_WINOGRAD, PLAN_KEEP = 1, 2, 4, 8, 16
+PLAN_NO_GRAPH, PLAN_PROFILE, PLAN_NO_ROUND, PLAN_WINOGRAD, PLAN_KEEP, PLAN_NO_FUSE = 1, 2, 4, 8, 16, 32
 
 # ENNF operator codes (SPINN/ennf_op_types.h:79,134,135)
 OP_CONV, OP_GEMM, OP_MATMUL = 60, 160, 161
