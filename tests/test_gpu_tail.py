@@ -41,13 +41,13 @@ def _run(img, x, flags):
     return y, kinds
 
 
-# rows = batch * hw^2 must reach two waves of 128-row tiles on 148 SMs (37,888)
+# rows = batch * hw^2 must reach eight waves of 128-row tiles on 148 SMs (151,552)
 TAIL_CASES = [
-    # batch, hw, n1, k1, n2, relu on the reduce
-    (2, 140, 256, 64, 64, True),     # 39,200 rows: a partial last tile
-    (1, 200, 512, 128, 128, True),   # 40,000 rows
-    (3, 115, 1024, 256, 256, True),  # 39,675 rows, the ResNet 14x14-stage widths
-    (2, 139, 256, 32, 96, False),    # 38,642 rows, K1 = 32, no ReLU after the reduce
+    # batch, hw, n1, k1, n2, relu on the reduce (the planner fuses expands of <= 64 input channels)
+    (4, 199, 256, 64, 64, True),     # 158,404 rows: a partial last tile; the ResNet 56x56-stage widths
+    (4, 200, 512, 64, 128, True),    # 160,000 rows
+    (3, 225, 1024, 64, 256, True),   # 151,875 rows, the widest reduce the kernel takes
+    (5, 175, 256, 32, 96, False),    # 153,125 rows, K1 = 32, no ReLU after the reduce
 ]
 
 
@@ -71,20 +71,20 @@ def test_tail_fused_matches_unfused_and_reference(cuda_lib, ref_oracle, tmp_path
 
 
 def test_tail_fused_resnet50_stage1(cuda_lib, ref_oracle, tmp_path):
-    """ResNet-50 at batch 16: the 56x56 stage has 50,176 rows, so its three block ends fuse
+    """ResNet-50 at batch 64: the 56x56 stage has 200,704 rows, so its three block ends fuse
     (the first one is the stride-1 projection that carries the residual)."""
     from spinn_b200 import ennf, lib, netdef
-    g = netdef.resnet(50, batch=16, seed=2)
-    x = netdef.resnet_input(16, seed=2)
+    g = netdef.resnet(50, batch=64, seed=2)
+    x = netdef.resnet_input(64, seed=2)
     img = ennf.convert(g)
     fused, kinds = _run(img, x, 0)
     assert kinds.count(9) == 3, kinds
     plain, _ = _run(img, x, lib.PLAN_NO_FUSE)
-    fused, plain = fused.reshape(16, -1), plain.reshape(16, -1)
+    fused, plain = fused.reshape(64, -1), plain.reshape(64, -1)
     assert rel_l2(fused, plain) <= 1e-6, rel_l2(fused, plain)
     p = tmp_path / "r50.ennf"
     p.write_bytes(img)
-    ref = list(ref_oracle.run_model(str(p), x).values())[0].reshape(16, -1)
+    ref = list(ref_oracle.run_model(str(p), x).values())[0].reshape(64, -1)
     assert rel_l2(fused, ref) <= 2e-3, rel_l2(fused, ref)
     assert float(np.abs(fused - ref).max()) <= 1e-2 * float(np.abs(ref).max())
     assert (fused.argmax(1) == ref.argmax(1)).all()
