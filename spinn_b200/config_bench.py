@@ -10,9 +10,11 @@
 * cfg2 -- ResNet-50, batch 1 and 64.
 * cfg4 -- the YOLOv10n-shaped network (``netdef.yolo_shaped``), 640x640, batch 1 and 32.
 * layer -- one fused convolution (Conv+BN+ReLU, optionally +residual or a projection shortcut)
-  of a chosen shape, the unit the single-kernel ncu summaries capture:
+  of a chosen shape, the unit the single-kernel ncu summaries capture; --tail times the
+  bottleneck-tail pair fused and as separate launches:
 
     python -m spinn_b200.config_bench --layer --batch 128 --c 256 --hw 14 --oc 1024 --k 1 --projection
+    python -m spinn_b200.config_bench --layer --tail --batch 4 --hw 199 --c 64 --oc 256 --tail-n2 64
 
 Every case is planned once (weights uploaded, graph captured), its input staged on the device,
 and the captured step list replayed: ``ms`` is the mean device time per run from CUDA events on
@@ -62,6 +64,8 @@ def layer(a) -> int:
     from spinn_b200 import lib, netdef
 
     pad = a.k // 2
+    if a.tail:
+        return tail(a)
     if a.projection:
         g, x = netdef.conv_bn_proj_add_relu(batch=a.batch, c=a.c, hw=a.hw, oc=a.oc, k=a.k)
     elif a.residual:
@@ -101,6 +105,39 @@ def layer(a) -> int:
     return 0
 
 
+def tail(a) -> int:
+    """Times the bottleneck-tail pair (1x1 c -> oc with a fused residual, then 1x1 oc -> tail_n2)
+    planned fused and planned as separate launches (NO_FUSE): the two convolutions' device
+    time each way, and the fused kernel's algorithmic GB/s (t2 + x read, y + t written, once)."""
+    import torch
+    from spinn_b200 import ennf, lib, netdef, runtime
+    g, x = netdef.bottleneck_tail(a.batch, a.hw, a.oc, a.c, a.tail_n2)
+    img = ennf.convert(g)
+    out = {"layer": {k: v for k, v in vars(a).items() if k != "only"}}
+    for name, flags in (("fused", 0), ("separate", lib.PLAN_NO_FUSE)):
+        model = runtime.Model(img, flags=flags | lib.PLAN_PROFILE)
+        model.run(x)
+        _time(model, a.iters, a.warmup)
+        stream = torch.cuda.Stream()
+        prof = None
+        for _ in range(max(3, a.warmup)):
+            model.run_profiled(stream.cuda_stream)
+            cur = model.profile()
+            prof = cur if prof is None else [(o, min(t, pt), f) for (o, t, f), (_, pt, _) in zip(cur, prof)]
+        kinds = model.step_kinds()
+        # the first convolution (x -> t2) is not part of the pair
+        conv = [t for (o, t, f), k in zip(prof, kinds) if k in (1, 9)]
+        out[name + "_ms"] = sum(conv[1:])
+        out[name + "_kinds"] = kinds
+        model.close()
+    rows = a.batch * a.hw * a.hw
+    byts = 4.0 * rows * (a.c + a.oc + a.oc + a.tail_n2)
+    out["algorithmic_mb"] = byts / 1e6
+    out["fused_gbs"] = byts / out["fused_ms"] / 1e6
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="cfg0,cfg1,cfg2,cfg4")
@@ -119,6 +156,9 @@ def main(argv=None):
                     help="bottleneck end with a projection shortcut: ReLU(BN(conv(x)) + BN(conv1x1(x))); "
                          "the second conv (c -> oc) carries the fused residual")
     ap.add_argument("--winograd", action="store_true", help="plan with Winograd F(4x4,3x3)")
+    ap.add_argument("--tail", action="store_true",
+                    help="the bottleneck-tail pair: 1x1 c -> oc with a residual, then 1x1 oc -> --tail-n2")
+    ap.add_argument("--tail-n2", type=int, default=64)
     a = ap.parse_args(argv)
     if a.layer:
         return layer(a)

@@ -318,6 +318,25 @@ def conv_bn_proj_add_relu(batch: int = 1, c: int = 256, hw: int = 14, oc: int = 
 RESNET_DEPTHS = {18: None, 50: [3, 4, 6, 3], 101: [3, 4, 23, 3], 152: [3, 8, 36, 3]}
 
 
+def bottleneck_tail(batch: int, hw: int, n1: int, k1: int, n2: int, relu_reduce: bool = True,
+                    seed: int = 11) -> Tuple[Graph, np.ndarray]:
+    """The end of one bottleneck block and the start of the next, on their own:
+    x [n1 channels] -> 1x1 (n1 -> k1)+BN+ReLU -> 1x1 (k1 -> n1)+BN, + x, ReLU -> 1x1 (n1 -> n2)
+    +BN (+ReLU) -> output.  The last two convolutions are the pair the bottleneck-tail kernel
+    fuses.  Input N(0, 1) from the same generator, after the weights."""
+    rng = np.random.default_rng(seed)
+    g = Graph("bottleneck_tail")
+    b = _Builder(g, rng)
+    x = g.add_input("input", (batch, n1, hw, hw))
+    t2 = b.unary("Relu", b.bn(b.conv(x, k1, 1, 1, 0)))
+    y = b.unary("Relu", b.add(b.bn(b.conv(t2, n1, 1, 1, 0)), x))
+    t = b.bn(b.conv(y, n2, 1, 1, 0))
+    if relu_reduce:
+        t = b.unary("Relu", t)
+    g.mark_output(t)
+    return g, rng.standard_normal((batch, n1, hw, hw)).astype(np.float32)
+
+
 def resnet(depth: int = 50, batch: int = 1, image: int = 224, num_classes: int = 1000,
            seed: int = 2, width: int = 64) -> Graph:
     """Bottleneck ResNet (v1.5: stride on the 3x3 conv), torchvision export order."""

@@ -17,19 +17,8 @@ pytestmark = pytest.mark.gpu
 
 
 def _tail_graph(batch, hw, n1, k1, n2, relu_reduce=True, seed=11):
-    """x [n1] -> 1x1 (n1->k1)+BN+ReLU -> 1x1 (k1->n1)+BN, + x, ReLU -> 1x1 (n1->n2)+BN(+ReLU) -> out."""
     from spinn_b200 import netdef
-    rng = np.random.default_rng(seed)
-    g = netdef.Graph("tail")
-    b = netdef._Builder(g, rng)
-    x = g.add_input("input", (batch, n1, hw, hw))
-    t2 = b.unary("Relu", b.bn(b.conv(x, k1, 1, 1, 0)))
-    y = b.unary("Relu", b.add(b.bn(b.conv(t2, n1, 1, 1, 0)), x))
-    t = b.bn(b.conv(y, n2, 1, 1, 0))
-    if relu_reduce:
-        t = b.unary("Relu", t)
-    g.mark_output(t)
-    return g, rng.standard_normal((batch, n1, hw, hw)).astype(np.float32)
+    return netdef.bottleneck_tail(batch, hw, n1, k1, n2, relu_reduce, seed)
 
 
 def _run(img, x, flags):
