@@ -65,15 +65,14 @@ def test_tail_fused_matches_unfused_and_reference(cuda_lib, ref_oracle, tmp_path
 
 
 def test_tail_fused_resnet50_stage1(cuda_lib, ref_oracle, tmp_path):
-    """ResNet-50 at batch 64: the 56x56 stage (200,704 rows) fuses its three block ends on single
-    CTAs (the first one is the stride-1 projection that carries the residual), the 28x28 stage
-    (50,176 rows) its three later block ends on CTA pairs; the 14x14 stage has too few rows."""
+    """ResNet-50 at batch 64: the 56x56 stage has 200,704 rows, so its three block ends fuse
+    (the first one is the stride-1 projection that carries the residual)."""
     from spinn_b200 import ennf, lib, netdef
     g = netdef.resnet(50, batch=64, seed=2)
     x = netdef.resnet_input(64, seed=2)
     img = ennf.convert(g)
     fused, kinds = _run(img, x, 0)
-    assert kinds.count(9) == 6, kinds
+    assert kinds.count(9) == 3, kinds
     plain, _ = _run(img, x, lib.PLAN_NO_FUSE)
     fused, plain = fused.reshape(64, -1), plain.reshape(64, -1)
     assert rel_l2(fused, plain) <= 1e-6, rel_l2(fused, plain)
