@@ -125,7 +125,6 @@ struct TailArgs {
   float* t = nullptr;
   int M = 0, k1 = 0, n1 = 0, n2 = 0, kpad3 = 0, kpad1 = 0;
   int act_e = 5, act_r = 1, round_out = 1;
-  int pair = 1;        // 2: 256-row units on 2-SM CTA pairs (cta_group::2), half the W bytes per SM
   int* err = nullptr;  // device error word; nullptr = the per-device flag
 };
 bool tail_fused_supported(const TailArgs& a, std::string* why);

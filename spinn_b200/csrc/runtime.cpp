@@ -607,10 +607,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         bool tail = false;
         if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && !wino && !s2d && G == 1 && KH == 1 && KW == 1 && SH == 1 &&
             SW == 1 && PH == 0 && PW == 0 && OH == H && OW == Wd && has_res && n_real == 3 && C % 32 == 0 &&
-            OC % 128 == 0 && nb && nb->op == OP_CONV && nb->in.size() == 3 && nb->out.size() == 1 &&
-            nb->in[0] == nd.out[0] &&
-            (C <= 64 ? (long)N * H * Wd >= 8L * 128 * sm_count(m->device)
-                     : (long)N * H * Wd >= 2L * 256 * (sm_count(m->device) / 2))) {
+            C <= 64 && OC % 128 == 0 && nb && nb->op == OP_CONV && nb->in.size() == 3 && nb->out.size() == 1 &&
+            nb->in[0] == nd.out[0] && (long)N * H * Wd >= 8L * 128 * sm_count(m->device)) {
           ConvParams c2{};
           if (nb->params.size() >= sizeof(ConvParams)) std::memcpy(&c2, nb->params.data(), sizeof(c2));
           W2 = &m->tensors[nb->in[1]];
@@ -646,7 +644,6 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           for (int o = 0; o < oc2; ++o) m->whost[b1 + o] = B2->host[o];
           const double fl = conv_flops(W, Y) + conv_flops(*W2, m->tensors[tb]);
           const int rnd = P.round_out, M = N * H * Wd, n1 = OC, k1 = C, n2 = oc2, ae = act, ar = act2;
-          const int pair = C <= 64 ? 1 : 2;
           const int s = add_step(ni, OP_CONV, 9, fl, [=](StepRec& r) {
             const Buf* xbp = &m->bufs[xb];
             const Buf* rbp = &m->bufs[rb];
@@ -672,7 +669,6 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
               a.act_e = ae;
               a.act_r = ar;
               a.round_out = rnd;
-              a.pair = pair;
               return tail_fused_launch(a, st);
             };
             return 0;

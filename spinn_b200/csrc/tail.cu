@@ -31,14 +31,6 @@
 //   warps 4..11 epilogue, two groups of four (one warp per TMEM lane quarter); group g takes
 //               the 32-column blocks c with c % 2 == g of every chunk, then the same blocks of t
 //
-// PAIR = 2 runs the same schedule on a cluster of two CTAs with one cta_group::2 MMA stream
-// issued by the leader: a work unit is 256 rows, each CTA holds its own 128 rows of t2, x and
-// the y chunk, and loads half of every W3 / W1 box (the MMA reads the other half from the peer),
-// so each SM streams half the weight bytes of a single-CTA tile.  Barrier roles as in
-// tc_gemm.cu's pairs: the leader's `full` counts both CTAs' bytes, the leader's MMA thread
-// commits `empty`, the accumulator barriers and `yempty` to both CTAs, and both CTAs' epilogue
-// warps arrive on the leader's `temptyE`, `temptyR` and `yfull`.
-//
 // Every mbarrier wait is bounded (4 s); on expiry the CTA drains what it issued, frees TMEM
 // and returns with the device error flag set.
 #include <algorithm>
@@ -54,19 +46,12 @@ constexpr int kBM = 128;
 constexpr uint64_t kTimeoutNs = 4000000000ull;
 constexpr uint64_t kDrainNs = 200000000ull;
 constexpr uint32_t kSub = kBM * 32 * 4;    // one 128-row x 32-column fp32 block: 16 KiB
+constexpr uint32_t kStage = 2 * kSub;      // 32 KiB
+constexpr int kStages = 3;
 constexpr uint32_t kYbuf = 4 * kSub;       // one 128-channel chunk of y: 64 KiB
 constexpr int kResSlots = 4;               // two per epilogue group
 constexpr int kThreads = 384;
-// Ring: an E stage is a 128x32 box of t2 (16 KiB) and 128/PAIR rows of a W3 box; an R stage
-// n2/PAIR rows of a W1 box.  Pairs halve the W boxes, so four 24 KiB stages fit where a single
-// CTA has three of 32 KiB.
-template <int PAIR>
-struct TailCfg {
-  static constexpr uint32_t STAGE = kSub + kSub / PAIR;
-  static constexpr int STAGES = PAIR == 2 ? 4 : 3;
-  static constexpr uint32_t SMEM = STAGES * STAGE + kYbuf + kResSlots * kSub + 1024 + 1024;
-  static_assert(SMEM <= 232448, "shared memory");
-};
+constexpr uint32_t kSmem = kStages * kStage + kYbuf + kResSlots * kSub + 1024 + 1024;
 
 struct TailParams {
   int M;          // rows (pixels)
@@ -95,18 +80,14 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr, uint32_t sub, int
   return make_smem_desc(addr + (uint32_t)((8 * k) / 32) * sub + (uint32_t)((8 * k) % 32) * 4, 16, 8 * 32 * 4, kSw128);
 }
 
-template <int PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     tail_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW3,
                 const __grid_constant__ CUtensorMap mapW1, const __grid_constant__ CUtensorMap mapR,
                 const __grid_constant__ CUtensorMap mapY, const __grid_constant__ CUtensorMap mapT,
                 const TailParams p) {
-  using Cf = TailCfg<PAIR>;
-  constexpr int kStages = Cf::STAGES;
-  constexpr uint32_t kStage = Cf::STAGE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sRing = smem;                   // [kStages][kStage]
+  uint8_t* sRing = smem;                   // [kStages][32 KiB]
   uint8_t* sY = sRing + kStages * kStage;  // [4][16 KiB]: chunk j of y, K-major, swizzled
   uint8_t* sRes = sY + kYbuf;              // [kResSlots][16 KiB]
   uint64_t* full = reinterpret_cast<uint64_t*>(sRes + kResSlots * kSub);
@@ -124,32 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int TM = kBM * PAIR;  // rows of a work unit
-  const int tiles = (p.M + TM - 1) / TM;
-  const uint32_t rank = PAIR == 2 ? cluster_ctarank() : 0;
-  const int unit0 = blockIdx.x / PAIR, unit_step = gridDim.x / PAIR;
-  // rows this CTA loads: its own 128 of the unit (a pair's second half past the end loads the
-  // first half again; those rows are never stored)
-  auto load_row = [&](int t) {
-    const int r0 = t * TM + (int)rank * kBM;
-    return r0 < p.M ? r0 : t * TM;
-  };
-  // barrier of the pair leader that a CTA's copies complete on / its epilogue arrives on
-  auto leader = [&](uint64_t* bar) { return PAIR == 2 ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar); };
-  auto arrive_leader = [&](uint64_t* bar) {
-    if constexpr (PAIR == 2)
-      mbar_arrive_cluster(leader(bar));
-    else
-      mbar_arrive(bar);
-  };
-  auto commit_all = [&](uint64_t* bar) {  // tcgen05.commit to this barrier in every CTA of the unit
-    if constexpr (PAIR == 2) {
-      umma_commit_pair(mapa_shared(smem_u32(bar), 0));
-      umma_commit_pair(mapa_shared(smem_u32(bar), 1));
-    } else {
-      umma_commit(bar);
-    }
-  };
+  const int tiles = (p.M + kBM - 1) / kBM;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -158,11 +114,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfullE[b], 1);
-      mbar_init(&temptyE[b], 8 * PAIR);
+      mbar_init(&temptyE[b], 8);
     }
     mbar_init(tfullR, 1);
-    mbar_init(temptyR, 8 * PAIR);
-    mbar_init(yfull, 8 * PAIR);
+    mbar_init(temptyR, 8);
+    mbar_init(yfull, 8);
     mbar_init(yempty, 1);
     for (int r = 0; r < kResSlots; ++r) {
       mbar_init(&rfull[r], 1);
@@ -181,17 +137,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&mapT);
   }
   if (warp == 2) {
-    if constexpr (PAIR == 2) {
-      tmem_alloc_pair(tmem_slot, 512);
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(tmem_slot, 512);
-      tmem_relinquish();
-    }
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR == 2) cluster_sync();  // the peer's barriers are initialised before use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   griddep_wait();
@@ -209,19 +159,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         return nullptr;
       }
       if (lane == 0) {
-        if (rank == 0) {  // the leader's barrier counts the bytes of every CTA of the unit
-          mbar_arrive_expect_tx(&full[s], bytes * PAIR);
-          armed |= 1u << s;
-          armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
-        }
+        mbar_arrive_expect_tx(&full[s], bytes);
+        armed |= 1u << s;
+        armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
       }
       return sRing + s * kStage;
-    };
-    auto load2 = [&](const CUtensorMap* m, void* dst, int c0, int c1) {
-      if constexpr (PAIR == 2)
-        tma_load_2d_pair(m, leader(&full[s]), dst, c0, c1);
-      else
-        tma_load_2d(m, &full[s], dst, c0, c1);
     };
     auto advance = [&]() {
       __syncwarp();
@@ -232,25 +174,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     auto load_e = [&](int m0, int j) {
       for (int kb = 0; ok && kb < p.k1_blocks; ++kb) {
-        uint8_t* st = next_stage(kSub + kSub / PAIR);
+        uint8_t* st = next_stage(kStage);
         if (!ok) return;
         if (lane == 0) {
-          load2(&mapA, st, kb * 32, m0);
-          load2(&mapW3, st + kSub, kb * 32, j * 128 + (int)rank * (128 / PAIR));
+          tma_load_2d(&mapA, &full[s], st, kb * 32, m0);
+          tma_load_2d(&mapW3, &full[s], st + kSub, kb * 32, j * 128);
         }
         advance();
       }
     };
     auto load_r = [&](int j) {
       for (int kb = 0; ok && kb < 4; ++kb) {
-        uint8_t* st = next_stage((uint32_t)(p.n2 / PAIR) * 128);
+        uint8_t* st = next_stage((uint32_t)p.n2 * 128);
         if (!ok) return;
-        if (lane == 0) load2(&mapW1, st, j * 128 + kb * 32, (int)rank * (p.n2 / PAIR));
+        if (lane == 0) tma_load_2d(&mapW1, &full[s], st, j * 128 + kb * 32, 0);
         advance();
       }
     };
-    for (int t = unit0; ok && t < tiles && !warp_aborted(abort_flag); t += unit_step) {
-      const int m0 = load_row(t);
+    for (int t = blockIdx.x; ok && t < tiles && !warp_aborted(abort_flag); t += gridDim.x) {
+      const int m0 = t * kBM;
       load_e(m0, 0);
       for (int j = 1; ok && j < p.nch; ++j) {
         load_e(m0, j);
@@ -264,16 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (armed & (1u << st)) mbar_wait(&full[st], (armed_ph >> st) & 1, &dummy, kDrainNs);
     }
     __syncwarp();
-  } else if (warp == 1 && rank == 0) {
-    // ------------------------------------------------------------ MMA issuer (pair leader)
-    const uint32_t idescE = make_idesc_tf32(TM, 128);
-    const uint32_t idescR = make_idesc_tf32(TM, (uint32_t)p.n2);
-    auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-      if constexpr (PAIR == 2)
-        umma_tf32_pair(d, a, b, idesc, acc);
-      else
-        umma_tf32(d, a, b, idesc, acc);
-    };
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idescE = make_idesc_tf32(kBM, 128);
+    const uint32_t idescR = make_idesc_tf32(kBM, (uint32_t)p.n2);
     const uint32_t ring = smem_u32(sRing), ybase = smem_u32(sY);
     int s = 0;
     uint32_t ph = 0;
@@ -297,8 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t st = ring + s * kStage;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma(d, kmajor_desc(st, kSub, k), kmajor_desc(st + kSub, kSub, k), idescE, (kb | k) ? 1u : 0u);
-          commit_all(&empty[s]);
+            umma_tf32(d, kmajor_desc(st, kSub, k), kmajor_desc(st + kSub, kSub, k), idescE, (kb | k) ? 1u : 0u);
+          umma_commit(&empty[s]);
         }
         __syncwarp();
         issued = true;
@@ -307,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph ^= 1;
         }
       }
-      if (lane == 0) commit_all(&tfullE[b]);
+      if (lane == 0) umma_commit(&tfullE[b]);
       __syncwarp();
       ++ecnt;
     };
@@ -332,8 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t st = ring + s * kStage;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma(d, kmajor_desc(ybase, kSub, kb * 4 + k), kmajor_desc(st, kSub, k), idescR, (j | kb | k) ? 1u : 0u);
-          commit_all(&empty[s]);
+            umma_tf32(d, kmajor_desc(ybase, kSub, kb * 4 + k), kmajor_desc(st, kSub, k), idescR,
+                      (j | kb | k) ? 1u : 0u);
+          umma_commit(&empty[s]);
         }
         __syncwarp();
         if (++s == kStages) {
@@ -341,27 +278,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph ^= 1;
         }
       }
-      if (lane == 0) commit_all(yempty);
+      if (lane == 0) umma_commit(yempty);
       __syncwarp();
       ++rcnt;
     };
-    for (int t = unit0; ok && t < tiles && !warp_aborted(abort_flag); t += unit_step) {
+    for (int t = blockIdx.x; ok && t < tiles && !warp_aborted(abort_flag); t += gridDim.x) {
       issue_e();
       for (int j = 1; ok && j < p.nch; ++j) {
         issue_e();
         if (ok) issue_r(j - 1);
       }
       if (ok) issue_r(p.nch - 1);
-      if (ok && lane == 0) commit_all(tfullR);
+      if (ok && lane == 0) umma_commit(tfullR);
       __syncwarp();
       ++tcnt;
     }
     if (warp_aborted(abort_flag) && issued && lane == 0) {
       volatile int dummy = 0;
-      if constexpr (PAIR == 2)
-        umma_commit_pair(mapa_shared(smem_u32(drain), 0));
-      else
-        umma_commit(drain);
+      umma_commit(drain);
       mbar_wait(drain, 0, &dummy, kDrainNs);
     }
     __syncwarp();
@@ -371,8 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int count[2] = {0, 0};
       uint32_t armed = 0, armed_ph = 0;
       bool ok = true;
-      for (int t = unit0; ok && t < tiles && !*abort_flag; t += unit_step) {
-        const int m0 = load_row(t);
+      for (int t = blockIdx.x; ok && t < tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = t * kBM;
         for (int j = 0; ok && j < p.nch; ++j)
           for (int c = 0; c < 4; ++c) {
             const int g = c & 1;
@@ -400,8 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wq = warp & 3, eg = (warp - 4) >> 2;
     int ecnt = 0, rc = 0, tcnt = 0;
     bool ok = true;
-    for (int t = unit0; ok && t < tiles; t += unit_step) {
-      const int m0 = t * TM + (int)rank * kBM, row0 = m0 + wq * 32;
+    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int m0 = t * kBM, row0 = m0 + wq * 32;
       const bool rows_live = row0 < p.M;
       const int r = wq * 32 + lane;  // row inside the tile = TMEM lane
       // ---- chunks of y
@@ -480,8 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          arrive_leader(&temptyE[b]);
-          arrive_leader(yfull);
+          mbar_arrive(&temptyE[b]);
+          mbar_arrive(yfull);
         }
         ++ecnt;
       }
@@ -529,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) arrive_leader(temptyR);
+      if (lane == 0) mbar_arrive(temptyR);
       ++tcnt;
     }
     if (lane == 0) tma_store_wait0();
@@ -537,77 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
-  // In a pair, neither CTA leaves while the other may still touch its shared memory or TMEM.
-  if constexpr (PAIR == 2) cluster_sync();
   if (warp == 2) {
     tc_fence_after();
-    if constexpr (PAIR == 2)
-      tmem_dealloc_pair(tmem_base, 512);
-    else
-      tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, 512);
   }
   if (threadIdx.x == 0 && *abort_flag && p.err) atomicExch(p.err, 1);
-}
-
-template <int PAIR>
-int launch_tail(const CUtensorMap* maps, const TailParams& p, int dev, cudaStream_t stream) {
-  using Cf = TailCfg<PAIR>;
-  auto kern = tail_kernel<PAIR>;
-  static std::atomic<uint64_t> configured{0};
-  const uint64_t bit = 1ull << (dev & 63);
-  if (!(configured.load() & bit)) {
-    SPINN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
-    configured.fetch_or(bit);
-  }
-  const int units = (p.M + kBM * PAIR - 1) / (kBM * PAIR);
-  int slots = sm_count(dev) / PAIR;
-  if constexpr (PAIR == 2) {
-    static std::atomic<int> clusters[64];
-    int nc = clusters[dev & 63].load();
-    if (nc <= 0) {
-      cudaLaunchConfig_t q = {};
-      q.gridDim = dim3(2 * (sm_count(dev) / 2), 1, 1);
-      q.blockDim = dim3(kThreads, 1, 1);
-      q.dynamicSmemBytes = Cf::SMEM;
-      cudaLaunchAttribute ca;
-      ca.id = cudaLaunchAttributeClusterDimension;
-      ca.val.clusterDim.x = 2;
-      ca.val.clusterDim.y = 1;
-      ca.val.clusterDim.z = 1;
-      q.attrs = &ca;
-      q.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&nc, kern, &q) != cudaSuccess || nc <= 0) {
-        cudaGetLastError();
-        nc = sm_count(dev) / 2;
-      }
-      clusters[dev & 63].store(nc);
-    }
-    slots = nc;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(PAIR * std::min(units, slots)), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cf::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attrs[2];
-  int na = 0;
-  if (!getenv("SPINN_NO_PDL")) {
-    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  if constexpr (PAIR == 2) {
-    attrs[na].id = cudaLaunchAttributeClusterDimension;
-    attrs[na].val.clusterDim.x = 2;
-    attrs[na].val.clusterDim.y = 1;
-    attrs[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  cfg.attrs = attrs;
-  cfg.numAttrs = na;
-  SPINN_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p));
-  SPINN_CUDA_TRY(cudaGetLastError());
-  return 0;
 }
 
 }  // namespace
@@ -635,23 +503,28 @@ int tail_fused_launch(const TailArgs& a, cudaStream_t stream) {
     set_error("bottleneck tail: %s", why.c_str());
     return SPINN_CUDA_EINVAL;
   }
-  const int pair = a.pair == 2 ? 2 : 1;
   int dev = 0;
   SPINN_CUDA_TRY(cudaGetDevice(&dev));
-  CUtensorMap maps[6];  // t2, W3, W1, x, y, t
-  int rc = encode_tiled_2d(&maps[0], a.t2, (uint64_t)a.k1, (uint64_t)a.M, (uint64_t)a.k1 * 4, 32, kBM,
+  CUtensorMap mA, mW3, mW1, mR, mY, mT;
+  int rc = encode_tiled_2d(&mA, a.t2, (uint64_t)a.k1, (uint64_t)a.M, (uint64_t)a.k1 * 4, 32, kBM,
                            CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_tiled_2d(&maps[1], a.w3, (uint64_t)a.kpad3, (uint64_t)a.n1, (uint64_t)a.kpad3 * 4, 32,
-                                (uint32_t)(128 / pair), CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_tiled_2d(&maps[2], a.w1, (uint64_t)a.kpad1, (uint64_t)a.n2, (uint64_t)a.kpad1 * 4, 32,
-                                (uint32_t)(a.n2 / pair), CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_tiled_2d(&maps[3], a.x, (uint64_t)a.n1, (uint64_t)a.M, (uint64_t)a.n1 * 4, 32, kBM,
+  if (!rc) rc = encode_tiled_2d(&mW3, a.w3, (uint64_t)a.kpad3, (uint64_t)a.n1, (uint64_t)a.kpad3 * 4, 32, 128,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_tiled_2d(&maps[4], a.y, (uint64_t)a.n1, (uint64_t)a.M, (uint64_t)a.n1 * 4, 32, 32,
+  if (!rc) rc = encode_tiled_2d(&mW1, a.w1, (uint64_t)a.kpad1, (uint64_t)a.n2, (uint64_t)a.kpad1 * 4, 32,
+                                (uint32_t)a.n2, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_tiled_2d(&mR, a.x, (uint64_t)a.n1, (uint64_t)a.M, (uint64_t)a.n1 * 4, 32, kBM,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_tiled_2d(&maps[5], a.t, (uint64_t)a.n2, (uint64_t)a.M, (uint64_t)a.n2 * 4, 32, 32,
+  if (!rc) rc = encode_tiled_2d(&mY, a.y, (uint64_t)a.n1, (uint64_t)a.M, (uint64_t)a.n1 * 4, 32, 32,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_tiled_2d(&mT, a.t, (uint64_t)a.n2, (uint64_t)a.M, (uint64_t)a.n2 * 4, 32, 32,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  static std::atomic<uint64_t> configured{0};
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    SPINN_CUDA_TRY(cudaFuncSetAttribute(tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+    configured.fetch_or(bit);
+  }
   TailParams p{};
   p.M = a.M;
   p.k1_blocks = a.k1 / 32;
@@ -663,7 +536,20 @@ int tail_fused_launch(const TailArgs& a, cudaStream_t stream) {
   p.b3 = a.b3;
   p.b1 = a.b1;
   p.err = a.err ? a.err : device_error_flag(dev);
-  return pair == 2 ? launch_tail<2>(maps, p, dev, stream) : launch_tail<1>(maps, p, dev, stream);
+  const int tiles = (a.M + kBM - 1) / kBM;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min(tiles, sm_count(dev)), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = getenv("SPINN_NO_PDL") ? 0 : 1;
+  SPINN_CUDA_TRY(cudaLaunchKernelEx(&cfg, tail_kernel, mA, mW3, mW1, mR, mY, mT, p));
+  SPINN_CUDA_TRY(cudaGetLastError());
+  return 0;
 }
 
 }  // namespace spinn

@@ -30,18 +30,13 @@ def _run(img, x, flags):
     return y, kinds
 
 
-# Expands of <= 64 input channels run on single CTAs and need eight waves of 128-row tiles on
-# 148 SMs (151,552 rows); wider ones run on CTA pairs and need two waves of 256-row units over
-# 74 pairs (37,888 rows).
+# rows = batch * hw^2 must reach eight waves of 128-row tiles on 148 SMs (151,552)
 TAIL_CASES = [
-    # batch, hw, n1, k1, n2, relu on the reduce
-    (4, 199, 256, 64, 64, True),     # single CTAs, 158,404 rows: a partial last tile (56x56-stage widths)
-    (4, 200, 512, 64, 128, True),    # single CTAs, 160,000 rows
-    (3, 225, 1024, 64, 256, True),   # single CTAs, 151,875 rows, the widest reduce the kernel takes
-    (5, 175, 256, 32, 96, False),    # single CTAs, 153,125 rows, K1 = 32, no ReLU after the reduce
-    (1, 200, 512, 128, 128, True),   # pairs, 40,000 rows (28x28-stage widths)
-    (3, 115, 1024, 256, 256, True),  # pairs, 39,675 rows: the last unit's second CTA has 123 rows
-    (4, 98, 512, 128, 64, False),    # pairs, 38,416 rows: the last unit's second CTA has none
+    # batch, hw, n1, k1, n2, relu on the reduce (the planner fuses expands of <= 64 input channels)
+    (4, 199, 256, 64, 64, True),     # 158,404 rows: a partial last tile; the ResNet 56x56-stage widths
+    (4, 200, 512, 64, 128, True),    # 160,000 rows
+    (3, 225, 1024, 64, 256, True),   # 151,875 rows, the widest reduce the kernel takes
+    (5, 175, 256, 32, 96, False),    # 153,125 rows, K1 = 32, no ReLU after the reduce
 ]
 
 
