@@ -594,12 +594,13 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         // chunks in shared memory for the reduce (tail.cu) -- when there are rows enough for
         // eight waves of 128-row tiles (with fewer, the separate launches spread their more
         // numerous, narrower tiles better: ResNet-101 at batch 32, 5.3 waves, was 0.6% slower
-        // fused, at 64 and 256 0.9% and 1.4% faster) and the expand's input is at most 64
-        // channels wide.  Measured at batch 256: the
-        // 64 -> 256 -> 64 ends of the 56x56 stage take 397-422 us fused against 457-498 us as two
-        // launches; 128 -> 512 -> 128 at 28x28 ties (252 vs 250); 256 -> 1024 -> 256 at 14x14
-        // loses (180 vs 149 us): every 128-row tile then streams ~3.5 MB through a 96 KiB ring
-        // and the ring's TMA latency, not HBM, sets the pace.
+        // fused, at 64 and 256 0.9% and 1.4% faster) and the expand's input is at most 128
+        // channels wide.  Measured at batch 256: the 64 -> 256 -> 64 ends of the 56x56 stage
+        // take 397-422 us fused against 457-498 us as two launches; 128 -> 512 -> 128 at 28x28
+        // ties per launch (252 vs 250 us) and saves 0.07 ms over the step; 256 -> 1024 -> 256 at
+        // 14x14 loses: 180 vs 149 us per pair of layers, 191 us on CTA pairs (half the weight
+        // bytes per SM), and 64-column chunks through two y buffers made the step 15% slower;
+        // its 128-row tiles stream ~3.5 MB each through shared memory, eight chunks in a row.
         const NodeRec* nb = ni + 1 < (int)m->nodes.size() ? &m->nodes[ni + 1] : nullptr;
         int oc2 = 0, act2 = 0;
         const TensorRec* W2 = nullptr;
@@ -607,7 +608,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         bool tail = false;
         if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && !wino && !s2d && G == 1 && KH == 1 && KW == 1 && SH == 1 &&
             SW == 1 && PH == 0 && PW == 0 && OH == H && OW == Wd && has_res && n_real == 3 && C % 32 == 0 &&
-            C <= 64 && OC % 128 == 0 && nb && nb->op == OP_CONV && nb->in.size() == 3 && nb->out.size() == 1 &&
+            C <= 128 && OC % 128 == 0 && nb && nb->op == OP_CONV && nb->in.size() == 3 && nb->out.size() == 1 &&
             nb->in[0] == nd.out[0] && (long)N * H * Wd >= 8L * 128 * sm_count(m->device)) {
           ConvParams c2{};
           if (nb->params.size() >= sizeof(ConvParams)) std::memcpy(&c2, nb->params.data(), sizeof(c2));

@@ -32,9 +32,9 @@ def _run(img, x, flags):
 
 # rows = batch * hw^2 must reach eight waves of 128-row tiles on 148 SMs (151,552)
 TAIL_CASES = [
-    # batch, hw, n1, k1, n2, relu on the reduce (the planner fuses expands of <= 64 input channels)
+    # batch, hw, n1, k1, n2, relu on the reduce (the planner fuses expands of <= 128 input channels)
     (4, 199, 256, 64, 64, True),     # 158,404 rows: a partial last tile; the ResNet 56x56-stage widths
-    (4, 200, 512, 64, 128, True),    # 160,000 rows
+    (4, 200, 512, 128, 128, True),   # 160,000 rows, the ResNet 28x28-stage widths
     (3, 225, 1024, 64, 256, True),   # 151,875 rows, the widest reduce the kernel takes
     (5, 175, 256, 32, 96, False),    # 153,125 rows, K1 = 32, no ReLU after the reduce
 ]
