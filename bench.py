@@ -208,24 +208,37 @@ def min_profile(prev, cur):
     return [(op, min(ms, pms), fl) for (op, ms, fl), (_, pms, _) in zip(cur, prev)]
 
 
+CONV_KINDS = (1, 9)  # step kinds of tensor-core convolutions: one layer (1) or a fused pair (9)
+
+
 def layer_roofline(img: bytes, prof, kinds, tf32_tflops: float, hbm_gbs: float):
-    """Per-layer roofline of the convolutions' profiled times.  Each layer's floor is
-    the larger of its algorithmic FLOPs at the tf32 peak and its algorithmic bytes (input,
-    weights, output and fused residual, each touched once) at the copy bandwidth; `frac` is
-    the sum of the floors over the measured convolution time."""
+    """Per-layer roofline of the convolutions' profiled times.  Each step's floor is the
+    larger of its algorithmic FLOPs at the tf32 peak and its algorithmic bytes at the copy
+    bandwidth: input, weights, output and fused residual, each touched once; a fused pair of
+    1x1 layers (step kind 9) reads its input and residual and writes both outputs once.
+    `frac` is the sum of the floors over the measured convolution time."""
     from spinn_b200 import ennf
     em = ennf.read(img)
     convs = [n for n in em.nodes if n.op_type == ennf.OP["Conv"]]
-    steps = [(ms, fl) for (op, ms, fl), k in zip(prof, kinds) if k == 1]
-    if len(convs) != len(steps):
+    steps = [(k, ms, fl) for (op, ms, fl), k in zip(prof, kinds) if k in CONV_KINDS]
+    if len(convs) != sum(2 if k == 9 else 1 for k, _, _ in steps):
         return None
+
+    def elems(t):
+        return float(np.prod(em.tensors[t].dims))
+
     floor = conv_ms = 0.0
     n_tensor = n_hbm = 0
-    for n, (ms, fl) in zip(convs, steps):
-        dims = [em.tensors[t].dims for t in (n.inputs[0], n.inputs[1], n.outputs[0])]
-        x, w, y = (float(np.prod(d)) for d in dims)
+    ci = 0
+    for k, ms, fl in steps:
+        n = convs[ci]
         res = ennf.ConvParams.unpack(n.params).fused_act in (4, 5)
-        byts = 4.0 * (x + w + y * (2 if res else 1))
+        byts = 4.0 * (elems(n.inputs[0]) + elems(n.inputs[1]) + elems(n.outputs[0]) * (2 if res else 1))
+        ci += 1
+        if k == 9:  # + the second layer's weights and output; its input is the first one's output
+            n2 = convs[ci]
+            byts += 4.0 * (elems(n2.inputs[1]) + elems(n2.outputs[0]))
+            ci += 1
         t_c = fl / (tf32_tflops * 1e12) * 1e3
         t_m = byts / (hbm_gbs * 1e9) * 1e3
         floor += max(t_c, t_m)
@@ -235,7 +248,7 @@ def layer_roofline(img: bytes, prof, kinds, tf32_tflops: float, hbm_gbs: float):
         else:
             n_hbm += 1
     return {"floor_ms": floor, "conv_ms": conv_ms, "frac": floor / conv_ms if conv_ms > 0 else None,
-            "tensor_bound_layers": n_tensor, "hbm_bound_layers": n_hbm,
+            "tensor_bound_steps": n_tensor, "hbm_bound_steps": n_hbm,
             "peaks": {"tf32_tflops": tf32_tflops, "hbm_gbs": hbm_gbs}}
 
 
@@ -407,14 +420,14 @@ def main():
         model.run_profiled(sid)
         cur = model.profile()
         prof = min_profile(prof, cur)
-    conv_ms = sum(ms for (op, ms, fl), k in zip(prof, kinds) if k == 1)
-    conv_fl = sum(fl for (op, ms, fl), k in zip(prof, kinds) if k == 1)
-    conv_launches = sum(1 for k in kinds if k == 1)
+    conv_ms = sum(ms for (op, ms, fl), k in zip(prof, kinds) if k in CONV_KINDS)
+    conv_fl = sum(fl for (op, ms, fl), k in zip(prof, kinds) if k in CONV_KINDS)
+    conv_launches = sum(1 for k in kinds if k in CONV_KINDS)
     by_kind = {}
     for (op, ms, fl), k in zip(prof, kinds):
         by_kind[k] = by_kind.get(k, 0.0) + ms
     kind_names = {0: "alias", 1: "tc_conv", 2: "tc_gemm", 3: "depthwise", 4: "direct", 5: "pool", 6: "eltwise",
-                  7: "layout", 8: "winograd"}
+                  7: "layout", 8: "winograd", 9: "tc_conv_pair"}
     breakdown = {kind_names.get(k, str(k)): round(v, 4) for k, v in sorted(by_kind.items())}
 
     # end to end through the C ABI with pinned host buffers: synchronous spinn_cuda_run, then
@@ -486,7 +499,8 @@ def main():
                          "traffic": None,
                          "traffic_source": "per-launch DRAM bytes come from single-kernel ncu captures of "
                                            "small cases, listed with the kernel summaries",
-                         "kernel": "tc_gemm_kernel (implicit-GEMM conv, tcgen05 kind::tf32)",
+                         "kernel": "tcgen05 kind::tf32 convolutions: tc_gemm_kernel (implicit GEMM) and "
+                                   "tail_kernel (fused 1x1 pairs)",
                          "peak_source": f"dense tf32 tensor rate: {tf32_peak_how}",
                          "peak_measured_burst": burst_tf32,
                          "frac_of_measured_burst": achieved / burst_tf32 if burst_tf32 else None,

@@ -32,8 +32,28 @@ def test_layer_roofline_floors():
               max(fl / 100e12, 4.0 * (x + w + 2 * y) / 1e12) * 1e3]
     assert np.isclose(r["floor_ms"], sum(floors))
     assert np.isclose(r["conv_ms"], 0.030)
-    assert r["hbm_bound_layers"] == 2 and r["tensor_bound_layers"] == 0
+    assert r["hbm_bound_steps"] == 2 and r["tensor_bound_steps"] == 0
     assert bench.layer_roofline(img, prof[:1], [1], 100.0, 1000.0) is None  # step/node mismatch
+
+
+def test_layer_roofline_counts_a_fused_pair_once():
+    """A fused pair of 1x1 layers (step kind 9) reads its input and residual and writes both
+    outputs once: the first layer's output is not read back."""
+    from spinn_b200 import ennf, netdef
+    bench = _bench()
+    g = netdef.bottleneck_tail(1, 8, 64, 32, 32)[0]   # conv a (x -> t2), then the fusable pair
+    img = ennf.convert(g)
+    m = ennf.read(img)
+    convs = [n for n in m.nodes if n.op_type == ennf.OP["Conv"]]
+    assert len(convs) == 3
+    fl = [2.0 * 64 * 32 * 64, 2.0 * 64 * 64 * 32, 2.0 * 64 * 32 * 64]  # rows 64: a, b (expand), c (reduce)
+    prof = [(60, 0.01, fl[0]), (60, 0.02, fl[1] + fl[2])]
+    r = bench.layer_roofline(img, prof, [1, 9], tf32_tflops=1e6, hbm_gbs=1000.0)
+    rows = 64
+    pair_bytes = 4.0 * (rows * 32 + 64 * 32 + rows * 64 * 2 + 32 * 64 + rows * 32)
+    first_bytes = 4.0 * (rows * 64 + 32 * 64 + rows * 32)
+    assert np.isclose(r["floor_ms"], (first_bytes + pair_bytes) / 1e12 * 1e3)
+    assert r["hbm_bound_steps"] == 2
 
 
 def test_min_profile_keeps_each_steps_minimum():
