@@ -150,18 +150,19 @@ SpinnCudaModel *spinn_cuda_load_buffer(const void *data, size_t size);
  *        bit 2 = keep activations fp32 on store (no tf32 rounding of conv outputs);
  *        bit 3 = Winograd F(4x4,3x3) for 3x3 stride-1 group-1 convolutions;
  *        bit 4 = keep every intermediate tensor after a run (each gets its own arena range);
- *        bit 5 = no cross-layer fusion.  By default a 1x1 convolution with a fused residual
+ *        bit 5 = no cross-layer fusion.  By default (a) a 1x1 convolution with a fused residual
  *        followed by a 1x1 convolution of its output (a bottleneck block's end and the next
- *        block's start) runs as one kernel when the tensors have rows enough for two waves of
- *        tiles: its output is written once and fed to the second convolution from on-chip
- *        memory. */
+ *        block's start) runs as one kernel when the tensors are large enough: its output is
+ *        written once and fed to the second convolution from on-chip memory; (b) a channel
+ *        Concat whose only reader is a tensor-core convolution is not materialised: the
+ *        convolution fetches each channel block from the Concat's inputs. */
 #define SPINN_CUDA_PLAN_NO_GRAPH 1
 #define SPINN_CUDA_PLAN_PROFILE 2
 #define SPINN_CUDA_PLAN_NO_ROUND 4
 #define SPINN_CUDA_PLAN_WINOGRAD 8 /* run 3x3 stride-1 convolutions with Winograd F(4x4,3x3) */
 #define SPINN_CUDA_PLAN_KEEP 16    /* keep every intermediate tensor (no arena reuse) for
                                       spinn_cuda_copy_tensor; same kernels and tile plans */
-#define SPINN_CUDA_PLAN_NO_FUSE 32 /* run every convolution as its own launch (see below) */
+#define SPINN_CUDA_PLAN_NO_FUSE 32 /* no cross-layer fusion (see below) */
 int spinn_cuda_plan(SpinnCudaModel *m, int device, uint64_t max_arena_bytes, int flags);
 
 /* Stage 3: run one inference.  Copies input 0 (NCHW fp32, host memory) to the device, runs

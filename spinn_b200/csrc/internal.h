@@ -99,6 +99,13 @@ struct TcGemmArgs {
   // that applies the epilogue; results stay deterministic.
   float* ws = nullptr;
   size_t ws_bytes = 0;
+  // A as the channel concatenation of up to four NHWC tensors (nparts > 1; x unused): part i
+  // holds channels [part_c0[i], part_c0[i] + part_cpad[i]) of cpad (im2col) or of K (tiled),
+  // each a whole number of channel blocks, stored with its own channel stride part_cpad[i].
+  int nparts = 1;
+  const float* xpart[4] = {nullptr, nullptr, nullptr, nullptr};
+  int part_c0[4] = {0, 0, 0, 0};
+  int part_cpad[4] = {0, 0, 0, 0};
 };
 // Workspace a launch of `a` would use (0 when it would not split), for planners.
 size_t tc_gemm_workspace_bytes(const TcGemmArgs& a);

@@ -140,6 +140,7 @@ struct SpinnCudaModel {
   float* wdev = nullptr;
   uint64_t wbytes = 0;
   int tc_layers = 0;               // tensor-core conv steps planned so far (tile walk direction)
+  std::map<int, std::vector<int>> virt_cat;  // Concat outputs read in parts: tensor -> part buffers
   float* splitk_ws = nullptr;      // split-K partial sums, shared by all steps (one stream)
   size_t splitk_bytes = 0;
   std::vector<float> whost;        // pre-transformed weights before upload
@@ -393,6 +394,49 @@ double conv_flops(const TensorRec& w, const TensorRec& y) {
 
 }  // namespace
 
+// Whether node `ci` is a convolution that reads tensor `whole` (a channel Concat of `parts`) as
+// its input through the tcgen05 path and can fetch it part by part: group 1, not Winograd, not
+// the bottleneck-tail pattern's expand, every part a whole number of the tensor-core channel
+// blocks (32 channels in tiled mode, the im2col block of the concatenated channels otherwise).
+static bool concat_feeds_tc_conv(SpinnCudaModel* m, int ci, int whole, const std::vector<uint16_t>& parts) {
+  const NodeRec& nd = m->nodes[ci];
+  if (nd.op != OP_CONV || nd.in.size() < 2 || nd.in[0] != whole) return false;
+  for (size_t i = 1; i < nd.in.size(); ++i)
+    if (nd.in[i] == whole) return false;
+  ConvParams cp{};
+  if (nd.params.size() >= sizeof(ConvParams)) std::memcpy(&cp, nd.params.data(), sizeof(cp));
+  const TensorRec& W = m->tensors[nd.in[1]];
+  const TensorRec& X = m->tensors[whole];
+  const TensorRec& Y = m->tensors[nd.out[0]];
+  if (W.ndim != 4 || !W.host || X.ndim != 4 || Y.ndim != 4) return false;
+  const int G = cp.group > 0 ? cp.group : 1;
+  const int KH = cp.kernel_shape[0] ? cp.kernel_shape[0] : (int)W.dims[2];
+  const int KW = cp.kernel_shape[1] ? cp.kernel_shape[1] : (int)W.dims[3];
+  const int SH = cp.strides[0] ? cp.strides[0] : 1, SW = cp.strides[1] ? cp.strides[1] : 1;
+  const int DH = cp.dilations[0] ? cp.dilations[0] : 1, DW = cp.dilations[1] ? cp.dilations[1] : 1;
+  if (G != 1 || cp.auto_pad != 0) return false;
+  if ((m->flags & SPINN_CUDA_PLAN_WINOGRAD) && KH == 3 && KW == 3 && SH == 1 && SW == 1 && DH == 1 && DW == 1)
+    return false;
+  const int act = cp.fused_act;
+  if ((act == 4 || act == 5) && KH == 1 && KW == 1) return false;  // may become a bottleneck-tail expand
+  const int C = (int)X.dims[1];
+  if (C % 4) return false;
+  const bool tiled = KH == 1 && KW == 1 && SH == 1 && SW == 1 && cp.pads[0] == 0 && cp.pads[1] == 0 &&
+                     Y.dims[2] == X.dims[2] && Y.dims[3] == X.dims[3];
+  int cb = 32;
+  if (!tiled)
+    for (int c : {32, 16, 8, 4})
+      if (C % c == 0) {
+        cb = c;
+        break;
+      }
+  for (auto id : parts) {
+    const TensorRec& t = m->tensors[id];
+    if (t.ndim != 4 || (int)t.dims[1] % cb) return false;
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ plan
 static int compile_model(SpinnCudaModel* m, uint64_t budget) {
   Planner P(m);
@@ -402,6 +446,17 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
   int step = 0;
   // pass-1 records: lambdas that build the closure once pointers are known
   std::vector<std::function<int(StepRec&)>> builders;
+  // readers of each tensor (graph outputs count as one more); a channel Concat whose only
+  // reader is a tensor-core convolution is not materialised: the convolution reads its parts
+  std::vector<int> readers(nt, 0);
+  std::vector<int> reader_node(nt, -1);
+  for (int ni = 0; ni < (int)m->nodes.size(); ++ni)
+    for (auto id : m->nodes[ni].in) {
+      ++readers[id];
+      reader_node[id] = ni;
+    }
+  for (auto id : m->outputs) ++readers[id];
+  std::map<int, std::vector<int>> virt_cat;  // concat tensor -> NHWC buffers of its parts
 
   auto add_step = [&](int node, uint16_t op, int kind, double flops, std::function<int(StepRec&)> b) {
     StepRec s;
@@ -606,7 +661,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         const TensorRec* W2 = nullptr;
         const TensorRec* B2 = nullptr;
         bool tail = false;
-        if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && !wino && !s2d && G == 1 && KH == 1 && KW == 1 && SH == 1 &&
+        if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && !virt_cat.count(nd.in[0]) && !wino && !s2d && G == 1 &&
+            KH == 1 && KW == 1 && SH == 1 &&
             SW == 1 && PH == 0 && PW == 0 && OH == H && OW == Wd && has_res && n_real == 3 && C % 32 == 0 &&
             C <= 128 && OC % 128 == 0 && nb && nb->op == OP_CONV && nb->in.size() == 3 && nb->out.size() == 1 &&
             nb->in[0] == nd.out[0] && (long)N * H * Wd >= 8L * 128 * sm_count(m->device)) {
@@ -754,6 +810,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             boff = P.wreserve(ocpad);
             for (int o = 0; o < OC; ++o) m->whost[boff + o] = B->host[o];
           }
+          const std::vector<int> vparts = virt_cat.count(nd.in[0]) ? virt_cat[nd.in[0]] : std::vector<int>{};
           const int s = add_step(ni, OP_CONV, 1, fl, [=](StepRec& r) {
             TcGemmArgs a;
             a.a_mode = 0;
@@ -789,10 +846,24 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             const Buf* xbp = &m->bufs[xb];
             const Buf* ybp = &m->bufs[yb];
             const Buf* rbp = rb >= 0 ? &m->bufs[rb] : nullptr;
+            std::vector<const Buf*> xparts;  // a Concat read in parts
+            if (vparts.size() > 1) {
+              a.nparts = (int)vparts.size();
+              int c0 = 0;
+              for (int i = 0; i < a.nparts; ++i) {
+                const Buf* pbuf = &m->bufs[vparts[i]];
+                xparts.push_back(pbuf);
+                a.xpart[i] = pbuf->ptr;
+                a.part_c0[i] = c0;
+                a.part_cpad[i] = pbuf->cpad;
+                c0 += pbuf->cpad;
+              }
+            }
             note_ws(m, a);
-            r.run = [m, a, xbp, ybp, rbp, woff, boff](cudaStream_t st) mutable {
+            r.run = [m, a, xbp, ybp, rbp, woff, boff, xparts](cudaStream_t st) mutable {
               a.ws = m->splitk_ws;
               a.ws_bytes = m->splitk_bytes;
+              for (size_t i = 0; i < xparts.size(); ++i) a.xpart[i] = xparts[i]->ptr;
               a.x = xbp->ptr;
               a.y = ybp->ptr;
               a.res = rbp ? rbp->ptr : nullptr;
@@ -803,6 +874,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             return 0;
           });
           P.touch(xb, s);
+          for (int b : vparts) P.touch(b, s);
           P.touch(yb, s);
           if (rb >= 0) P.touch(rb, s);
         } else if (G == C && G == OC) {
@@ -1196,6 +1268,22 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             return SPINN_CUDA_EUNSUPPORTED;
           }
         const bool nhwc = TW.ndim == 4 && axis == 1;
+        if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && is_cat && nhwc && parts.size() >= 2 && parts.size() <= 4 &&
+            readers[whole] == 1 &&
+            reader_node[whole] > ni && concat_feeds_tc_conv(m, reader_node[whole], whole, parts)) {
+          // the convolution reading this Concat fetches each channel block from its part
+          std::vector<int> pbv;
+          for (auto id : parts) pbv.push_back(ensure_nhwc(id, ni));
+          bool all = true;
+          for (int b : pbv) all &= b >= 0;
+          if (all) {
+            virt_cat[whole] = pbv;
+            set_nhwc(m->bufs[whole], TW);
+            m->bufs[whole].bytes = 0;  // no storage of its own
+            produced[whole] = 1;
+            break;
+          }
+        }
         std::vector<int> pb;  // buffers of the parts
         int wb;
         if (nhwc) {
@@ -1587,6 +1675,7 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     P.touch(src, s);
   }
 
+  m->virt_cat = virt_cat;
   // arena
   const int nsteps = (int)m->steps.size();
   int rc = plan_arena(m, nsteps, budget);
@@ -1982,6 +2071,28 @@ __attribute__((visibility("default"))) int spinn_cuda_copy_tensor(SpinnCudaModel
   while (m->bufs[r].alias >= 0) r = m->bufs[r].alias;
   const Buf& b = m->bufs[tensor_id];
   const float* base = m->bufs[r].ptr;
+  auto vc = m->virt_cat.find(tensor_id);
+  if (vc != m->virt_cat.end() && t.ndim == 4 && first >= 0 && count >= 1 &&
+      (uint64_t)first + count <= t.dims[0] && bytes == (uint64_t)count * (t.elems / t.dims[0]) * 4) {
+    // a Concat read in parts by its convolution: gather the parts (NCHW, channel after channel)
+    SPINN_CUDA_TRY(cudaSetDevice(m->device));
+    SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    const uint64_t hw = (uint64_t)t.dims[2] * t.dims[3];
+    float* dst = static_cast<float*>(host);
+    int c0 = 0;
+    for (int pbi : vc->second) {
+      const Buf& pb = m->bufs[pbi];
+      const uint64_t img = hw * pb.cpad;
+      std::vector<float> tmp((size_t)(count * img));
+      SPINN_CUDA_TRY(cudaMemcpy(tmp.data(), pb.ptr + (uint64_t)first * img, tmp.size() * 4, cudaMemcpyDeviceToHost));
+      for (int n = 0; n < count; ++n)
+        for (int c = 0; c < pb.c; ++c)
+          for (uint64_t q = 0; q < hw; ++q)
+            dst[((uint64_t)n * t.dims[1] + c0 + c) * hw + q] = tmp[n * img + q * pb.cpad + c];
+      c0 += pb.c;
+    }
+    return 0;
+  }
   if (t.is_weight || !base || b.lay == LAY_NONE || t.ndim < 1 || t.dims[0] == 0) {
     set_error("spinn_cuda_copy_tensor: tensor %d has no device buffer (weight, fused away or unused)", tensor_id);
     return SPINN_CUDA_EINVAL;

@@ -51,6 +51,14 @@ constexpr int kSmemBudget = 232448 - 2048;      // 227 KiB opt-in minus barriers
 
 enum AMode { kIm2col = 0, kTiled = 1 };
 
+// The A operand's tensor maps: one per part when A is the channel concatenation of up to four
+// NHWC tensors (a Concat that only this convolution reads is never materialised; each channel
+// block of K is fetched from the part holding it).
+constexpr int kMaxAParts = 4;
+struct AMaps {
+  CUtensorMap m[kMaxAParts];
+};
+
 struct TcParams {
   int M, N;
   int num_kb;
@@ -65,7 +73,19 @@ struct TcParams {
   float alpha;
   const float* bias;
   int* err;
+  int nparts;                // tensor maps of A in use (1 = an ordinary tensor)
+  int part_c0[kMaxAParts];   // first channel (K column) of each part
 };
+
+// Part of A holding channel (K column) c, and c relative to that part.
+__device__ __forceinline__ int a_part(const TcParams& p, int* c) {
+  int pi = 0;
+#pragma unroll
+  for (int q = 1; q < kMaxAParts; ++q)
+    if (q < p.nparts && *c >= p.part_c0[q]) pi = q;
+  *c -= p.part_c0[pi];
+  return pi;
+}
 
 // BK: K depth of one pipeline stage, 32 or 64.  Deeper stages halve the barrier handoffs per
 // K (each handoff costs a few hundred cycles of single-thread latency); CTA pairs use 64 (one
@@ -176,7 +196,7 @@ __device__ __forceinline__ bool warp_wait_backoff(uint64_t* bar, uint32_t parity
 // diverged lane spends about half again as long per barrier handoff.
 template <int BN, int CB, int MODE, bool RES, int PAIR, int BK_, int MS_, bool WR_>
 __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+    tc_gemm_kernel(const __grid_constant__ AMaps amaps, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapY, const __grid_constant__ CUtensorMap mapR,
                    const TcParams p) {
   using C = Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>;
@@ -226,7 +246,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&mapA);
+    for (int i = 0; i < p.nparts; ++i) prefetch_tmap(&amaps.m[i]);
     prefetch_tmap(&mapB);
     prefetch_tmap(&mapY);
     if constexpr (RES) prefetch_tmap(&mapR);
@@ -320,12 +340,13 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
               // K padding past the last tap: re-read the last tap, its weights are zero
               const int rr = tap < p.taps ? r : (p.taps - 1) / p.kw;
               const int qq = tap < p.taps ? q : (p.taps - 1) - ((p.taps - 1) / p.kw) * p.kw;
-              const int cc = tap < p.taps ? c0 : p.cpad - CB;
+              int cc = tap < p.taps ? c0 : p.cpad - CB;
+              const CUtensorMap* mapA = &amaps.m[a_part(p, &cc)];
               if constexpr (PAIR == 2)
-                tma_load_im2col_4d_pair(&mapA, bar_leader, a_dst + j * C::A_SUB, cc, w0, h0, img,
+                tma_load_im2col_4d_pair(mapA, bar_leader, a_dst + j * C::A_SUB, cc, w0, h0, img,
                                         (uint16_t)(qq * p.dil_w), (uint16_t)(rr * p.dil_h));
               else
-                tma_load_im2col_4d(&mapA, &full[s], a_dst + j * C::A_SUB, cc, w0, h0, img, (uint16_t)(qq * p.dil_w),
+                tma_load_im2col_4d(mapA, &full[s], a_dst + j * C::A_SUB, cc, w0, h0, img, (uint16_t)(qq * p.dil_w),
                                    (uint16_t)(rr * p.dil_h));
               c0 += CB;
               if (c0 == p.cpad) {
@@ -337,10 +358,12 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
                 }
               }
             } else {
+              int kc = k;
+              const CUtensorMap* mapA = &amaps.m[a_part(p, &kc)];
               if constexpr (PAIR == 2)
-                tma_load_3d_pair(&mapA, bar_leader, a_dst + j * C::A_SUB, k, m0, bz);
+                tma_load_3d_pair(mapA, bar_leader, a_dst + j * C::A_SUB, kc, m0, bz);
               else
-                tma_load_3d(&mapA, &full[s], a_dst + j * C::A_SUB, k, m0, bz);
+                tma_load_3d(mapA, &full[s], a_dst + j * C::A_SUB, kc, m0, bz);
             }
             if (do_b) {
               if constexpr (PAIR == 2)
@@ -718,7 +741,7 @@ int pair_clusters(K kern, uint32_t smem, int threads, int sms) {
 }
 
 template <int BN, int CB, int MODE, bool RES, int PAIR, int BK, int MS = 1, bool WR = false>
-int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr,
+int launch_variant(const AMaps& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr,
                    const TcParams& p, int sms, cudaStream_t stream) {
   using C = Cfg<BN, CB, RES, PAIR, BK, MS, WR>;
   auto kern = tc_gemm_kernel<BN, CB, MODE, RES, PAIR, BK, MS, WR>;
@@ -781,7 +804,7 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
 }
 
 template <int MODE, bool RES>
-int dispatch_bn_cb(int bn, int cb, int pair, int bk, int ms, int wr, const CUtensorMap& ma, const CUtensorMap& mb,
+int dispatch_bn_cb(int bn, int cb, int pair, int bk, int ms, int wr, const AMaps& ma, const CUtensorMap& mb,
                    const CUtensorMap& my, const CUtensorMap& mr, const TcParams& p, int sms, cudaStream_t s) {
 #define SPINN_TC_CASE(BNV, CBV, PV, BKV)                                             \
   if (bn == BNV && cb == CBV && pair == PV && bk == BKV && ms == 1 && !wr) \
@@ -985,8 +1008,21 @@ bool tc_gemm_supported(const TcGemmArgs& a, std::string* why) {
   if (a.batch < 1) return fail("batch must be at least 1");
   if (a.batch > 1 && (a.a_mode != 1 || a.res)) return fail("batched GEMM needs a row-major A and no residual");
   if (a.ldy % 4 != 0 || a.ldy < a.N) return fail("output row stride must be a multiple of 4 floats");
-  if ((reinterpret_cast<uintptr_t>(a.y) & 15) || (reinterpret_cast<uintptr_t>(a.wt) & 15) ||
-      (reinterpret_cast<uintptr_t>(a.x) & 15))
+  if (a.nparts > 1) {
+    // A as the channel concatenation of parts: each a whole number of channel blocks
+    if (a.nparts > kMaxAParts || a.batch != 1) return fail("at most four parts of A, no batch");
+    const int cb = a.a_mode == 0 ? channel_block(a.cpad) : 32;
+    int c = 0;
+    for (int i = 0; i < a.nparts; ++i) {
+      if (!a.xpart[i] || (reinterpret_cast<uintptr_t>(a.xpart[i]) & 15)) return fail("part of A not 16-byte aligned");
+      if (a.part_c0[i] != c || cb == 0 || a.part_cpad[i] % cb) return fail("parts of A are not whole channel blocks");
+      c += a.part_cpad[i];
+    }
+    if (c != (a.a_mode == 0 ? a.cpad : a.K)) return fail("parts of A do not add up to its channels");
+  } else if (reinterpret_cast<uintptr_t>(a.x) & 15) {
+    return fail("operand not 16-byte aligned");
+  }
+  if ((reinterpret_cast<uintptr_t>(a.y) & 15) || (reinterpret_cast<uintptr_t>(a.wt) & 15))
     return fail("operand not 16-byte aligned");
   if (a.res && (a.ldr % 4 != 0 || (reinterpret_cast<uintptr_t>(a.res) & 15))) return fail("residual misaligned");
   if (a.kpad % 32 != 0) return fail("weight K padding must be a multiple of 32");
@@ -1028,8 +1064,12 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   const size_t ws_limit = (a.ws && a.batch == 1) ? std::min(a.ws_bytes, kWsCap) : 0;  // batched: no split
   const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn, a.batch == 1);
   const int arows = kBM * tp.ms;  // A rows per box
-  CUtensorMap ma, mb, my, mr;
+  AMaps ma;
+  CUtensorMap mb, my, mr;
   int rc;
+  const int nparts = a.nparts > 1 ? a.nparts : 1;
+  p.nparts = nparts;
+  for (int i = 0; i < kMaxAParts; ++i) p.part_c0[i] = i < nparts && a.nparts > 1 ? a.part_c0[i] : 0;
   if (a.a_mode == 0) {
     p.cpad = a.cpad;
     p.taps = a.kh * a.kw;
@@ -1044,15 +1084,23 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     p.pad_w = a.pw;
     int lw, lh, uw, uh;
     im2col_corners(a, &lw, &lh, &uw, &uh);
-    rc = encode_im2col_4d(&ma, a.x, a.n, a.h, a.w, a.cpad, lw, lh, uw, uh, cb, arows, a.sw, a.sh, swizzle_for(cb));
-    if (rc) return rc;
+    for (int i = 0; i < nparts; ++i) {
+      const float* x = nparts > 1 ? a.xpart[i] : a.x;
+      const int c = nparts > 1 ? a.part_cpad[i] : a.cpad;
+      rc = encode_im2col_4d(&ma.m[i], x, a.n, a.h, a.w, c, lw, lh, uw, uh, cb, arows, a.sw, a.sh, swizzle_for(cb));
+      if (rc) return rc;
+    }
   } else {
     p.cpad = a.K;
     p.taps = 1;
     p.kw = 1;
-    rc = encode_tiled_3d(&ma, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.batch, (uint64_t)a.lda * 4, 32,
-                         (uint32_t)arows, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
+    for (int i = 0; i < nparts; ++i) {
+      const float* x = nparts > 1 ? a.xpart[i] : a.x;
+      const int k = nparts > 1 ? a.part_cpad[i] : a.K, ld = nparts > 1 ? a.part_cpad[i] : a.lda;
+      rc = encode_tiled_3d(&ma.m[i], x, (uint64_t)k, (uint64_t)a.M, (uint64_t)a.batch, (uint64_t)ld * 4, 32,
+                           (uint32_t)arows, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
   }
   p.num_kb = (K + tp.bk - 1) / tp.bk;  // stages beyond kpad read zero weights
   const int bn = tp.bn;

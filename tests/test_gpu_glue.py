@@ -122,3 +122,23 @@ def test_concat_aligned_parts_one_launch(cuda_lib, ref_oracle, tmp_path):
     g.mark_output(y)
     out, ref = _run_both(ref_oracle, tmp_path, g, xv)
     assert rel_l2(out, ref) <= 2e-3, rel_l2(out, ref)
+
+
+def test_concat_read_in_parts_matches_materialised(cuda_lib):
+    """A channel Concat whose only reader is a tensor-core convolution is not materialised: the
+    convolution fetches each channel block from the Concat's inputs.  Same instructions per
+    element as the copied Concat (plan flag NO_FUSE), so the outputs are bit-identical."""
+    from spinn_b200 import ennf, lib, netdef, runtime
+    img = ennf.convert(netdef.yolo_shaped(batch=2, image=320))
+    x = netdef.yolo_input(2, 320)
+    em = ennf.read(img)
+    n_cat = sum(1 for nd in em.nodes if ennf.OP_NAME.get(nd.op_type) == "Concat")
+    outs, cats = [], []
+    for flags in (0, lib.PLAN_NO_FUSE):
+        m = runtime.Model(img, flags=flags | lib.PLAN_PROFILE)
+        outs.append(m.run(x))
+        m.run_profiled()
+        cats.append(sum(1 for op, ms, fl in m.profile() if ennf.OP_NAME.get(op) == "Concat"))
+        m.close()
+    assert np.array_equal(outs[0], outs[1])
+    assert cats[1] == n_cat and cats[0] < n_cat - 10, cats
