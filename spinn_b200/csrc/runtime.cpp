@@ -421,19 +421,26 @@ static bool concat_feeds_tc_conv(SpinnCudaModel* m, int ci, int whole, const std
   if ((act == 4 || act == 5) && KH == 1 && KW == 1) return false;  // may become a bottleneck-tail expand
   const int C = (int)X.dims[1];
   if (C % 4) return false;
-  const bool tiled = KH == 1 && KW == 1 && SH == 1 && SW == 1 && cp.pads[0] == 0 && cp.pads[1] == 0 &&
-                     Y.dims[2] == X.dims[2] && Y.dims[3] == X.dims[3];
+  // a pointwise convolution reads A in 32-column tiled boxes when every part is a multiple of
+  // 32 channels (conv_reads_parts_tiled), otherwise through the im2col path with the channel
+  // block of the concatenated channels
   int cb = 32;
-  if (!tiled)
-    for (int c : {32, 16, 8, 4})
-      if (C % c == 0) {
-        cb = c;
-        break;
-      }
+  for (int c : {32, 16, 8, 4})
+    if (C % c == 0) {
+      cb = c;
+      break;
+    }
   for (auto id : parts) {
     const TensorRec& t = m->tensors[id];
     if (t.ndim != 4 || (int)t.dims[1] % cb) return false;
   }
+  return true;
+}
+
+// Whether a pointwise convolution reading a Concat in parts can use tiled A boxes (32 columns).
+static bool conv_reads_parts_tiled(const SpinnCudaModel* m, const std::vector<int>& part_bufs) {
+  for (int b : part_bufs)
+    if (m->bufs[b].cpad % 32) return false;
   return true;
 }
 
@@ -837,7 +844,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             a.act = act;
             a.round_out = rnd;
             a.reverse = (m->tc_layers++) & 1;
-            if (KHc == 1 && KWc == 1 && SHc == 1 && SWc == 1 && PHc == 0 && PWc == 0 && OH == Hc && OW == Wc) {
+            if (KHc == 1 && KWc == 1 && SHc == 1 && SWc == 1 && PHc == 0 && PWc == 0 && OH == Hc && OW == Wc &&
+                (vparts.empty() || conv_reads_parts_tiled(m, vparts))) {
               // a pointwise conv over NHWC rows is a plain GEMM: tiled TMA boxes for A
               a.a_mode = 1;
               a.K = Cc;
