@@ -5,6 +5,7 @@
 //
 // Semantics follow the reference operators cited at each kernel; layouts are NHWC with the
 // channel dimension padded to `cpad` (a multiple of 4) where the tensor-core path needs it.
+#include <algorithm>
 #include <atomic>
 
 #include "internal.h"
@@ -294,6 +295,52 @@ __global__ void split_rows_kernel(SplitParts parts, const float* __restrict__ sr
   }
 }
 
+// Last-axis Concat gathered from pieces (launch_gather_rows): one 32 x 32 tile (channels x
+// positions of one image of one piece) per block iteration, staged in shared memory so that
+// both the read (along channels for NHWC pieces, along positions for row pieces) and the
+// write (along positions) are coalesced.  tile0[k] is the first tile of piece k.
+struct GatherTiles {
+  long tile0[kGatherMaxPieces + 1];
+  int ctiles[kGatherMaxPieces], ltiles[kGatherMaxPieces];
+};
+__global__ void __launch_bounds__(256) gather_rows_kernel(GatherPieces g, GatherTiles t, float* __restrict__ dst,
+                                                          int n, int ctot, int ltot) {
+  __shared__ float tile[32][33];
+  const long total = t.tile0[g.n];
+  for (long u = blockIdx.x; u < total; u += gridDim.x) {
+    int k = 0;
+    while (k + 1 < g.n && u >= t.tile0[k + 1]) ++k;
+    const long local = u - t.tile0[k];
+    const long per_img = (long)t.ctiles[k] * t.ltiles[k];
+    const int b = (int)(local / per_img);
+    const int r = (int)(local - (long)b * per_img);
+    const int cb = (r / t.ltiles[k]) * 32, lb = (r % t.ltiles[k]) * 32;
+    const int chans = g.chans[k], len = g.len[k], ld = g.ld[k];
+    if (g.nhwc[k]) {
+      // src[b][l][c0 + c]: lanes along channels
+      const float* s = g.src[k] + (size_t)b * len * ld + g.c0[k];
+      for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int l = lb + i, c = cb + threadIdx.x;
+        tile[threadIdx.x][i] = (l < len && c < chans) ? __ldg(s + (size_t)l * ld + c) : 0.0f;
+      }
+    } else {
+      // src[b][c][l]: lanes along positions
+      const float* s = g.src[k] + (size_t)b * chans * ld;
+      for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = cb + i, l = lb + threadIdx.x;
+        tile[i][threadIdx.x] = (l < len && c < chans) ? __ldg(s + (size_t)c * ld + l) : 0.0f;
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const int c = cb + i, l = lb + threadIdx.x;
+      if (c < chans && l < len)
+        dst[((size_t)b * ctot + g.dst_c[k] + c) * ltot + g.dst_l[k] + l] = tile[i][threadIdx.x];
+    }
+    __syncthreads();  // the tile is reused by the next iteration
+  }
+}
+
 // AveragePool (SPINN/run_time/ops/pool/avgpool.c): divisor = window taps inside the image,
 // or the full window when count_include_pad.
 __global__ void avgpool_nhwc_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
@@ -443,13 +490,16 @@ __global__ void depthwise_kernel(const float4* __restrict__ x, const float4* __r
 
 // Depthwise 3x3 convolution (dilation 1, stride S = 1 or 2), NHWC, persistent CTAs.  A work
 // unit is a tile of 8 x TW output pixels (TW = 16 at stride 1, 8 at stride 2) x 32 channels of
-// one image.  One thread per CTA loads the unit's input window (its halo included) with a
+// one image.  One thread per CTA loads each unit's input window (its halo included) with a
 // single 4-D TMA box -- each pixel's 32-channel slice is one 128-B line, out-of-range pixels
-// and channels arrive as zeros, which is the convolution's zero padding -- into one of two
-// shared-memory buffers, so the next unit's window is in flight while the CTA computes the
-// current one: HBM sees each input byte about once, the halo comes from L2.  Thread (p, q)
-// computes channel quad q of output pixels p, p + 32, ... with the taps in the order r, then s,
-// and applies the epilogue of depthwise_kernel (bias, residual, activation, tf32 rounding).
+// and channels arrive as zeros, which is the convolution's zero padding -- into a ring of
+// shared-memory buffers, up to three units ahead of the one being computed, so that HBM sees
+// each input byte about once (the halo comes from L2) and enough bytes are in flight per SM to
+// keep it streaming.  Thread (block, q) computes channel quad q of a block of RB x CB output
+// pixels (2 x 2 at stride 1, 2 x 1 at stride 2), reading each window pixel of the block once
+// from shared memory, with the taps accumulated in the order r, then s for every output; the
+// epilogue is depthwise_kernel's (bias, residual, activation, tf32 rounding).  The 9 weights
+// of the CTA's channel group stay in registers while consecutive units share it.
 // w is [9][cpad], bias [cpad], residual NHWC like y.  Waits are bounded; on expiry the CTA
 // raises *err (code 4) and stops.
 constexpr int kDwThreads = 256;
@@ -458,18 +508,26 @@ struct DwTile {
   static constexpr int TH = 8, TW = S == 1 ? 16 : 8;
   static constexpr int IH = (TH - 1) * S + 3, IW = (TW - 1) * S + 3;
   static constexpr uint32_t BYTES = IH * IW * 128;  // one window: IH x IW pixels x 32 channels
-  static constexpr int PIX = TH * TW / (kDwThreads / 8);  // output pixels per thread
+  static constexpr int RB = 2, CB = S == 1 ? 2 : 1;  // output block of one thread
+  static constexpr int BX = TW / CB;                 // blocks per tile row
+  static constexpr int BR = (RB - 1) * S + 3, BC = (CB - 1) * S + 3;  // window rows / columns a block reads
+  static_assert((TH / RB) * BX * 8 == kDwThreads, "one block per thread");
+  // Window buffers per CTA (loads run BUFS - 1 units ahead) and CTAs per SM: two CTAs of
+  // 128 registers a thread (a 2 x 2 block keeps 16 window pixels, 4 accumulators and the 9
+  // weights live); 4 x 23 KB or 3 x 37 KB of windows each.
+  static constexpr int BUFS = S == 1 ? 4 : 3;
+  static constexpr int MIN_CTAS = 2;
 };
 
 template <int S>
-__global__ void __launch_bounds__(kDwThreads) depthwise3x3_tma_kernel(
+__global__ void __launch_bounds__(kDwThreads, DwTile<S>::MIN_CTAS) depthwise3x3_tma_kernel(
     const __grid_constant__ CUtensorMap mx, const float4* __restrict__ w, const float4* __restrict__ bias,
     const float4* __restrict__ res, float4* __restrict__ y, int n, int c4, int oh, int ow, int ph, int pw,
     int tiles_x, int tiles_y, int groups, int act, int round_out, int* err) {
   using T = DwTile<S>;
   extern __shared__ uint8_t dw_raw[];
   float4* buf = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(dw_raw) + 127) & ~uintptr_t(127));
-  __shared__ __align__(8) uint64_t full[2];
+  __shared__ __align__(8) uint64_t full[T::BUFS];
   __shared__ volatile int abort_flag;
   const long units = (long)groups * n * tiles_y * tiles_x;
   auto unit_coords = [&](long u, int* g, int* b, int* ty, int* tx) {
@@ -480,100 +538,123 @@ __global__ void __launch_bounds__(kDwThreads) depthwise3x3_tma_kernel(
     *b = (int)(r % n);
     *g = (int)(r / n);
   };
-  auto issue = [&](long u, int slot) {
+  // thread 0's record of loads in flight: bit s set while buffer s awaits the phase in bit s of armed_ph
+  uint32_t armed = 0, armed_ph = 0;
+  auto issue = [&](long u, int it) {  // unit u is the CTA's it-th: buffer it % BUFS, phase (it / BUFS) & 1
     int g, b, ty, tx;
     unit_coords(u, &g, &b, &ty, &tx);
+    const int slot = it % T::BUFS;
     mbar_arrive_expect_tx(&full[slot], T::BYTES);
     tma_load_4d(&mx, &full[slot], buf + (size_t)slot * (T::BYTES / 16), g * 32, tx * T::TW * S - pw,
                 ty * T::TH * S - ph, b);
+    armed |= 1u << slot;
+    armed_ph = (armed_ph & ~(1u << slot)) | ((uint32_t)((it / T::BUFS) & 1) << slot);
   };
   if (threadIdx.x == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+    for (int sl = 0; sl < T::BUFS; ++sl) mbar_init(&full[sl], 1);
     abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0 && (long)blockIdx.x < units) {
+  if (threadIdx.x == 0) {
     prefetch_tmap(&mx);
-    issue(blockIdx.x, 0);
+    for (int k = 0; k < T::BUFS - 1; ++k)
+      if ((long)blockIdx.x + (long)k * gridDim.x < units) issue(blockIdx.x + (long)k * gridDim.x, k);
   }
-  const int q = threadIdx.x & 7, slot_p = threadIdx.x >> 3;
+  const int q = threadIdx.x & 7, blk = threadIdx.x >> 3;
+  const int by = blk / T::BX, bx = blk - by * T::BX;  // block origin: output row RB*by, column CB*bx of the tile
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  // thread 0's record of loads in flight: bit s set while buffer s awaits the phase in bit s of armed_ph
-  uint32_t armed = (long)blockIdx.x < units ? 1u : 0u, armed_ph = 0;
+  int wg = -1;  // channel quad whose weights are in registers
+  float4 k[9];
   int it = 0;
   for (long u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-    const int cur = it & 1;
-    const long nu = u + gridDim.x;
-    if (threadIdx.x == 0 && nu < units) {  // the other buffer was released by the last iteration's barrier
-      issue(nu, cur ^ 1);
-      armed |= 1u << (cur ^ 1);
-      armed_ph = (armed_ph & ~(1u << (cur ^ 1))) | ((uint32_t)(((it + 1) >> 1) & 1) << (cur ^ 1));
-    }
-    bool ok = mbar_wait(&full[cur], (it >> 1) & 1, &abort_flag, 4000000000ull);
+    const int cur = it % T::BUFS;
+    const long nu = u + (long)(T::BUFS - 1) * gridDim.x;
+    // the buffer of unit it + BUFS - 1 held unit it - 1, released by the last iteration's barrier
+    if (threadIdx.x == 0 && nu < units) issue(nu, it + T::BUFS - 1);
+    bool ok = mbar_wait(&full[cur], (uint32_t)((it / T::BUFS) & 1), &abort_flag, 4000000000ull);
     if (!__syncthreads_and(ok)) break;
     if (threadIdx.x == 0) armed &= ~(1u << cur);
     int g, b, ty, tx;
     unit_coords(u, &g, &b, &ty, &tx);
     const int qq = g * 8 + q;  // channel quad
     if (qq < c4) {
-      float4 k[9];
+      if (qq != wg) {  // a new channel group: its weights
 #pragma unroll
-      for (int t = 0; t < 9; ++t) k[t] = __ldg(w + (size_t)t * c4 + qq);
-      const float4 bb = bias ? __ldg(bias + qq) : zero;
-      const float4* win = buf + (size_t)cur * (T::BYTES / 16);
-#pragma unroll
-      for (int j = 0; j < T::PIX; ++j) {
-        const int p = slot_p + j * (kDwThreads / 8);
-        const int ly = p / T::TW, lx = p - ly * T::TW;
-        const int oy = ty * T::TH + ly, ox = tx * T::TW + lx;
-        if (oy >= oh || ox >= ow) continue;
-        float4 acc = zero;
-#pragma unroll
-        for (int r = 0; r < 3; ++r)
-#pragma unroll
-          for (int s = 0; s < 3; ++s) {
-            const float4 v = win[((ly * S + r) * T::IW + lx * S + s) * 8 + q];
-            const float4 kk = k[r * 3 + s];
-            acc.x = fmaf(v.x, kk.x, acc.x);
-            acc.y = fmaf(v.y, kk.y, acc.y);
-            acc.z = fmaf(v.z, kk.z, acc.z);
-            acc.w = fmaf(v.w, kk.w, acc.w);
-          }
-        if (bias) {
-          acc.x += bb.x;
-          acc.y += bb.y;
-          acc.z += bb.z;
-          acc.w += bb.w;
-        }
-        const size_t o = (((size_t)b * oh + oy) * ow + ox) * c4 + qq;
-        if (res && (act == 4 || act == 5)) {
-          const float4 rr = res[o];
-          acc.x += rr.x;
-          acc.y += rr.y;
-          acc.z += rr.z;
-          acc.w += rr.w;
-        }
-        acc.x = apply_act(acc.x, act);
-        acc.y = apply_act(acc.y, act);
-        acc.z = apply_act(acc.z, act);
-        acc.w = apply_act(acc.w, act);
-        if (round_out) {
-          acc.x = to_tf32_rna(acc.x);
-          acc.y = to_tf32_rna(acc.y);
-          acc.z = to_tf32_rna(acc.z);
-          acc.w = to_tf32_rna(acc.w);
-        }
-        y[o] = acc;
+        for (int t = 0; t < 9; ++t) k[t] = __ldg(w + (size_t)t * c4 + qq);
+        wg = qq;
       }
+      const float4* win = buf + (size_t)cur * (T::BYTES / 16);
+      const float4 bb = bias ? __ldg(bias + qq) : zero;
+      float4 acc[T::RB][T::CB];
+#pragma unroll
+      for (int i = 0; i < T::RB; ++i)
+#pragma unroll
+        for (int j = 0; j < T::CB; ++j) acc[i][j] = zero;
+      // window row wr of the block feeds output row i with tap r = wr - i*S (0..2); each of its
+      // BC pixels feeds output column j with tap s = wc - j*S
+#pragma unroll
+      for (int wr = 0; wr < T::BR; ++wr) {
+        float4 v[T::BC];
+#pragma unroll
+        for (int wc = 0; wc < T::BC; ++wc)
+          v[wc] = win[((by * T::RB * S + wr) * T::IW + bx * T::CB * S + wc) * 8 + q];
+#pragma unroll
+        for (int i = 0; i < T::RB; ++i) {
+          const int r = wr - i * S;
+          if (r < 0 || r > 2) continue;
+#pragma unroll
+          for (int j = 0; j < T::CB; ++j)
+#pragma unroll
+            for (int s = 0; s < 3; ++s) {
+              const float4 x = v[j * S + s], kk = k[r * 3 + s];
+              acc[i][j].x = fmaf(x.x, kk.x, acc[i][j].x);
+              acc[i][j].y = fmaf(x.y, kk.y, acc[i][j].y);
+              acc[i][j].z = fmaf(x.z, kk.z, acc[i][j].z);
+              acc[i][j].w = fmaf(x.w, kk.w, acc[i][j].w);
+            }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < T::RB; ++i)
+#pragma unroll
+        for (int j = 0; j < T::CB; ++j) {
+          const int oy = ty * T::TH + by * T::RB + i, ox = tx * T::TW + bx * T::CB + j;
+          if (oy >= oh || ox >= ow) continue;
+          float4 a = acc[i][j];
+          if (bias) {
+            a.x += bb.x;
+            a.y += bb.y;
+            a.z += bb.z;
+            a.w += bb.w;
+          }
+          const size_t o = (((size_t)b * oh + oy) * ow + ox) * c4 + qq;
+          if (res && (act == 4 || act == 5)) {
+            const float4 rr = res[o];
+            a.x += rr.x;
+            a.y += rr.y;
+            a.z += rr.z;
+            a.w += rr.w;
+          }
+          a.x = apply_act(a.x, act);
+          a.y = apply_act(a.y, act);
+          a.z = apply_act(a.z, act);
+          a.w = apply_act(a.w, act);
+          if (round_out) {
+            a.x = to_tf32_rna(a.x);
+            a.y = to_tf32_rna(a.y);
+            a.z = to_tf32_rna(a.z);
+            a.w = to_tf32_rna(a.w);
+          }
+          y[o] = a;
+        }
     }
-    __syncthreads();  // every thread is done with buffer `cur`; the next iteration may refill it
+    __syncthreads();  // every thread is done with buffer `cur`; it may be refilled
   }
   if (threadIdx.x == 0 && abort_flag) {
-    // let any window still in flight land before the CTA's shared memory goes away
+    // let every window still in flight land before the CTA's shared memory goes away
     volatile int dummy = 0;
-    for (int sl = 0; sl < 2; ++sl)
+    for (int sl = 0; sl < T::BUFS; ++sl)
       if (armed & (1u << sl)) mbar_wait(&full[sl], (armed_ph >> sl) & 1, &dummy, 200000000ull);
     atomicExch(err, 4);
   }
@@ -861,6 +942,27 @@ int launch_split_rows(const SplitParts& parts, const float* src, int src_ld, lon
   SPINN_LAUNCH_CHECK();
 }
 
+int launch_gather_rows(const GatherPieces& g, float* dst, int n, int ctot, int ltot, cudaStream_t s) {
+  SPINN_CHECK_ARG(g.n >= 1 && g.n <= kGatherMaxPieces && n >= 0 && ctot >= 0 && ltot >= 0,
+                  "gather_rows: %d pieces", g.n);
+  GatherTiles t{};
+  t.tile0[0] = 0;
+  for (int k = 0; k < g.n; ++k) {
+    SPINN_CHECK_ARG(g.chans[k] >= 0 && g.len[k] >= 0 && g.dst_c[k] >= 0 && g.dst_c[k] + g.chans[k] <= ctot &&
+                        g.dst_l[k] >= 0 && g.dst_l[k] + g.len[k] <= ltot && g.c0[k] >= 0 &&
+                        (g.nhwc[k] ? g.c0[k] + g.chans[k] <= g.ld[k] : g.len[k] <= g.ld[k]),
+                    "gather_rows: piece %d out of range", k);
+    t.ctiles[k] = (g.chans[k] + 31) / 32;
+    t.ltiles[k] = (g.len[k] + 31) / 32;
+    t.tile0[k + 1] = t.tile0[k] + (long)n * t.ctiles[k] * t.ltiles[k];
+  }
+  const long total = t.tile0[g.n];
+  if (total == 0) return 0;
+  const int grid = (int)std::min<long>(total, 148L * 8);
+  gather_rows_kernel<<<grid, dim3(32, 8), 0, s>>>(g, t, dst, n, ctot, ltot);
+  SPINN_LAUNCH_CHECK();
+}
+
 int launch_avgpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh, int kw,
                         int sh, int sw, int ph, int pw, int count_include_pad, cudaStream_t s) {
   SPINN_CHECK_ARG(cpad % 4 == 0, "avgpool: channel stride %d not a multiple of 4", cpad);
@@ -905,7 +1007,7 @@ int launch_depthwise3x3_tma(const float* x, const float* w, const float* bias, c
   const int tiles_x = (ow + T::TW - 1) / T::TW, tiles_y = (oh + T::TH - 1) / T::TH;
   const int groups = (cpad / 4 + 7) / 8;
   const long units = (long)groups * n * tiles_y * tiles_x;
-  const int smem = (int)(2 * T::BYTES + 128);
+  const int smem = (int)(T::BUFS * T::BYTES + 128);
   static std::atomic<uint64_t> configured{0};
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {

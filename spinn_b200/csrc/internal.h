@@ -226,6 +226,20 @@ struct SplitParts {
   int ld[kCatMaxParts], off[kCatMaxParts], width[kCatMaxParts];
 };
 int launch_split_rows(const SplitParts& parts, const float* src, int src_ld, long rows, cudaStream_t s);
+// Concat along the last axis of 3-D row-major parts [N][C][L_i] into dst [N][ctot][ltot], where
+// a part is given as pieces: channel ranges stored row-major ([N][chans][ld], nhwc = 0) or as
+// an NHWC tensor whose H x W positions are the part's L axis ([N][L][ld], channels c0.. of ld;
+// nhwc = 1), which is read transposed -- the NCHW conversion of a Reshape [N,C,H,W] -> [N,C,HW]
+// and any channel Concat before it happen in this one pass.
+constexpr int kGatherMaxPieces = 16;
+struct GatherPieces {
+  int n;
+  const float* src[kGatherMaxPieces];
+  int nhwc[kGatherMaxPieces], ld[kGatherMaxPieces], c0[kGatherMaxPieces];
+  int chans[kGatherMaxPieces], len[kGatherMaxPieces];
+  int dst_c[kGatherMaxPieces], dst_l[kGatherMaxPieces];
+};
+int launch_gather_rows(const GatherPieces& g, float* dst, int n, int ctot, int ltot, cudaStream_t s);
 // TopK over the last axis of a row-major [rows][n] tensor (n <= kTopkMaxN): k largest values
 // (descending, ties by ascending index) and their int64 indices, each [rows][k].
 constexpr int kTopkMaxN = 16384;

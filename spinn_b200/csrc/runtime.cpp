@@ -141,6 +141,8 @@ struct SpinnCudaModel {
   uint64_t wbytes = 0;
   int tc_layers = 0;               // tensor-core conv steps planned so far (tile walk direction)
   std::map<int, std::vector<int>> virt_cat;  // Concat outputs read in parts: tensor -> part buffers
+  std::map<int, int> lazy_nchw;  // Reshape outputs gathered from NHWC: tensor -> viewed tensor
+  std::map<int, int> b_trans;    // Transposes folded into a MatMul's B: tensor -> untransposed tensor
   float* splitk_ws = nullptr;      // split-K partial sums, shared by all steps (one stream)
   size_t splitk_bytes = 0;
   std::vector<float> whost;        // pre-transformed weights before upload
@@ -444,6 +446,32 @@ static bool conv_reads_parts_tiled(const SpinnCudaModel* m, const std::vector<in
   return true;
 }
 
+// Whether node `ri` is a Reshape [N,C,H,W] -> [N,C,H*W] whose only reader is a Concat along
+// the last axis of 3-D tensors with at most four inputs.  Such a Reshape of an NHWC tensor is
+// left as a view: the Concat reads the NHWC data transposed (launch_gather_rows), so the NCHW
+// copy that the Reshape would otherwise need is never made.
+static bool reshape_feeds_gather(const SpinnCudaModel* m, int ri, const std::vector<int>& readers,
+                                 const std::vector<int>& reader_node) {
+  const NodeRec& nd = m->nodes[ri];
+  if (nd.op != OP_RESHAPE || nd.in.empty() || nd.out.size() != 1) return false;
+  const TensorRec& X = m->tensors[nd.in[0]];
+  const int yid = nd.out[0];
+  const TensorRec& Y = m->tensors[yid];
+  if (X.ndim != 4 || Y.ndim != 3 || Y.dims[0] != X.dims[0] || Y.dims[1] != X.dims[1] ||
+      (uint64_t)Y.dims[2] != (uint64_t)X.dims[2] * X.dims[3] || X.dtype == kDtypeInt64)
+    return false;
+  if (readers[yid] != 1 || reader_node[yid] <= ri) return false;
+  const NodeRec& cat = m->nodes[reader_node[yid]];
+  if (cat.op != OP_CONCAT || cat.in.size() > 4 || cat.out.size() != 1) return false;
+  int axis = 1;
+  if (cat.params.size() >= 4) std::memcpy(&axis, cat.params.data(), 4);
+  if (axis != 2 && axis != -1) return false;
+  if (m->tensors[cat.out[0]].ndim != 3) return false;
+  int uses = 0;
+  for (auto id : cat.in) uses += id == yid;
+  return uses == 1;
+}
+
 // ------------------------------------------------------------------ plan
 static int compile_model(SpinnCudaModel* m, uint64_t budget) {
   Planner P(m);
@@ -464,6 +492,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     }
   for (auto id : m->outputs) ++readers[id];
   std::map<int, std::vector<int>> virt_cat;  // concat tensor -> NHWC buffers of its parts
+  std::map<int, int> lazy_nchw;  // Reshape output -> the NHWC tensor it views (read by a gathering Concat)
+  std::map<int, int> b_trans;    // Transpose output read only as a MatMul's B -> the untransposed tensor
 
   auto add_step = [&](int node, uint16_t op, int kind, double flops, std::function<int(StepRec&)> b) {
     StepRec s;
@@ -999,6 +1029,15 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         const int xid = nd.in[0], yid = nd.out[0];
         const TensorRec& Y = m->tensors[yid];
         Buf& xbuf = m->bufs[xid];
+        if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && xbuf.lay == LAY_NHWC &&
+            reshape_feeds_gather(m, ni, readers, reader_node)) {
+          // an NCHW view that only a last-axis Concat reads: it gathers from the NHWC tensor
+          lazy_nchw[yid] = xid;
+          set_row(m->bufs[yid], Y);
+          m->bufs[yid].bytes = 0;
+          produced[yid] = 1;
+          break;
+        }
         const bool nhwc_trivial = xbuf.lay == LAY_NHWC && xbuf.h * xbuf.w == 1 && xbuf.cpad == xbuf.c;
         int src = xid;
         if (xbuf.lay == LAY_NHWC && !nhwc_trivial) src = ensure_row(xid, ni);
@@ -1277,6 +1316,94 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
           }
         const bool nhwc = TW.ndim == 4 && axis == 1;
         if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && is_cat && nhwc && parts.size() >= 2 && parts.size() <= 4 &&
+            readers[whole] == 1 && reader_node[whole] > ni && m->nodes[reader_node[whole]].in[0] == whole &&
+            reshape_feeds_gather(m, reader_node[whole], readers, reader_node)) {
+          // a channel Concat viewed as NCHW by a Reshape that a last-axis Concat gathers: that
+          // gather reads each part where it lies
+          std::vector<int> pbv;
+          for (auto id : parts) pbv.push_back(ensure_nhwc(id, ni));
+          bool all = true;
+          for (int b : pbv) all &= b >= 0;
+          if (all) {
+            virt_cat[whole] = pbv;
+            set_nhwc(m->bufs[whole], TW);
+            m->bufs[whole].bytes = 0;
+            produced[whole] = 1;
+            break;
+          }
+        }
+        if (is_cat && TW.ndim == 3 && axis == 2) {
+          bool any_lazy = false;
+          for (auto id : parts) any_lazy |= lazy_nchw.count(id) > 0;
+          if (any_lazy) {
+            // last-axis Concat of [N][C][L_i] parts, some of them NCHW views of NHWC tensors (or
+            // of channel Concats of them): one gathering pass writes the result
+            struct Piece {
+              int buf, nhwc, ld, chans, len, dst_c, dst_l;
+            };
+            std::vector<Piece> pcs;
+            const int N = TW.dims[0], C = TW.dims[1];
+            int col = 0;
+            for (auto id : parts) {
+              const TensorRec& T = m->tensors[id];
+              if (T.ndim != 3 || (int)T.dims[0] != N || (int)T.dims[1] != C) {
+                set_error("plan: Concat node %d: parts differ outside the concatenated axis", ni);
+                return SPINN_CUDA_EFORMAT;
+              }
+              const int L = T.dims[2];
+              auto lz = lazy_nchw.find(id);
+              if (lz != lazy_nchw.end()) {
+                auto vc = virt_cat.find(lz->second);
+                if (vc != virt_cat.end()) {
+                  int cc = 0;
+                  for (int pb : vc->second) {
+                    pcs.push_back({pb, 1, m->bufs[pb].cpad, m->bufs[pb].c, L, cc, col});
+                    cc += m->bufs[pb].c;
+                  }
+                } else {
+                  const int src = lz->second;
+                  pcs.push_back({src, 1, m->bufs[src].cpad, C, L, 0, col});
+                }
+              } else {
+                pcs.push_back({ensure_row(id, ni), 0, L, C, L, 0, col});
+              }
+              col += L;
+            }
+            if ((int)pcs.size() > kGatherMaxPieces) {
+              set_error("plan: Concat node %d gathers %d pieces (at most %d)", ni, (int)pcs.size(),
+                        kGatherMaxPieces);
+              return SPINN_CUDA_EUNSUPPORTED;
+            }
+            set_row(m->bufs[whole], TW);
+            const int L = TW.dims[2];
+            const int s = add_step(ni, nd.op, 6, 0, [=](StepRec& r) {
+              const Buf* w = &m->bufs[whole];
+              std::vector<const Buf*> src;
+              for (const Piece& p : pcs) src.push_back(&m->bufs[p.buf]);
+              r.run = [=](cudaStream_t st) {
+                GatherPieces g{};
+                g.n = (int)pcs.size();
+                for (size_t k = 0; k < pcs.size(); ++k) {
+                  g.src[k] = src[k]->ptr;
+                  g.nhwc[k] = pcs[k].nhwc;
+                  g.ld[k] = pcs[k].ld;
+                  g.c0[k] = 0;
+                  g.chans[k] = pcs[k].chans;
+                  g.len[k] = pcs[k].len;
+                  g.dst_c[k] = pcs[k].dst_c;
+                  g.dst_l[k] = pcs[k].dst_l;
+                }
+                return launch_gather_rows(g, w->ptr, N, C, L, st);
+              };
+              return 0;
+            });
+            P.touch(whole, s);
+            for (const Piece& p : pcs) P.touch(p.buf, s);
+            produced[whole] = 1;
+            break;
+          }
+        }
+        if (!(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && is_cat && nhwc && parts.size() >= 2 && parts.size() <= 4 &&
             readers[whole] == 1 &&
             reader_node[whole] > ni && concat_feeds_tc_conv(m, reader_node[whole], whole, parts)) {
           // the convolution reading this Concat fetches each channel block from its part
@@ -1421,16 +1548,43 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         for (int d = 0; d < X.ndim; ++d) perm[d] = (uint8_t)(X.ndim - 1 - d);  // default: reverse
         if (nd.params.size() >= 9 && nd.params[8] == X.ndim)
           for (int d = 0; d < X.ndim; ++d) perm[d] = nd.params[d];
-        const int xb = ensure_row(nd.in[0], ni);
+        // a swap of the last two axes (leading axes in place) is a batch of matrix transposes
+        bool last2 = X.ndim >= 2 && perm[X.ndim - 2] == X.ndim - 1 && perm[X.ndim - 1] == X.ndim - 2;
+        for (int d = 0; d + 2 < X.ndim; ++d) last2 &= perm[d] == d;
         const int yb = nd.out[0];
+        if (last2 && !(m->flags & SPINN_CUDA_PLAN_NO_FUSE) && readers[yb] == 1 && reader_node[yb] > ni &&
+            m->nodes[reader_node[yb]].op == OP_MATMUL && m->nodes[reader_node[yb]].in.size() >= 2 &&
+            m->nodes[reader_node[yb]].in[1] == yb && m->nodes[reader_node[yb]].in[0] != yb && X.dtype != kDtypeInt64) {
+          // B of the MatMul that reads it: the MatMul packs B from its transpose anyway, which is
+          // this tensor's input
+          b_trans[yb] = nd.in[0];
+          set_row(m->bufs[yb], m->tensors[yb]);
+          m->bufs[yb].bytes = 0;
+          produced[yb] = 1;
+          break;
+        }
+        const int xb = ensure_row(nd.in[0], ni);
         set_row(m->bufs[yb], m->tensors[yb]);
         std::vector<uint32_t> dims(X.dims, X.dims + 8);
         std::vector<uint8_t> pv(perm, perm + 8);
         const int ndim = X.ndim;
+        long mats = 1;
+        for (int d = 0; d + 2 < ndim; ++d) mats *= X.dims[d];
+        const int rows = ndim >= 2 ? (int)X.dims[ndim - 2] : 1, cols = ndim >= 1 ? (int)X.dims[ndim - 1] : 1;
         const int s = add_step(ni, nd.op, 7, 0, [=](StepRec& r) {
           const Buf* x = &m->bufs[xb];
           const Buf* y = &m->bufs[yb];
-          r.run = [=](cudaStream_t st) { return launch_permute(x->ptr, y->ptr, ndim, dims.data(), pv.data(), st); };
+          r.run = [=](cudaStream_t st) -> int {
+            if (!last2) return launch_permute(x->ptr, y->ptr, ndim, dims.data(), pv.data(), st);
+            const size_t plane = (size_t)rows * cols;
+            if (plane == 0) return 0;
+            for (long b0 = 0; b0 < mats; b0 += 65535) {  // grid.z holds at most 65535 matrices
+              const int nb = (int)std::min<long>(65535, mats - b0);
+              const int rc = launch_transpose(x->ptr + b0 * plane, y->ptr + b0 * plane, nb, rows, cols, st);
+              if (rc) return rc;
+            }
+            return 0;
+          };
           return 0;
         });
         P.touch(xb, s);
@@ -1558,9 +1712,15 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
                 row[2 * seg + k] = lo;
               }
         } else {
-          bb = ensure_row(nd.in[1], ni);
-          t.bytes = (uint64_t)batch_b * N * K * 4;
-          btt = P.new_buf(t);
+          auto bt_it = b_trans.find(nd.in[1]);
+          if (bt_it != b_trans.end()) {
+            // B is the transpose of a [.., N, K] tensor: that tensor is B's [N][K] form already
+            btt = ensure_row(bt_it->second, ni);
+          } else {
+            bb = ensure_row(nd.in[1], ni);
+            t.bytes = (uint64_t)batch_b * N * K * 4;
+            btt = P.new_buf(t);
+          }
           t.bytes = (uint64_t)batch_b * Np * kpad * 4;
           bpt = P.new_buf(t);
         }
@@ -1595,9 +1755,11 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
             int rc = launch_split_tf32(a->ptr, ap->ptr, batch * M, K, K, seg, 3 * seg, 0, 1, 0, st);
             if (rc) return rc;
             const float* wbase = woff != ~0ull ? m->wdev + woff : nullptr;
-            if (b) {
-              rc = launch_transpose(b->ptr, bt->ptr, (int)batch_b, K, N, st);  // -> [batch_b][N][K]
-              if (rc) return rc;
+            if (bt) {
+              if (b) {
+                rc = launch_transpose(b->ptr, bt->ptr, (int)batch_b, K, N, st);  // -> [batch_b][N][K]
+                if (rc) return rc;
+              }
               SPINN_CUDA_TRY(cudaMemsetAsync(bp->ptr, 0, bp->bytes, st));
               if (Np == N) {  // the planes are contiguous rows: one packing pass
                 rc = launch_split_tf32(bt->ptr, bp->ptr, batch_b * N, K, K, seg, kpad, 0, 0, 1, st);
@@ -1636,8 +1798,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
         });
         P.touch(ab, s);
         P.touch(at, s);
-        if (bb >= 0) {
-          P.touch(bb, s);
+        if (bb >= 0) P.touch(bb, s);
+        if (btt >= 0) {
           P.touch(btt, s);
           P.touch(bpt, s);
         }
@@ -1660,14 +1822,25 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
       return SPINN_CUDA_EFORMAT;
     }
     const TensorRec& t = m->tensors[id];
+    const int src = P.root(id);
+    const bool nhwc = m->bufs[id].lay == LAY_NHWC;
+    const uint64_t obytes = t.elems * elem_bytes(t);
+    // A row-major output that fills its own buffer is handed to the host where it lies: the
+    // buffer leaves the arena (nothing reuses it), and no staging copy runs.
+    bool direct = !nhwc && m->bufs[id].lay == LAY_ROW && m->bufs[src].lay == LAY_ROW && !m->bufs[src].external &&
+                  m->bufs[src].bytes == obytes && obytes > 0;
+    for (int ob : m->out_buf) direct &= ob != src;
+    if (direct) {
+      m->bufs[src].external = 1;
+      m->out_buf.push_back(src);
+      continue;
+    }
     Buf st;
     st.lay = LAY_ROW;
-    st.bytes = t.elems * elem_bytes(t);
+    st.bytes = obytes;
     st.external = 1;
     const int sb = P.new_buf(st);
     m->out_buf.push_back(sb);
-    const int src = P.root(id);
-    const bool nhwc = m->bufs[id].lay == LAY_NHWC;
     const int s = add_step(-1, 0, 7, 0, [m, id, sb, nhwc](StepRec& r) {
       const Buf* x = &m->bufs[id];
       const Buf* xr = x;
@@ -1684,6 +1857,8 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
   }
 
   m->virt_cat = virt_cat;
+  m->lazy_nchw = lazy_nchw;
+  m->b_trans = b_trans;
   // arena
   const int nsteps = (int)m->steps.size();
   int rc = plan_arena(m, nsteps, budget);
@@ -2074,6 +2249,27 @@ __attribute__((visibility("default"))) int spinn_cuda_copy_tensor(SpinnCudaModel
   if (!(m->flags & SPINN_CUDA_PLAN_KEEP) && !is_output) {
     set_error("spinn_cuda_copy_tensor: tensor %d is not a graph output; plan with SPINN_CUDA_PLAN_KEEP", tensor_id);
     return SPINN_CUDA_ESTATE;
+  }
+  // views without storage of their own: a Reshape to [N, C, H*W] gathered from its NHWC input
+  // has that input's NCHW bytes; a Transpose folded into a MatMul is its input transposed
+  auto lz = m->lazy_nchw.find(tensor_id);
+  if (lz != m->lazy_nchw.end()) return spinn_cuda_copy_tensor(m, lz->second, first, count, host, bytes);
+  auto bt = m->b_trans.find(tensor_id);
+  if (bt != m->b_trans.end()) {
+    const TensorRec& x = m->tensors[bt->second];
+    if (x.ndim < 2 || bytes % 4) {
+      set_error("spinn_cuda_copy_tensor: tensor %d is a folded transpose of a tensor below 2-D", tensor_id);
+      return SPINN_CUDA_EINVAL;
+    }
+    std::vector<float> tmp(bytes / 4);
+    const int rc = spinn_cuda_copy_tensor(m, bt->second, first, count, tmp.data(), bytes);
+    if (rc) return rc;
+    const uint64_t rows = x.dims[x.ndim - 2], cols = x.dims[x.ndim - 1], plane = rows * cols;
+    float* dst = static_cast<float*>(host);
+    for (uint64_t p0 = 0; plane && p0 + plane <= tmp.size(); p0 += plane)
+      for (uint64_t r = 0; r < rows; ++r)
+        for (uint64_t c = 0; c < cols; ++c) dst[p0 + c * rows + r] = tmp[p0 + r * cols + c];
+    return 0;
   }
   int r = tensor_id;
   while (m->bufs[r].alias >= 0) r = m->bufs[r].alias;

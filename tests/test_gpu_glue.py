@@ -142,3 +142,50 @@ def test_concat_read_in_parts_matches_materialised(cuda_lib):
         m.close()
     assert np.array_equal(outs[0], outs[1])
     assert cats[1] == n_cat and cats[0] < n_cat - 10, cats
+
+
+def test_head_concat_gathered_from_nhwc_parts(cuda_lib, ref_oracle, tmp_path):
+    """Detection-head pattern: per level a channel Concat of two convolution outputs, a Reshape
+    [N, C, H, W] -> [N, C, H*W] and one last-axis Concat of the levels as the graph output.  The
+    last Concat gathers straight from the NHWC convolution outputs (no NCHW copies, no channel
+    Concat, no output staging copy); one level's view has a second reader and is materialised
+    the ordinary way.  Against the reference, and bit-identical to the unfused plan."""
+    from spinn_b200 import ennf, lib, runtime
+    g, b, x, xv = _builder((2, 8, 12, 10))
+    levels = []
+    y = x
+    for i, width in enumerate((8, 16, 24)):
+        y = b.conv_bn(y, width, 3, 2 if i else 1)
+        n, c, h, w = g.shape(y)
+        box = b.conv(y, 5, 1, 1, 0, bias=True)      # odd channel counts: pad lanes in NHWC
+        cls = b.conv(y, 7, 3, 1, 1, bias=True)
+        levels.append(b.reshape(b.concat([box, cls]), (n, 12, h * w)))
+    extra = b.unary("Sigmoid", levels[1])           # a second reader: that view is materialised
+    g.mark_output(b.concat(levels, axis=2))
+    g.mark_output(extra)
+    img = ennf.convert(g)
+    p = tmp_path / "m.ennf"
+    p.write_bytes(img)
+    refs = list(ref_oracle.run_model(str(p), xv).values())
+    outs, steps = [], []
+    for flags in (0, lib.PLAN_NO_FUSE):
+        m = runtime.Model(img, flags=flags)
+        m.run(xv)
+        outs.append([m.output(0).ravel().copy(), m.output(1).ravel().copy()])
+        steps.append(m.plan_info()["steps"])
+        m.close()
+    for got, ref in zip(outs[0], refs):
+        assert rel_l2(got, ref) <= 2e-3, rel_l2(got, ref)
+    for a, c in zip(outs[0], outs[1]):
+        assert np.array_equal(a, c)
+    assert steps[0] < steps[1], steps
+
+
+@pytest.mark.parametrize("shape,perm", [((3, 5, 37, 70), (0, 1, 3, 2)), ((33, 65), (1, 0)), ((2, 4, 3, 6), (0, 2, 1, 3))])
+def test_transpose_matches_reference(cuda_lib, ref_oracle, tmp_path, shape, perm):
+    """Transpose as a graph node: a swap of the last two axes runs as tiled matrix transposes,
+    other permutations through the general kernel; both exact."""
+    g, b, x, xv = _builder(shape)
+    g.mark_output(b.transpose(x, perm))
+    out, ref = _run_both(ref_oracle, tmp_path, g, xv)
+    assert np.array_equal(out, ref)
