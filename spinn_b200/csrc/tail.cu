@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(temptyR);
       ++tcnt;
     }
-    if (lane == 0) tma_store_wait0();
+    if (lane == 0) tma_store_wait_read0();  // global writes complete with the grid
     __syncwarp();
   }
 

@@ -48,6 +48,7 @@ constexpr int kBM = 128;       // tile rows (output pixels) = TMEM lanes
 constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s per wait; a stage takes microseconds
 constexpr uint64_t kDrainNs = 200000000ull;
 constexpr int kSmemBudget = 232448 - 2048;      // 227 KiB opt-in minus barriers and alignment slack
+constexpr int kWPrefetchKb = 8;                 // W k-blocks of the first unit warmed in L2 before the wait
 
 enum AMode { kIm2col = 0, kTiled = 1 };
 
@@ -259,6 +260,19 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
       tmem_alloc(tmem_slot, C::TMEM_COLS);
       tmem_relinquish();
     }
+  }
+  // The weights do not depend on the previous kernel: warm L2 with this CTA's first W boxes
+  // while that kernel finishes, so the first stages after the wait below hit L2.
+  if (warp == (C::SPLIT_LOAD ? 3 : 0) && lane == 0 && unit0 < p.num_units) {
+    const int z = unit0 / p.num_tiles, t = unit0 - z * p.num_tiles;
+    const int tile = p.reverse ? p.num_tiles - 1 - t : t;
+    const int tn = tile % p.tiles_n;
+    const int ks = p.batch > 1 ? 0 : z, bzb = p.b_batched ? z : 0;
+    const int kb0 = ks * p.kb_per, kb1 = min(p.num_kb, kb0 + min(p.kb_per, kWPrefetchKb));
+    for (int kb = kb0; kb < kb1; ++kb)
+#pragma unroll
+      for (int j = 0; j < C::NSUB; ++j)
+        tma_prefetch_3d(&mapB, kb * BK + j * CB, tn * BN + (int)rank * C::BNC, bzb);
   }
   tc_fence_before();
   __syncthreads();
@@ -640,7 +654,9 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
           mbar_arrive(&tempty[b]);
       }
     }
-    if (lane == 0) tma_store_wait0();
+    // the stores' shared-memory reads are done before the CTA may exit; their global writes
+    // complete with the grid, which is what a dependent launch waits for
+    if (lane == 0) tma_store_wait_read0();
     __syncwarp();
   }
 
