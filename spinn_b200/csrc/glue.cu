@@ -405,6 +405,28 @@ __global__ void binary_kernel(const float* __restrict__ a, long na, const float*
   }
 }
 
+// Same-shape operands (no broadcast), 16-byte aligned, n a multiple of 4: four elements per
+// thread with 16-byte accesses; the same arithmetic per element as binary_kernel.
+__global__ void binary4_kernel(const float4* __restrict__ a, const float4* __restrict__ b, float4* __restrict__ y,
+                               long n4, int op, int act) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const float4 u = a[i], v = b[i];
+    float r[4] = {u.x, u.y, u.z, u.w};
+    const float w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      switch (op) {
+        case ELT_MUL: r[k] = r[k] * w[k]; break;
+        case ELT_SUB: r[k] = r[k] - w[k]; break;
+        case ELT_DIV: r[k] = r[k] / w[k]; break;
+        default: r[k] = r[k] + w[k]; break;
+      }
+      if (act) r[k] = r[k] < 0.0f ? 0.0f : r[k];
+    }
+    y[i] = make_float4(r[0], r[1], r[2], r[3]);
+  }
+}
+
 __global__ void unary_kernel(const float* __restrict__ x, float* __restrict__ y, long n, int op) {
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const float v = x[i];
@@ -529,18 +551,20 @@ __global__ void __launch_bounds__(kDwThreads, DwTile<S>::MIN_CTAS) depthwise3x3_
   float4* buf = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(dw_raw) + 127) & ~uintptr_t(127));
   __shared__ __align__(8) uint64_t full[T::BUFS];
   __shared__ volatile int abort_flag;
-  const long units = (long)groups * n * tiles_y * tiles_x;
-  auto unit_coords = [&](long u, int* g, int* b, int* ty, int* tx) {
-    *tx = (int)(u % tiles_x);
-    long r = u / tiles_x;
-    *ty = (int)(r % tiles_y);
+  // 32-bit unit arithmetic (the launcher keeps the unit count below 2^31): a 64-bit division
+  // costs ~100 instructions, and every thread decodes its unit
+  const int units = groups * n * tiles_y * tiles_x;
+  auto unit_coords = [&](int u, int* g, int* b, int* ty, int* tx) {
+    *tx = u % tiles_x;
+    int r = u / tiles_x;
+    *ty = r % tiles_y;
     r /= tiles_y;
-    *b = (int)(r % n);
-    *g = (int)(r / n);
+    *b = r % n;
+    *g = r / n;
   };
   // thread 0's record of loads in flight: bit s set while buffer s awaits the phase in bit s of armed_ph
   uint32_t armed = 0, armed_ph = 0;
-  auto issue = [&](long u, int it) {  // unit u is the CTA's it-th: buffer it % BUFS, phase (it / BUFS) & 1
+  auto issue = [&](int u, int it) {  // unit u is the CTA's it-th: buffer it % BUFS, phase (it / BUFS) & 1
     int g, b, ty, tx;
     unit_coords(u, &g, &b, &ty, &tx);
     const int slot = it % T::BUFS;
@@ -559,7 +583,7 @@ __global__ void __launch_bounds__(kDwThreads, DwTile<S>::MIN_CTAS) depthwise3x3_
   if (threadIdx.x == 0) {
     prefetch_tmap(&mx);
     for (int k = 0; k < T::BUFS - 1; ++k)
-      if ((long)blockIdx.x + (long)k * gridDim.x < units) issue(blockIdx.x + (long)k * gridDim.x, k);
+      if ((long)blockIdx.x + (long)k * gridDim.x < units) issue((int)(blockIdx.x + k * gridDim.x), k);
   }
   const int q = threadIdx.x & 7, blk = threadIdx.x >> 3;
   const int by = blk / T::BX, bx = blk - by * T::BX;  // block origin: output row RB*by, column CB*bx of the tile
@@ -567,11 +591,11 @@ __global__ void __launch_bounds__(kDwThreads, DwTile<S>::MIN_CTAS) depthwise3x3_
   int wg = -1;  // channel quad whose weights are in registers
   float4 k[9];
   int it = 0;
-  for (long u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
     const int cur = it % T::BUFS;
-    const long nu = u + (long)(T::BUFS - 1) * gridDim.x;
+    const long nu = (long)u + (long)(T::BUFS - 1) * gridDim.x;
     // the buffer of unit it + BUFS - 1 held unit it - 1, released by the last iteration's barrier
-    if (threadIdx.x == 0 && nu < units) issue(nu, it + T::BUFS - 1);
+    if (threadIdx.x == 0 && nu < units) issue((int)nu, it + T::BUFS - 1);
     bool ok = mbar_wait(&full[cur], (uint32_t)((it / T::BUFS) & 1), &abort_flag, 4000000000ull);
     if (!__syncthreads_and(ok)) break;
     if (threadIdx.x == 0) armed &= ~(1u << cur);
@@ -981,6 +1005,13 @@ int launch_gap_nhwc(const float* x, float* y, int n, int hw, int cpad, cudaStrea
 
 int launch_binary(const float* a, long na, const float* b, long nb, float* y, long n, int op, int act, cudaStream_t s) {
   SPINN_CHECK_ARG(na > 0 && nb > 0, "binary: empty operand");
+  if (na == n && nb == n && n % 4 == 0 &&
+      ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
+    binary4_kernel<<<grid_for(n / 4, kEltThreads), kEltThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(y), n / 4, op,
+        act);
+    SPINN_LAUNCH_CHECK();
+  }
   binary_kernel<<<grid_for(n, kEltThreads), kEltThreads, 0, s>>>(a, na, b, nb, y, n, op, act);
   SPINN_LAUNCH_CHECK();
 }
@@ -1007,6 +1038,7 @@ int launch_depthwise3x3_tma(const float* x, const float* w, const float* bias, c
   const int tiles_x = (ow + T::TW - 1) / T::TW, tiles_y = (oh + T::TH - 1) / T::TH;
   const int groups = (cpad / 4 + 7) / 8;
   const long units = (long)groups * n * tiles_y * tiles_x;
+  SPINN_CHECK_ARG(units < (1l << 31) - 2l * 148 * 8 * T::BUFS, "depthwise: %ld work units", units);
   const int smem = (int)(T::BUFS * T::BYTES + 128);
   static std::atomic<uint64_t> configured{0};
   const uint64_t bit = 1ull << (dev & 63);

@@ -1760,7 +1760,19 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
                 rc = launch_transpose(b->ptr, bt->ptr, (int)batch_b, K, N, st);  // -> [batch_b][N][K]
                 if (rc) return rc;
               }
-              SPINN_CUDA_TRY(cudaMemsetAsync(bp->ptr, 0, bp->bytes, st));
+              // zeros where the packing writes nothing: with seg == K only the K padding past
+              // the three segments and the rows past N (a full clear would write the whole,
+              // three times widened B once more)
+              if (seg != K) {
+                SPINN_CUDA_TRY(cudaMemsetAsync(bp->ptr, 0, bp->bytes, st));
+              } else {
+                if (kpad > 3 * seg)
+                  SPINN_CUDA_TRY(cudaMemset2DAsync(bp->ptr + 3 * seg, (size_t)kpad * 4, 0, (size_t)(kpad - 3 * seg) * 4,
+                                                   (size_t)batch_b * Np, st));
+                if (Np > N)
+                  SPINN_CUDA_TRY(cudaMemset2DAsync(bp->ptr + (size_t)N * kpad, (size_t)Np * kpad * 4, 0,
+                                                   (size_t)(Np - N) * kpad * 4, (size_t)batch_b, st));
+              }
               if (Np == N) {  // the planes are contiguous rows: one packing pass
                 rc = launch_split_tf32(bt->ptr, bp->ptr, batch_b * N, K, K, seg, kpad, 0, 0, 1, st);
                 if (rc) return rc;
