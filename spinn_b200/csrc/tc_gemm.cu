@@ -48,7 +48,7 @@ constexpr int kBM = 128;       // tile rows (output pixels) = TMEM lanes
 constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s per wait; a stage takes microseconds
 constexpr uint64_t kDrainNs = 200000000ull;
 constexpr int kSmemBudget = 232448 - 2048;      // 227 KiB opt-in minus barriers and alignment slack
-constexpr int kWPrefetchKb = 8;                 // W k-blocks of the first unit warmed in L2 before the wait
+constexpr int kWPrefetchKb = 1;                 // W k-blocks of the first unit warmed in L2 before the wait
 
 enum AMode { kIm2col = 0, kTiled = 1 };
 
@@ -261,9 +261,12 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
       tmem_relinquish();
     }
   }
-  // The weights do not depend on the previous kernel: warm L2 with this CTA's first W boxes
-  // while that kernel finishes, so the first stages after the wait below hit L2.
-  if (warp == (C::SPLIT_LOAD ? 3 : 0) && lane == 0 && unit0 < p.num_units) {
+  // The weights do not depend on the previous kernel: warm L2 with the W boxes of this CTA's
+  // first stage while that kernel finishes, so the first stage after the wait below hits L2.
+  // (One stage only: prefetches occupy the SM's copy engine ahead of the loads that follow,
+  // and eight stages' worth slowed the narrow YOLO-shaped layers by ~10%.  Resident weights
+  // are loaded whole right after the wait anyway.)
+  if (!WR && warp == (C::SPLIT_LOAD ? 3 : 0) && lane == 0 && unit0 < p.num_units) {
     const int z = unit0 / p.num_tiles, t = unit0 - z * p.num_tiles;
     const int tile = p.reverse ? p.num_tiles - 1 - t : t;
     const int tn = tile % p.tiles_n;
