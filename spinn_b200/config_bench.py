@@ -141,6 +141,7 @@ def tail(a) -> int:
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="cfg0,cfg1,cfg2,cfg4")
+    ap.add_argument("--cfg4-batches", default="1,32", help="batches of the cfg4 cases")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--layer", action="store_true", help="time one convolution layer (shape below)")
@@ -188,7 +189,7 @@ def main(argv=None):
             _case(f"cfg2 resnet50 batch {batch}", g, netdef.resnet_input(batch, seed=2), a.iters, a.warmup,
                   per_item=batch)
     if "cfg4" in which:
-        for batch in (1, 32):
+        for batch in [int(b) for b in a.cfg4_batches.split(",")]:
             g = netdef.yolo_shaped(batch=batch, image=640)
             _case(f"cfg4 yolo-shaped 640 batch {batch}", g, netdef.yolo_input(batch, 640), a.iters, a.warmup,
                   per_item=batch)
