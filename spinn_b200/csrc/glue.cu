@@ -723,7 +723,7 @@ __global__ void grouped_kernel(const float* __restrict__ x, const float* __restr
   }
 }
 
-template <typename Idx>
+template <typename Idx, bool W32>
 __global__ void resize_nearest_kernel(const float4* __restrict__ x, float4* __restrict__ y, int n, int h, int w,
                                       int c4, int oh, int ow) {
   const Idx total = (Idx)n * oh * ow * c4;
@@ -734,7 +734,10 @@ __global__ void resize_nearest_kernel(const float4* __restrict__ x, float4* __re
     t /= ow;
     const int oy = (int)(t % oh);
     const int b = (int)(t / oh);
-    const int iy = (int)((long)oy * h / oh), ix = (int)((long)ox * w / ow);
+    // 32-bit products when they fit (the launcher checks): a 64-bit division per element would
+    // dominate this copy
+    const int iy = W32 ? (int)((unsigned)oy * (unsigned)h / (unsigned)oh) : (int)((long)oy * h / oh);
+    const int ix = W32 ? (int)((unsigned)ox * (unsigned)w / (unsigned)ow) : (int)((long)ox * w / ow);
     y[i] = x[(((size_t)b * h + iy) * w + ix) * c4 + cq];
   }
 }
@@ -793,15 +796,16 @@ __global__ void transpose_kernel(const float* __restrict__ x, float* __restrict_
   }
 }
 
-__global__ void split_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst, long rows, int cols,
+template <typename Idx>
+__global__ void split_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst, Idx rows, int cols,
                                   int src_ld, int seg, int dst_ld, int o0, int o1, int o2) {
-  const long total = rows * cols;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / cols;
+  const Idx total = rows * cols;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
+    const Idx r = i / cols;  // Idx = int when the element count fits: no 64-bit division per element
     const int c = (int)(i - r * cols);
-    const float v = src[r * src_ld + c];
+    const float v = src[(size_t)r * src_ld + c];
     const float hi = to_tf32_rna(v), lo = to_tf32_rna(v - hi);
-    float* d = dst + r * (long)dst_ld + c;
+    float* d = dst + (size_t)r * dst_ld + c;
     d[0] = o0 ? lo : hi;
     d[seg] = o1 ? lo : hi;
     d[2 * (long)seg] = o2 ? lo : hi;
@@ -1101,12 +1105,21 @@ int launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, in
   SPINN_CHECK_ARG(cpad % 4 == 0, "resize: channel stride %d not a multiple of 4", cpad);
   const long work = (long)n * oh * ow * (cpad / 4);
   const long span = (long)grid_for(work, kEltThreads) * kEltThreads;  // the loop index reaches work + span
-  if (work < (1l << 31) - span)
-    resize_nearest_kernel<int><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
-        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow);
-  else
-    resize_nearest_kernel<long><<<grid_for(work, kEltThreads), kEltThreads, 0, s>>>(
-        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n, h, w, cpad / 4, oh, ow);
+  const bool w32 = (long)oh * h < (1l << 32) && (long)ow * w < (1l << 32);
+  const float4* xv = reinterpret_cast<const float4*>(x);
+  float4* yv = reinterpret_cast<float4*>(y);
+  const int g = grid_for(work, kEltThreads), c4 = cpad / 4;
+  if (work < (1l << 31) - span) {
+    if (w32)
+      resize_nearest_kernel<int, true><<<g, kEltThreads, 0, s>>>(xv, yv, n, h, w, c4, oh, ow);
+    else
+      resize_nearest_kernel<int, false><<<g, kEltThreads, 0, s>>>(xv, yv, n, h, w, c4, oh, ow);
+  } else {
+    if (w32)
+      resize_nearest_kernel<long, true><<<g, kEltThreads, 0, s>>>(xv, yv, n, h, w, c4, oh, ow);
+    else
+      resize_nearest_kernel<long, false><<<g, kEltThreads, 0, s>>>(xv, yv, n, h, w, c4, oh, ow);
+  }
   SPINN_LAUNCH_CHECK();
 }
 
@@ -1143,8 +1156,12 @@ int launch_transpose(const float* x, float* y, int batch, int rows, int cols, cu
 int launch_split_tf32(const float* src, float* dst, long rows, int cols, int src_ld, int seg, int dst_ld, int o0,
                       int o1, int o2, cudaStream_t s) {
   SPINN_CHECK_ARG(seg >= cols && src_ld >= cols && dst_ld >= 3 * seg, "split_tf32: bad strides");
-  split_tf32_kernel<<<grid_for(rows * cols, kEltThreads), kEltThreads, 0, s>>>(src, dst, rows, cols, src_ld, seg,
-                                                                               dst_ld, o0, o1, o2);
+  const long work = rows * cols;
+  const int g = grid_for(work, kEltThreads);
+  if (work < (1l << 31) - (long)g * kEltThreads)
+    split_tf32_kernel<int><<<g, kEltThreads, 0, s>>>(src, dst, (int)rows, cols, src_ld, seg, dst_ld, o0, o1, o2);
+  else
+    split_tf32_kernel<long><<<g, kEltThreads, 0, s>>>(src, dst, rows, cols, src_ld, seg, dst_ld, o0, o1, o2);
   SPINN_LAUNCH_CHECK();
 }
 
