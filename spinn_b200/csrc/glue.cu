@@ -295,48 +295,59 @@ __global__ void split_rows_kernel(SplitParts parts, const float* __restrict__ sr
   }
 }
 
-// Last-axis Concat gathered from pieces (launch_gather_rows): one 32 x 32 tile (channels x
-// positions of one image of one piece) per block iteration, staged in shared memory so that
-// both the read (along channels for NHWC pieces, along positions for row pieces) and the
-// write (along positions) are coalesced.  tile0[k] is the first tile of piece k.
+// Last-axis Concat gathered from pieces (launch_gather_rows): one tile of 32 channels x 128
+// positions of one image of one piece per block iteration, staged in shared memory so that
+// both the read (along channels for NHWC pieces, along positions for row pieces) and the write
+// (along positions) are coalesced; every thread has 16 loads in flight per tile.  Tiles run
+// channel tile fastest, so blocks working at the same time read all channel slices of the same
+// pixels.  tile0[k] is the first tile of piece k.
+constexpr int kGatherTL = 128;  // positions per tile
 struct GatherTiles {
   long tile0[kGatherMaxPieces + 1];
   int ctiles[kGatherMaxPieces], ltiles[kGatherMaxPieces];
 };
 __global__ void __launch_bounds__(256) gather_rows_kernel(GatherPieces g, GatherTiles t, float* __restrict__ dst,
                                                           int n, int ctot, int ltot) {
-  __shared__ float tile[32][33];
+  __shared__ float tile[32][kGatherTL + 1];
   const long total = t.tile0[g.n];
   for (long u = blockIdx.x; u < total; u += gridDim.x) {
     int k = 0;
     while (k + 1 < g.n && u >= t.tile0[k + 1]) ++k;
-    const long local = u - t.tile0[k];
-    const long per_img = (long)t.ctiles[k] * t.ltiles[k];
-    const int b = (int)(local / per_img);
-    const int r = (int)(local - (long)b * per_img);
-    const int cb = (r / t.ltiles[k]) * 32, lb = (r % t.ltiles[k]) * 32;
+    const int local = (int)(u - t.tile0[k]);
+    const int per_img = t.ctiles[k] * t.ltiles[k];
+    const int b = local / per_img;
+    const int r = local - b * per_img;
+    const int cb = (r % t.ctiles[k]) * 32, lb = (r / t.ctiles[k]) * kGatherTL;
     const int chans = g.chans[k], len = g.len[k], ld = g.ld[k];
     if (g.nhwc[k]) {
       // src[b][l][c0 + c]: lanes along channels
       const float* s = g.src[k] + (size_t)b * len * ld + g.c0[k];
-      for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int l = lb + i, c = cb + threadIdx.x;
+      const int c = cb + threadIdx.x;
+#pragma unroll
+      for (int i = threadIdx.y; i < kGatherTL; i += 8) {
+        const int l = lb + i;
         tile[threadIdx.x][i] = (l < len && c < chans) ? __ldg(s + (size_t)l * ld + c) : 0.0f;
       }
     } else {
       // src[b][c][l]: lanes along positions
       const float* s = g.src[k] + (size_t)b * chans * ld;
-      for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int c = cb + i, l = lb + threadIdx.x;
-        tile[i][threadIdx.x] = (l < len && c < chans) ? __ldg(s + (size_t)c * ld + l) : 0.0f;
-      }
+#pragma unroll
+      for (int i = threadIdx.y; i < 32; i += 8)
+#pragma unroll
+        for (int q = 0; q < kGatherTL / 32; ++q) {
+          const int c = cb + i, l = lb + q * 32 + threadIdx.x;
+          tile[i][q * 32 + threadIdx.x] = (l < len && c < chans) ? __ldg(s + (size_t)c * ld + l) : 0.0f;
+        }
     }
     __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-      const int c = cb + i, l = lb + threadIdx.x;
-      if (c < chans && l < len)
-        dst[((size_t)b * ctot + g.dst_c[k] + c) * ltot + g.dst_l[k] + l] = tile[i][threadIdx.x];
-    }
+#pragma unroll
+    for (int i = threadIdx.y; i < 32; i += 8)
+#pragma unroll
+      for (int q = 0; q < kGatherTL / 32; ++q) {
+        const int c = cb + i, l = lb + q * 32 + threadIdx.x;
+        if (c < chans && l < len)
+          dst[((size_t)b * ctot + g.dst_c[k] + c) * ltot + g.dst_l[k] + l] = tile[i][q * 32 + threadIdx.x];
+      }
     __syncthreads();  // the tile is reused by the next iteration
   }
 }
@@ -521,7 +532,7 @@ __global__ void depthwise_kernel(const float4* __restrict__ x, const float4* __r
 // pixels (2 x 2 at stride 1, 2 x 1 at stride 2), reading each window pixel of the block once
 // from shared memory, with the taps accumulated in the order r, then s for every output; the
 // epilogue is depthwise_kernel's (bias, residual, activation, tf32 rounding).  The 9 weights
-// of the CTA's channel group stay in registers while consecutive units share it.
+// of a channel group stay in registers while the CTA's consecutive units share it.
 // w is [9][cpad], bias [cpad], residual NHWC like y.  Waits are bounded; on expiry the CTA
 // raises *err (code 4) and stops.
 constexpr int kDwThreads = 256;
@@ -554,13 +565,15 @@ __global__ void __launch_bounds__(kDwThreads, DwTile<S>::MIN_CTAS) depthwise3x3_
   // 32-bit unit arithmetic (the launcher keeps the unit count below 2^31): a 64-bit division
   // costs ~100 instructions, and every thread decodes its unit
   const int units = groups * n * tiles_y * tiles_x;
+  // channel group fastest: CTAs working at the same time read every 128-B channel slice of
+  // the same pixels, so DRAM sees whole pixel rows (c x 4 bytes) instead of one slice of each
   auto unit_coords = [&](int u, int* g, int* b, int* ty, int* tx) {
-    *tx = u % tiles_x;
-    int r = u / tiles_x;
+    *g = u % groups;
+    int r = u / groups;
+    *tx = r % tiles_x;
+    r /= tiles_x;
     *ty = r % tiles_y;
-    r /= tiles_y;
-    *b = r % n;
-    *g = r / n;
+    *b = r / tiles_y;
   };
   // thread 0's record of loads in flight: bit s set while buffer s awaits the phase in bit s of armed_ph
   uint32_t armed = 0, armed_ph = 0;
@@ -781,6 +794,45 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
   }
 }
 
+// Softmax over contiguous rows of dim <= 32 * NPL (inner == 1): each lane keeps its NPL values
+// and their exponentials in registers, so the row is read once and expf runs once per element.
+// Same operations in the same order as softmax_kernel (lane-strided sums, then the shuffle
+// tree), so the results are identical.
+template <int NPL>
+__global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restrict__ y, long rows, int dim) {
+  const int lane = threadIdx.x & 31;
+  const long warp = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  for (long r = warp; r < rows; r += nwarps) {
+    const float* xr = x + r * dim;
+    float* yr = y + r * dim;
+    float v[NPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      const int j = lane + 32 * k;
+      v[k] = j < dim ? xr[j] : -INFINITY;
+      m = fmaxf(m, v[k]);
+    }
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      if (lane + 32 * k < dim) {
+        v[k] = expf(v[k] - m);
+        sum += v[k];
+      }
+    }
+    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      const int j = lane + 32 * k;
+      if (j < dim) yr[j] = v[k] * inv;
+    }
+  }
+}
+
 __global__ void transpose_kernel(const float* __restrict__ x, float* __restrict__ y, int rows, int cols) {
   __shared__ float tile[32][33];
   const size_t off = (size_t)blockIdx.z * rows * cols;
@@ -981,7 +1033,8 @@ int launch_gather_rows(const GatherPieces& g, float* dst, int n, int ctot, int l
                         (g.nhwc[k] ? g.c0[k] + g.chans[k] <= g.ld[k] : g.len[k] <= g.ld[k]),
                     "gather_rows: piece %d out of range", k);
     t.ctiles[k] = (g.chans[k] + 31) / 32;
-    t.ltiles[k] = (g.len[k] + 31) / 32;
+    t.ltiles[k] = (g.len[k] + kGatherTL - 1) / kGatherTL;
+    SPINN_CHECK_ARG((long)n * t.ctiles[k] * t.ltiles[k] < (1l << 31), "gather_rows: piece %d has too many tiles", k);
     t.tile0[k + 1] = t.tile0[k] + (long)n * t.ctiles[k] * t.ltiles[k];
   }
   const long total = t.tile0[g.n];
@@ -1143,6 +1196,10 @@ int launch_permute(const float* x, float* y, int ndim, const uint32_t* dims, con
 
 int launch_softmax(const float* x, float* y, long outer, int dim, long inner, cudaStream_t s) {
   const long rows = outer * inner;
+  if (inner == 1 && dim <= 32 * 16) {
+    softmax_rows_kernel<16><<<grid_for(rows * 32, kEltThreads), kEltThreads, 0, s>>>(x, y, rows, dim);
+    SPINN_LAUNCH_CHECK();
+  }
   softmax_kernel<<<grid_for(rows * 32, kEltThreads), kEltThreads, 0, s>>>(x, y, outer, dim, inner);
   SPINN_LAUNCH_CHECK();
 }
