@@ -298,9 +298,10 @@ __global__ void split_rows_kernel(SplitParts parts, const float* __restrict__ sr
 // Last-axis Concat gathered from pieces (launch_gather_rows): one tile of 32 channels x 128
 // positions of one image of one piece per block iteration, staged in shared memory so that
 // both the read (along channels for NHWC pieces, along positions for row pieces) and the write
-// (along positions) are coalesced; every thread has 16 loads in flight per tile.  Tiles run
-// channel tile fastest, so blocks working at the same time read all channel slices of the same
-// pixels.  tile0[k] is the first tile of piece k.
+// (along positions) are coalesced; every thread has 16 loads in flight per tile, and the next
+// tile's loads are issued before the current one is written.  Tiles run channel tile fastest,
+// so blocks working at the same time read all channel slices of the same pixels.  tile0[k] is
+// the first tile of piece k.
 constexpr int kGatherTL = 128;  // positions per tile
 struct GatherTiles {
   long tile0[kGatherMaxPieces + 1];
@@ -309,46 +310,76 @@ struct GatherTiles {
 __global__ void __launch_bounds__(256) gather_rows_kernel(GatherPieces g, GatherTiles t, float* __restrict__ dst,
                                                           int n, int ctot, int ltot) {
   __shared__ float tile[32][kGatherTL + 1];
+  constexpr int V = kGatherTL * 32 / 256;  // values per thread and tile
   const long total = t.tile0[g.n];
-  for (long u = blockIdx.x; u < total; u += gridDim.x) {
-    int k = 0;
-    while (k + 1 < g.n && u >= t.tile0[k + 1]) ++k;
-    const int local = (int)(u - t.tile0[k]);
-    const int per_img = t.ctiles[k] * t.ltiles[k];
-    const int b = local / per_img;
-    const int r = local - b * per_img;
-    const int cb = (r % t.ctiles[k]) * 32, lb = (r / t.ctiles[k]) * kGatherTL;
-    const int chans = g.chans[k], len = g.len[k], ld = g.ld[k];
-    if (g.nhwc[k]) {
-      // src[b][l][c0 + c]: lanes along channels
-      const float* s = g.src[k] + (size_t)b * len * ld + g.c0[k];
-      const int c = cb + threadIdx.x;
+  struct Coord {
+    int k, b, cb, lb;
+  };
+  auto coord = [&](long u) {
+    Coord c;
+    c.k = 0;
+    while (c.k + 1 < g.n && u >= t.tile0[c.k + 1]) ++c.k;
+    const int local = (int)(u - t.tile0[c.k]);
+    const int per_img = t.ctiles[c.k] * t.ltiles[c.k];
+    c.b = local / per_img;
+    const int r = local - c.b * per_img;
+    c.cb = (r % t.ctiles[c.k]) * 32;
+    c.lb = (r / t.ctiles[c.k]) * kGatherTL;
+    return c;
+  };
+  // value v of a thread: NHWC pieces row (position) ty + 8 v, lane = channel; row pieces
+  // channel ty + 8 (v / 4), position (v % 4) * 32 + lane
+  auto load = [&](const Coord& c, float (&r)[V]) {
+    const int chans = g.chans[c.k], len = g.len[c.k], ld = g.ld[c.k];
+    if (g.nhwc[c.k]) {
+      const float* s = g.src[c.k] + (size_t)c.b * len * ld + g.c0[c.k];
+      const int ch = c.cb + threadIdx.x;
 #pragma unroll
-      for (int i = threadIdx.y; i < kGatherTL; i += 8) {
-        const int l = lb + i;
-        tile[threadIdx.x][i] = (l < len && c < chans) ? __ldg(s + (size_t)l * ld + c) : 0.0f;
+      for (int v = 0; v < V; ++v) {
+        const int l = c.lb + threadIdx.y + 8 * v;
+        r[v] = (l < len && ch < chans) ? __ldg(s + (size_t)l * ld + ch) : 0.0f;
       }
     } else {
-      // src[b][c][l]: lanes along positions
-      const float* s = g.src[k] + (size_t)b * chans * ld;
+      const float* s = g.src[c.k] + (size_t)c.b * chans * ld;
 #pragma unroll
-      for (int i = threadIdx.y; i < 32; i += 8)
+      for (int v = 0; v < V; ++v) {
+        const int ch = c.cb + threadIdx.y + 8 * (v / 4), l = c.lb + (v % 4) * 32 + threadIdx.x;
+        r[v] = (l < len && ch < chans) ? __ldg(s + (size_t)ch * ld + l) : 0.0f;
+      }
+    }
+  };
+  float r[V];
+  long u = blockIdx.x;
+  Coord c{};
+  if (u < total) {
+    c = coord(u);
+    load(c, r);
+  }
+  for (; u < total; u += gridDim.x) {
+    if (g.nhwc[c.k]) {
 #pragma unroll
-        for (int q = 0; q < kGatherTL / 32; ++q) {
-          const int c = cb + i, l = lb + q * 32 + threadIdx.x;
-          tile[i][q * 32 + threadIdx.x] = (l < len && c < chans) ? __ldg(s + (size_t)c * ld + l) : 0.0f;
-        }
+      for (int v = 0; v < V; ++v) tile[threadIdx.x][threadIdx.y + 8 * v] = r[v];
+    } else {
+#pragma unroll
+      for (int v = 0; v < V; ++v) tile[threadIdx.y + 8 * (v / 4)][(v % 4) * 32 + threadIdx.x] = r[v];
     }
     __syncthreads();
+    const Coord cur = c;
+    const long nu = u + gridDim.x;
+    if (nu < total) {  // the next tile's loads are in flight while this one is written
+      c = coord(nu);
+      load(c, r);
+    }
+    const int chans = g.chans[cur.k], len = g.len[cur.k];
 #pragma unroll
     for (int i = threadIdx.y; i < 32; i += 8)
 #pragma unroll
       for (int q = 0; q < kGatherTL / 32; ++q) {
-        const int c = cb + i, l = lb + q * 32 + threadIdx.x;
-        if (c < chans && l < len)
-          dst[((size_t)b * ctot + g.dst_c[k] + c) * ltot + g.dst_l[k] + l] = tile[i][q * 32 + threadIdx.x];
+        const int ch = cur.cb + i, l = cur.lb + q * 32 + threadIdx.x;
+        if (ch < chans && l < len)
+          dst[((size_t)cur.b * ctot + g.dst_c[cur.k] + ch) * ltot + g.dst_l[cur.k] + l] = tile[i][q * 32 + threadIdx.x];
       }
-    __syncthreads();  // the tile is reused by the next iteration
+    __syncthreads();  // the tile is refilled by the next iteration
   }
 }
 
