@@ -312,51 +312,59 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherPieces g, Gather
   __shared__ float tile[32][kGatherTL + 1];
   constexpr int V = kGatherTL * 32 / 256;  // values per thread and tile
   const long total = t.tile0[g.n];
-  struct Coord {
-    int k, b, cb, lb;
+  // One tile's parameters, read from the (dynamically indexed) piece table once per tile; the
+  // element loops then index with 32-bit offsets from per-tile base pointers (the launcher
+  // bounds one image of a piece and one destination row block below 2^31 elements).
+  struct Tile {
+    const float* src;  // first element this thread's lane column / row reads
+    float* dst;        // destination element (channel cb, position lb) of the tile
+    int nhwc, ld, cl, ll;  // channels / positions of the tile still inside the piece
   };
-  auto coord = [&](long u) {
-    Coord c;
-    c.k = 0;
-    while (c.k + 1 < g.n && u >= t.tile0[c.k + 1]) ++c.k;
-    const int local = (int)(u - t.tile0[c.k]);
-    const int per_img = t.ctiles[c.k] * t.ltiles[c.k];
-    c.b = local / per_img;
-    const int r = local - c.b * per_img;
-    c.cb = (r % t.ctiles[c.k]) * 32;
-    c.lb = (r / t.ctiles[c.k]) * kGatherTL;
-    return c;
+  auto tile_of = [&](long u) {
+    int k = 0;
+    while (k + 1 < g.n && u >= t.tile0[k + 1]) ++k;
+    const int local = (int)(u - t.tile0[k]);
+    const int per_img = t.ctiles[k] * t.ltiles[k];
+    const int b = local / per_img;
+    const int r = local - b * per_img;
+    const int cb = (r % t.ctiles[k]) * 32, lb = (r / t.ctiles[k]) * kGatherTL;
+    Tile x;
+    x.nhwc = g.nhwc[k];
+    x.ld = g.ld[k];
+    x.cl = g.chans[k] - cb;
+    x.ll = g.len[k] - lb;
+    x.src = g.nhwc[k] ? g.src[k] + (size_t)b * g.len[k] * x.ld + (size_t)lb * x.ld + g.c0[k] + cb
+                      : g.src[k] + (size_t)b * g.chans[k] * x.ld + (size_t)cb * x.ld + lb;
+    x.dst = dst + ((size_t)b * ctot + g.dst_c[k] + cb) * ltot + g.dst_l[k] + lb;
+    return x;
   };
-  // value v of a thread: NHWC pieces row (position) ty + 8 v, lane = channel; row pieces
-  // channel ty + 8 (v / 4), position (v % 4) * 32 + lane
-  auto load = [&](const Coord& c, float (&r)[V]) {
-    const int chans = g.chans[c.k], len = g.len[c.k], ld = g.ld[c.k];
-    if (g.nhwc[c.k]) {
-      const float* s = g.src[c.k] + (size_t)c.b * len * ld + g.c0[c.k];
-      const int ch = c.cb + threadIdx.x;
+  // value v of a thread: NHWC pieces position ty + 8 v, lane = channel; row pieces channel
+  // ty + 8 (v / 4), position (v % 4) * 32 + lane
+  auto load = [&](const Tile& x, float (&r)[V]) {
+    if (x.nhwc) {
+      const bool cin = (int)threadIdx.x < x.cl;
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        const int l = c.lb + threadIdx.y + 8 * v;
-        r[v] = (l < len && ch < chans) ? __ldg(s + (size_t)l * ld + ch) : 0.0f;
+        const int l = threadIdx.y + 8 * v;
+        r[v] = (cin && l < x.ll) ? __ldg(x.src + l * x.ld + threadIdx.x) : 0.0f;
       }
     } else {
-      const float* s = g.src[c.k] + (size_t)c.b * chans * ld;
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        const int ch = c.cb + threadIdx.y + 8 * (v / 4), l = c.lb + (v % 4) * 32 + threadIdx.x;
-        r[v] = (l < len && ch < chans) ? __ldg(s + (size_t)ch * ld + l) : 0.0f;
+        const int c = threadIdx.y + 8 * (v / 4), l = (v % 4) * 32 + threadIdx.x;
+        r[v] = (c < x.cl && l < x.ll) ? __ldg(x.src + c * x.ld + l) : 0.0f;
       }
     }
   };
   float r[V];
   long u = blockIdx.x;
-  Coord c{};
+  Tile cur{};
   if (u < total) {
-    c = coord(u);
-    load(c, r);
+    cur = tile_of(u);
+    load(cur, r);
   }
   for (; u < total; u += gridDim.x) {
-    if (g.nhwc[c.k]) {
+    if (cur.nhwc) {
 #pragma unroll
       for (int v = 0; v < V; ++v) tile[threadIdx.x][threadIdx.y + 8 * v] = r[v];
     } else {
@@ -364,20 +372,18 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherPieces g, Gather
       for (int v = 0; v < V; ++v) tile[threadIdx.y + 8 * (v / 4)][(v % 4) * 32 + threadIdx.x] = r[v];
     }
     __syncthreads();
-    const Coord cur = c;
+    const Tile w = cur;
     const long nu = u + gridDim.x;
     if (nu < total) {  // the next tile's loads are in flight while this one is written
-      c = coord(nu);
-      load(c, r);
+      cur = tile_of(nu);
+      load(cur, r);
     }
-    const int chans = g.chans[cur.k], len = g.len[cur.k];
 #pragma unroll
     for (int i = threadIdx.y; i < 32; i += 8)
 #pragma unroll
       for (int q = 0; q < kGatherTL / 32; ++q) {
-        const int ch = cur.cb + i, l = cur.lb + q * 32 + threadIdx.x;
-        if (ch < chans && l < len)
-          dst[((size_t)cur.b * ctot + g.dst_c[cur.k] + ch) * ltot + g.dst_l[cur.k] + l] = tile[i][q * 32 + threadIdx.x];
+        const int l = q * 32 + threadIdx.x;
+        if (i < w.cl && l < w.ll) w.dst[i * ltot + l] = tile[i][l];
       }
     __syncthreads();  // the tile is refilled by the next iteration
   }
@@ -1065,7 +1071,9 @@ int launch_gather_rows(const GatherPieces& g, float* dst, int n, int ctot, int l
                     "gather_rows: piece %d out of range", k);
     t.ctiles[k] = (g.chans[k] + 31) / 32;
     t.ltiles[k] = (g.len[k] + kGatherTL - 1) / kGatherTL;
-    SPINN_CHECK_ARG((long)n * t.ctiles[k] * t.ltiles[k] < (1l << 31), "gather_rows: piece %d has too many tiles", k);
+    SPINN_CHECK_ARG((long)n * t.ctiles[k] * t.ltiles[k] < (1l << 31) &&
+                        (long)(g.nhwc[k] ? g.len[k] : g.chans[k]) * g.ld[k] < (1l << 31) && 32l * ltot < (1l << 31),
+                    "gather_rows: piece %d too large for 32-bit offsets", k);
     t.tile0[k + 1] = t.tile0[k] + (long)n * t.ctiles[k] * t.ltiles[k];
   }
   const long total = t.tile0[g.n];
