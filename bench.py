@@ -20,7 +20,8 @@ forward pass of every rank's shard.  Rank 0 prints one JSON line:
             taken from profiled replays (CUDA events between the graph's kernels; each
             kernel's minimum over PROFILE_REPLAYS replays).  The peak is the dense tf32
             tensor rate, 2048 MAC per cycle per SM (one 128x256x8 kind::tf32 MMA every 128
-            cycles) x 2 FLOP x SMs x the median SM clock sampled during the timed region;
+            cycles) x 2 FLOP x SMs x the median SM clock sampled from the warm-up through the
+            timed region;
             `frac_of_measured_burst` divides by half the measured bf16 cuBLAS burst instead.
             `layer_roofline` adds the per-layer view of the same times: every convolution's
             floor is max(FLOPs / tf32 peak, algorithmic bytes / copy bandwidth), and `frac`
@@ -123,7 +124,7 @@ def physical_gpu(local: int) -> str:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons of one GPU, sampled every 100 ms while running."""
+    """nvidia-smi clocks / throttle reasons of one GPU, sampled every 50 ms while running."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -136,13 +137,25 @@ class ClockSampler:
 
     def command(self):
         return ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                "-lms", "100"]
+                "-lms", "50"]
 
     def start(self):
         try:
             self.p = subprocess.Popen(self.command(), stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
+
+    def wait_first(self, seconds: float) -> None:
+        """Returns once the first sample is written (nvidia-smi takes a moment to start), so
+        that a short timed region is sampled too; gives up after `seconds`."""
+        t0 = time.time()
+        while self.p is not None and time.time() - t0 < seconds:
+            try:
+                if os.path.getsize(self.f.name) > 0:
+                    return
+            except OSError:
+                return
+            time.sleep(0.02)
 
     def stop(self):
         if self.p is None:
@@ -171,9 +184,9 @@ class ClockSampler:
 
 
 def tf32_peak_tflops(sms: int, clocks) -> tuple:
-    """Dense tf32 tensor peak (TFLOP/s) at the median SM clock sampled during the timed region
-    (the maximum clock when no sample was taken), and a description of it."""
-    mhz, how = None, "median SM clock sampled during the timed region"
+    """Dense tf32 tensor peak (TFLOP/s) at the median SM clock sampled under load (warm-up and
+    timed region; the maximum clock when no sample was taken), and a description of it."""
+    mhz, how = None, "median SM clock sampled during the warm-up and the timed region"
     if clocks and clocks.get("sm_mhz"):
         mhz = float(clocks["sm_mhz"])
     elif clocks and clocks.get("sm_max_mhz"):
@@ -387,14 +400,17 @@ def main():
         torch.cuda.synchronize()
 
     sid = stream.cuda_stream
+    # clocks are sampled from the warm-up through the timed region (both under load), so that
+    # a timed region shorter than the sampling interval still has samples
+    sampler = ClockSampler(physical_gpu(local)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        sampler.wait_first(3.0)
     for _ in range(args.warmup):
         model.run_device(sid)
         flush.zero_()
     barrier()
 
-    sampler = ClockSampler(physical_gpu(local)) if rank == 0 else None
-    if sampler:
-        sampler.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()
