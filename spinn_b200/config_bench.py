@@ -86,7 +86,8 @@ def layer(a) -> int:
         model.run_profiled(stream.cuda_stream)
         cur = model.profile()
         prof = cur if prof is None else [(o, min(t, pt), f) for (o, t, f), (_, pt, _) in zip(cur, prof)]
-    conv_ms = sum(t for (o, t, f), k in zip(prof, model.step_kinds()) if o == ennf.OP["Conv"])
+    conv_steps = [t for (o, t, f), k in zip(prof, model.step_kinds()) if o == ennf.OP["Conv"]]
+    conv_ms = sum(conv_steps)
     oc = a.c if a.residual else a.oc
     oh = a.hw if a.projection else (a.hw + 2 * pad - a.k) // a.stride + 1
     cin = a.c // a.group
@@ -98,7 +99,8 @@ def layer(a) -> int:
                   + a.batch * oh * oh * oc * ((3 if a.projection else 2) if res else 1)
                   + oc * cin * (a.k * a.k + (1 if a.projection else 0)))
     print(json.dumps({"layer": {k: v for k, v in vars(a).items() if k != "only"}, "ms_per_run": ms,
-                      "conv_ms": conv_ms, "tflops": flops / conv_ms / 1e9, "gbs": byts / conv_ms / 1e6,
+                      "conv_ms": conv_ms, "conv_steps_ms": conv_steps,
+                      "tflops": flops / conv_ms / 1e9, "gbs": byts / conv_ms / 1e6,
                       "algorithmic_mb": byts / 1e6, "steps": model.plan_info()["steps"],
                       "kinds": model.step_kinds()}), flush=True)
     model.close()
