@@ -925,7 +925,7 @@ void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms, int* wr) {
 // floats at 8 TB/s (the partials are L2-resident).  64-deep stages and sub-tiles need channel
 // blocks of 16 or 32 and no fused residual (the residual ring would leave too few stages).
 TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t ws_limit, int force_bn,
-                    bool allow_wr) {
+                    bool allow_wr, int taps) {
   int fbn, fks, fpair, fbk, fms, fwr;
   forced_tiles(&fbn, &fks, &fpair, &fbk, &fms, &fwr);
   if (force_bn <= 0 && (fbn == 64 || fbn == 128 || fbn == 256)) force_bn = fbn;
@@ -942,6 +942,11 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
                             {128, 1, 32, 2, 0, 0.46},  {64, 1, 32, 2, 0, 0.38},   {128, 1, 64, 2, 0, 0.86},
                             {64, 1, 64, 2, 0, 0.67}};
   const size_t ldw = (size_t)((N + 3) & ~3);
+  // Multi-tap im2col problems (3x3 and larger filters) load A one tap box per channel block;
+  // for 128-row single-CTA tiles with 64-deep stages that costs ~1.3x the stage time of the
+  // fit (forced-tile sweep of ResNet-101's 3x3 layers at batch 256: 0.57-0.60 us per stage
+  // against 0.405), while the pair and two-sub-tile shapes matched it.
+  const double im2col_single64 = taps > 1 ? 1.3 : 1.0;
   TilePlan best;
   double best_cost = 1e300;
   for (const Shape& sh : shapes) {
@@ -961,6 +966,7 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
     if (sh.ms == 2 && ((cb != 32 && cb != 16) || (has_res && (sh.bk != 32 || fms != 2)))) continue;
     if (force_bn <= 0 && sh.pair == 1 && bn > 64 && bn >= 2 * ((N + 63) / 64) * 64) continue;  // far wider than N
     const int slots = sh.pair == 2 ? sms / 2 : sms;
+    const double per_stage = sh.per_stage * (sh.pair == 1 && sh.ms == 1 && sh.bk == 64 ? im2col_single64 : 1.0);
     const int num_kb = (K + sh.bk - 1) / sh.bk;
     const int tm = kBM * sh.pair * sh.ms;
     const long tiles = (long)((M + tm - 1) / tm) * ((N + bn - 1) / bn);
@@ -977,7 +983,7 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
       // epilogue: ~0.8 us per 32-column chunk and warp group; 256-wide residual tiles use one
       // group; with two M sub-tiles each group drains a whole sub-tile
       const double epi = sh.ms == 2 ? 0.8 * (bn / 32) : 0.8 * (bn / 32) / ((has_res && bn == 256) ? 1 : 2);
-      double cost = 14.0 + (waves - 1) * 2.0 + waves * std::max(kb_per * sh.per_stage, epi);
+      double cost = 14.0 + (waves - 1) * 2.0 + waves * std::max(kb_per * per_stage, epi);
       if (ks > 1) cost += (double)(ks + 2) * M * N * 4 / 8.0e6;
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
@@ -1014,7 +1020,8 @@ size_t tc_gemm_workspace_bytes(const TcGemmArgs& a) {
   if (!tc_gemm_supported(a, nullptr) || a.batch > 1) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  return plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), kWsCap, a.bn, true)
+  return plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), kWsCap, a.bn, true,
+                    a.a_mode == 0 ? a.kh * a.kw : 1)
       .ws_bytes;
 }
 
@@ -1081,7 +1088,8 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     return SPINN_CUDA_EINVAL;
   }
   const size_t ws_limit = (a.ws && a.batch == 1) ? std::min(a.ws_bytes, kWsCap) : 0;  // batched: no split
-  const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn, a.batch == 1);
+  const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn, a.batch == 1,
+                                 a.a_mode == 0 ? a.kh * a.kw : 1);
   const int arows = kBM * tp.ms;  // A rows per box
   AMaps ma;
   CUtensorMap mb, my, mr;
