@@ -589,11 +589,15 @@ struct DwTile {
   static constexpr int MIN_CTAS = 2;
 };
 
-template <int S>
+//
+// POOL: the same tiles, windows and ring compute a 3x3 MaxPool instead (SPINN/run_time/ops/
+// pool/maxpool.c:5-49): the maximum over the taps inside the image, starting from the
+// reference's -1e30 (the TMA zero fill of padding positions is masked, not maxed).
+template <int S, bool POOL = false>
 __global__ void __launch_bounds__(kDwThreads, DwTile<S>::MIN_CTAS) depthwise3x3_tma_kernel(
     const __grid_constant__ CUtensorMap mx, const float4* __restrict__ w, const float4* __restrict__ bias,
     const float4* __restrict__ res, float4* __restrict__ y, int n, int c4, int oh, int ow, int ph, int pw,
-    int tiles_x, int tiles_y, int groups, int act, int round_out, int* err) {
+    int tiles_x, int tiles_y, int groups, int act, int round_out, int* err, int h = 0, int wd = 0) {
   using T = DwTile<S>;
   extern __shared__ uint8_t dw_raw[];
   float4* buf = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(dw_raw) + 127) & ~uintptr_t(127));
@@ -652,7 +656,47 @@ __global__ void __launch_bounds__(kDwThreads, DwTile<S>::MIN_CTAS) depthwise3x3_
     int g, b, ty, tx;
     unit_coords(u, &g, &b, &ty, &tx);
     const int qq = g * 8 + q;  // channel quad
-    if (qq < c4) {
+    if (POOL && qq < c4) {
+      const float4* win = buf + (size_t)cur * (T::BYTES / 16);
+      const int iy0 = ty * T::TH * S - ph + by * T::RB * S, ix0 = tx * T::TW * S - pw + bx * T::CB * S;
+      const float4 lo = make_float4(-1e30f, -1e30f, -1e30f, -1e30f);  // maxpool.c's initial value
+      float4 acc[T::RB][T::CB];
+#pragma unroll
+      for (int i = 0; i < T::RB; ++i)
+#pragma unroll
+        for (int j = 0; j < T::CB; ++j) acc[i][j] = lo;
+#pragma unroll
+      for (int wr = 0; wr < T::BR; ++wr) {
+        if ((unsigned)(iy0 + wr) >= (unsigned)h) continue;  // a padding row: no tap
+#pragma unroll
+        for (int wc = 0; wc < T::BC; ++wc) {
+          if ((unsigned)(ix0 + wc) >= (unsigned)wd) continue;
+          const float4 v = win[((by * T::RB * S + wr) * T::IW + bx * T::CB * S + wc) * 8 + q];
+#pragma unroll
+          for (int i = 0; i < T::RB; ++i) {
+            const int r = wr - i * S;
+            if (r < 0 || r > 2) continue;
+#pragma unroll
+            for (int j = 0; j < T::CB; ++j) {
+              const int sc = wc - j * S;
+              if (sc < 0 || sc > 2) continue;
+              float4& m = acc[i][j];
+              m.x = v.x > m.x ? v.x : m.x;
+              m.y = v.y > m.y ? v.y : m.y;
+              m.z = v.z > m.z ? v.z : m.z;
+              m.w = v.w > m.w ? v.w : m.w;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < T::RB; ++i)
+#pragma unroll
+        for (int j = 0; j < T::CB; ++j) {
+          const int oy = ty * T::TH + by * T::RB + i, ox = tx * T::TW + bx * T::CB + j;
+          if (oy < oh && ox < ow) y[(((size_t)b * oh + oy) * ow + ox) * c4 + qq] = acc[i][j];
+        }
+    } else if (!POOL && qq < c4) {
       if (qq != wg) {  // a new channel group: its weights
 #pragma unroll
         for (int t = 0; t < 9; ++t) k[t] = __ldg(w + (size_t)t * c4 + qq);
@@ -947,9 +991,20 @@ int launch_nhwc_to_nchw(const float* x, float* y, int n, int c, int h, int w, in
   SPINN_LAUNCH_CHECK();
 }
 
+template <int S, bool POOL>
+int launch_depthwise3x3_tma(const float* x, const float* w, const float* bias, const float* res, float* y, int n,
+                            int h, int wd, int cpad, int oh, int ow, int ph, int pw, int act, int round_out, int dev,
+                            cudaStream_t s);
+
 int launch_maxpool_nhwc(const float* x, float* y, int n, int h, int w, int cpad, int oh, int ow, int kh, int kw,
                         int sh, int sw, int ph, int pw, cudaStream_t s) {
   SPINN_CHECK_ARG(cpad % 4 == 0, "maxpool: channel stride %d not a multiple of 4", cpad);
+  // 3x3 stride 2 through the TMA window ring of the depthwise kernel (padding taps masked)
+  if (kh == 3 && kw == 3 && sh == 2 && sw == 2 && ph >= 0 && pw >= 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    int dev = 0;
+    SPINN_CUDA_TRY(cudaGetDevice(&dev));
+    return launch_depthwise3x3_tma<2, true>(x, nullptr, nullptr, nullptr, y, n, h, w, cpad, oh, ow, ph, pw, 0, 0, dev, s);
+  }
   // The tiled kernel needs every output window to hold at least one real tap (pads <= 1 with
   // the ONNX output size), which the -1e30 fill relies on like the generic kernel's skip.
   if (kh == 3 && kw == 3 && sh == 2 && sw == 2 && cpad / 4 <= kPoolMaxC4 && ph >= 0 && ph <= 1 && pw >= 0 &&
@@ -1123,7 +1178,7 @@ int launch_channel_affine_nhwc(const float* x, float* y, long pixels, int cpad, 
   SPINN_LAUNCH_CHECK();
 }
 
-template <int S>
+template <int S, bool POOL = false>
 int launch_depthwise3x3_tma(const float* x, const float* w, const float* bias, const float* res, float* y, int n,
                             int h, int wd, int cpad, int oh, int ow, int ph, int pw, int act, int round_out, int dev,
                             cudaStream_t s) {
@@ -1139,17 +1194,19 @@ int launch_depthwise3x3_tma(const float* x, const float* w, const float* bias, c
   static std::atomic<uint64_t> configured{0};
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    SPINN_CUDA_TRY(cudaFuncSetAttribute(depthwise3x3_tma_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    SPINN_CUDA_TRY(
+        cudaFuncSetAttribute(depthwise3x3_tma_kernel<S, POOL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured.fetch_or(bit);
   }
   int per_sm = 0;
-  SPINN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, depthwise3x3_tma_kernel<S>, kDwThreads, smem));
+  SPINN_CUDA_TRY(
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, depthwise3x3_tma_kernel<S, POOL>, kDwThreads, smem));
   const long grid = std::min<long>(units, (long)sm_count(dev) * std::max(per_sm, 1));
   if (grid <= 0) return 0;
-  depthwise3x3_tma_kernel<S><<<(int)grid, kDwThreads, smem, s>>>(
+  depthwise3x3_tma_kernel<S, POOL><<<(int)grid, kDwThreads, smem, s>>>(
       mx, reinterpret_cast<const float4*>(w), reinterpret_cast<const float4*>(bias),
       reinterpret_cast<const float4*>(res), reinterpret_cast<float4*>(y), n, cpad / 4, oh, ow, ph, pw, tiles_x,
-      tiles_y, groups, act, round_out, device_error_flag(dev));
+      tiles_y, groups, act, round_out, device_error_flag(dev), h, wd);
   SPINN_LAUNCH_CHECK();
 }
 
