@@ -240,6 +240,10 @@ void spinn_cuda_host_free(void *p);
 /* Library version string. */
 const char *spinn_cuda_version(void);
 
+/* Diagnostics: tcgen05 launches so far in this process that ran a stream-K schedule (each
+ * CTA an equal share of the problem's k-blocks across tile boundaries). */
+uint64_t spinn_cuda_stat_streamk_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

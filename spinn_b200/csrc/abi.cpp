@@ -37,8 +37,9 @@ struct Session {
   uint8_t* scratch = nullptr;
   size_t scratch_cap = 0;
   size_t scratch_used = 0;
-  float* ws = nullptr;  // split-K workspace of the tcgen05 launches
+  float* ws = nullptr;  // split-K / stream-K workspace of the tcgen05 launches
   size_t ws_cap = 0;
+  int* sk_flags = nullptr;  // stream-K handoff flags (kTcSkFlags ints, zero between launches)
   std::map<std::tuple<const void*, uint64_t, int, int>, DevWeight> wcache;
 };
 
@@ -71,9 +72,27 @@ float* scratch_take(size_t bytes) {
 }
 size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
 
-// Launches a tcgen05 GEMM with the split-K workspace its shape wants (grown on demand).
+// Device error check of the session; a launch that timed out may have left stream-K flags
+// raised, and they are cleared so that the session stays usable.
+int check_session(Session& S) {
+  const int rc = check_device_error_flag(S.device, S.stream);
+  if (rc && S.sk_flags) {
+    cudaMemsetAsync(S.sk_flags, 0, kTcSkFlags * sizeof(int), S.stream);
+    cudaStreamSynchronize(S.stream);
+  }
+  return rc;
+}
+
+// Launches a tcgen05 GEMM with the split-K / stream-K workspace its shape wants (grown on
+// demand).
 int tc_launch_ws(TcGemmArgs a, cudaStream_t st) {
   Session& S = g_sess;
+  if (!S.sk_flags) {
+    SPINN_CUDA_TRY(cudaMalloc(&S.sk_flags, kTcSkFlags * sizeof(int)));
+    SPINN_CUDA_TRY(cudaMemsetAsync(S.sk_flags, 0, kTcSkFlags * sizeof(int), S.stream));
+  }
+  a.sk = a.batch == 1;
+  a.sk_flags = S.sk_flags;
   const size_t need = tc_gemm_workspace_bytes(a);
   if (need > S.ws_cap) {
     SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));
@@ -222,7 +241,7 @@ int finish_output(SpinnTensor* Y, const float* dev_y, size_t bytes) {
   if (!is_device_ptr(Y->data)) {
     SPINN_CUDA_TRY(cudaMemcpyAsync(Y->data, dev_y, bytes, cudaMemcpyDeviceToHost, g_sess.stream));
     SPINN_CUDA_TRY(cudaStreamSynchronize(g_sess.stream));
-    return check_device_error_flag(g_sess.device, g_sess.stream);
+    return check_session(g_sess);
   }
   return 0;
 }
@@ -308,7 +327,7 @@ __attribute__((visibility("default"))) int spinn_cuda_sync(void) {
   Session& S = g_sess;
   if (!S.ready) return 0;
   SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));
-  return check_device_error_flag(S.device, S.stream);
+  return check_session(S);
 }
 
 __attribute__((visibility("default"))) int spinn_cuda_selftest_wait_expiry(uint64_t timeout_ns) {
@@ -334,6 +353,8 @@ __attribute__((visibility("default"))) void spinn_cuda_shutdown(void) {
   if (S.ws) cudaFree(S.ws);
   S.ws = nullptr;
   S.ws_cap = 0;
+  if (S.sk_flags) cudaFree(S.sk_flags);
+  S.sk_flags = nullptr;
   cudaStreamDestroy(S.stream);
   S.stream = nullptr;
   S.ready = false;
@@ -342,6 +363,10 @@ __attribute__((visibility("default"))) void spinn_cuda_shutdown(void) {
 __attribute__((visibility("default"))) const char* spinn_cuda_last_error(void) { return get_error(); }
 
 __attribute__((visibility("default"))) const char* spinn_cuda_version(void) { return "spinn_b200 0.1 (sm_100a)"; }
+
+__attribute__((visibility("default"))) uint64_t spinn_cuda_stat_streamk_launches(void) {
+  return spinn::tc_gemm_streamk_launches();
+}
 
 __attribute__((visibility("default"))) void* spinn_cuda_host_alloc(size_t bytes) {
   void* p = nullptr;

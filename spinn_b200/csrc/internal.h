@@ -106,12 +106,24 @@ struct TcGemmArgs {
   const float* xpart[4] = {nullptr, nullptr, nullptr, nullptr};
   int part_c0[4] = {0, 0, 0, 0};
   int part_cpad[4] = {0, 0, 0, 0};
+  // Stream-K schedule allowed (sk = 1; the planner decides): each CTA (pair) takes an equal
+  // share of the problem's k-blocks across tile boundaries, so a short last wave does not
+  // idle SMs.  A tile split between CTAs is finished by the CTA holding its first k-blocks,
+  // which adds the other CTAs' partial sums (left in `ws`, one slot per CTA) in k order after a
+  // bounded wait on their flags.  `sk_flags`: kTcSkFlags zero-initialised ints that only these
+  // launches use (each consumer clears the flags it read); launches sharing them must not
+  // overlap on the GPU.
+  int sk = 0;
+  int* sk_flags = nullptr;
 };
+constexpr int kTcSkFlags = 512;
 // Workspace a launch of `a` would use (0 when it would not split), for planners.
 size_t tc_gemm_workspace_bytes(const TcGemmArgs& a);
 // Checks whether the tcgen05 path accepts the problem (alignment, corner ranges ...).
 bool tc_gemm_supported(const TcGemmArgs& a, std::string* why);
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);
+// Launches so far (process-wide) that ran the stream-K schedule.
+uint64_t tc_gemm_streamk_launches();
 // Number of K blocks (32 wide) and padded K the weight matrix must have.
 inline int tc_num_kb(int K) { return (K + 31) / 32; }
 

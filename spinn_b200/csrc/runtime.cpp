@@ -145,6 +145,8 @@ struct SpinnCudaModel {
   std::map<int, int> b_trans;    // Transposes folded into a MatMul's B: tensor -> untransposed tensor
   float* splitk_ws = nullptr;      // split-K partial sums, shared by all steps (one stream)
   size_t splitk_bytes = 0;
+  int* sk_flags = nullptr;         // stream-K handoff flags (kTcSkFlags ints), shared the same way
+  bool sk_used = false;
   std::vector<float> whost;        // pre-transformed weights before upload
   std::vector<StepRec> steps;
   cudaGraph_t graph = nullptr;
@@ -897,10 +899,15 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
                 c0 += pbuf->cpad;
               }
             }
+            // stream-K schedules for convolutions whose tiles leave the last wave short
+            // (SPINN_NO_SK=1 turns them off, for comparisons)
+            a.sk = getenv("SPINN_NO_SK") == nullptr;
+            m->sk_used |= a.sk != 0;
             note_ws(m, a);
             r.run = [m, a, xbp, ybp, rbp, woff, boff, xparts](cudaStream_t st) mutable {
               a.ws = m->splitk_ws;
               a.ws_bytes = m->splitk_bytes;
+              a.sk_flags = m->sk_flags;
               for (size_t i = 0; i < xparts.size(); ++i) a.xpart[i] = xparts[i]->ptr;
               a.x = xbp->ptr;
               a.y = ybp->ptr;
@@ -1905,7 +1912,22 @@ static int compile_model(SpinnCudaModel* m, uint64_t budget) {
     if (m->steps[i].kind != 0) ++m->kernels;
   }
   if (m->splitk_bytes) SPINN_CUDA_TRY(cudaMalloc(&m->splitk_ws, m->splitk_bytes));
+  if (m->sk_used && m->splitk_bytes) {
+    SPINN_CUDA_TRY(cudaMalloc(&m->sk_flags, kTcSkFlags * sizeof(int)));
+    SPINN_CUDA_TRY(cudaMemset(m->sk_flags, 0, kTcSkFlags * sizeof(int)));
+  }
   return 0;
+}
+
+// Device error check after a run.  A run that timed out may have left stream-K flags raised;
+// they are cleared so that the model stays usable.
+static int check_run(SpinnCudaModel* m, cudaStream_t st) {
+  const int rc = check_device_error_flag(m->device, st);
+  if (rc && m->sk_flags) {
+    cudaMemsetAsync(m->sk_flags, 0, kTcSkFlags * sizeof(int), st);
+    cudaStreamSynchronize(st);
+  }
+  return rc;
 }
 
 static int run_steps(SpinnCudaModel* m, cudaStream_t st, bool prof) {
@@ -1933,6 +1955,7 @@ static void release_model(SpinnCudaModel* m) {
   if (m->arena) cudaFree(m->arena);
   if (m->wdev) cudaFree(m->wdev);
   if (m->splitk_ws) cudaFree(m->splitk_ws);
+  if (m->sk_flags) cudaFree(m->sk_flags);
   if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
   if (m->gexec_alt) cudaGraphExecDestroy(m->gexec_alt);
   if (m->graph_alt) cudaGraphDestroy(m->graph_alt);
@@ -2006,7 +2029,7 @@ __attribute__((visibility("default"))) int spinn_cuda_plan(SpinnCudaModel* m, in
   rc = run_steps(m, m->stream, false);
   if (rc) return rc;
   SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
-  rc = check_device_error_flag(device, m->stream);
+  rc = check_run(m, m->stream);
   if (rc) return rc;
   if (!(flags & SPINN_CUDA_PLAN_NO_GRAPH)) {
     for (int pass = 0; pass < ((flags & SPINN_CUDA_PLAN_PROFILE) ? 2 : 1); ++pass) {
@@ -2066,7 +2089,7 @@ extern "C" __attribute__((visibility("default"))) int spinn_cuda_run_profiled(Sp
   m->step_ms.assign(m->steps.size(), 0.0f);
   for (size_t i = 0; i < m->steps.size(); ++i)
     SPINN_CUDA_TRY(cudaEventElapsedTime(&m->step_ms[i], m->events[i], m->events[i + 1]));
-  return check_device_error_flag(m->device, st);
+  return check_run(m, st);
 }
 
 __attribute__((visibility("default"))) int spinn_cuda_run_device(SpinnCudaModel* m, void* stream) {
@@ -2100,7 +2123,7 @@ __attribute__((visibility("default"))) int spinn_cuda_run(SpinnCudaModel* m, con
     SPINN_CUDA_TRY(cudaMemcpyAsync(output, b.ptr, b.bytes, cudaMemcpyDeviceToHost, m->stream));
   }
   SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
-  return check_device_error_flag(m->device, m->stream);
+  return check_run(m, m->stream);
 }
 
 // Points input 0 -- its staging buffer and every tensor aliasing it -- at `p`; returns the
@@ -2189,7 +2212,7 @@ __attribute__((visibility("default"))) int spinn_cuda_wait(SpinnCudaModel* m) {
   }
   SPINN_CUDA_TRY(cudaSetDevice(m->device));
   SPINN_CUDA_TRY(cudaStreamSynchronize(m->stream));
-  return check_device_error_flag(m->device, m->stream);
+  return check_run(m, m->stream);
 }
 
 __attribute__((visibility("default"))) void* spinn_cuda_io_ptr(SpinnCudaModel* m, int is_output, int index,

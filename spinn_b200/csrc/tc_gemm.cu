@@ -76,7 +76,29 @@ struct TcParams {
   int* err;
   int nparts;                // tensor maps of A in use (1 = an ordinary tensor)
   int part_c0[kMaxAParts];   // first channel (K column) of each part
+  // Stream-K (sk = 1; batch 1, no split, no residual, no resident weights): worker w of
+  // G = gridDim.x / PAIR owns k-blocks [w T / G, (w+1) T / G) of the T = num_tiles * num_kb
+  // k-blocks laid out tile after tile.  A worker whose range starts inside a tile stores that
+  // first piece raw into its slot of sk_ws and counts it done on sk_flags[w * PAIR + rank];
+  // the worker holding the tile's first k-block adds those slots in worker order.
+  int sk;
+  float* sk_ws;
+  int* sk_flags;
 };
+
+// One piece of a CTA's work: k-blocks [kb0, kb1) of a tile.  kind 0: the whole reduction of
+// the tile (the ordinary epilogue); 1: a stream-K tail piece (raw partial to the worker's slot);
+// 2: the head piece of a tile that later workers finish (adds their partials first).
+struct Piece {
+  int tile, z, kb0, kb1, kind;
+};
+// Arrivals on a stream-K flag: each epilogue warp of the producing CTA once, then each
+// epilogue warp of the consuming CTA once; the last consumer arrival clears the flag.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // Part of A holding channel (K column) c, and c relative to that part.
 __device__ __forceinline__ int a_part(const TcParams& p, int* c) {
@@ -186,6 +208,20 @@ __device__ __forceinline__ bool warp_wait_backoff(uint64_t* bar, uint32_t parity
   const bool ok = mbar_wait_backoff(bar, parity, abort, ns);
   return __all_sync(0xffffffffu, ok);
 }
+// Bounded warp-wide wait until the stream-K flag `f` reaches `target` arrivals (acquire: the
+// partial sums published before those arrivals are visible afterwards).
+__device__ __forceinline__ bool warp_wait_flag(const int* f, int target, volatile int* abort, uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (__all_sync(0xffffffffu, ld_acquire_gpu(f) >= target)) return true;
+    if (warp_aborted(abort)) return false;
+    if (__any_sync(0xffffffffu, globaltimer_ns() - t0 > ns)) {
+      *abort = 1;
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
 
 // PAIR = 1: one CTA per 128 x BN tile.  PAIR = 2: a cluster of two CTAs per 256 x BN tile
 // with one cta_group::2 MMA stream issued by the leader (rank 0); each CTA loads its own 128
@@ -207,6 +243,10 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
   constexpr int MS = C::MS;
   constexpr int NRS = C::RES_SLOTS > 0 ? C::RES_SLOTS : 1;
   constexpr int TM = kBM * PAIR * MS;  // rows of one work unit
+  // stream-K: 32-column chunks one epilogue warp drains per tile, and how many later workers'
+  // partial sums (this CTA's rows) fit in the operand ring at once
+  constexpr int SK_MYCH = MS == 2 ? BN / 32 : BN / 32 / C::EPI_GROUPS;
+  constexpr int SK_NCAP = WR ? 0 : (int)((size_t)STAGES * C::STAGE / ((size_t)C::EPI_WARPS * SK_MYCH * 4096));
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -266,12 +306,43 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
   // (One stage only: prefetches occupy the SM's copy engine ahead of the loads that follow,
   // and eight stages' worth slowed the narrow YOLO-shaped layers by ~10%.  Resident weights
   // are loaded whole right after the wait anyway.)
-  if (!WR && warp == (C::SPLIT_LOAD ? 3 : 0) && lane == 0 && unit0 < p.num_units) {
-    const int z = unit0 / p.num_tiles, t = unit0 - z * p.num_tiles;
-    const int tile = p.reverse ? p.num_tiles - 1 - t : t;
-    const int tn = tile % p.tiles_n;
-    const int ks = p.batch > 1 ? 0 : z, bzb = p.b_batched ? z : 0;
-    const int kb0 = ks * p.kb_per, kb1 = min(p.num_kb, kb0 + min(p.kb_per, kWPrefetchKb));
+  // Work of this CTA.  Ordinary launches: units unit0, unit0 + unit_step, ... (a dynamic
+  // schedule -- units claimed from a global counter and handed to the other roles through a
+  // shared-memory queue -- evened out the CTAs' finishing times but measured 1-2% slower end
+  // to end).  Stream-K: consecutive tiles covering the worker's k-block range.
+  const bool sk = !RES && !WR && p.sk != 0;
+  const long sk_total = (long)p.num_tiles * p.num_kb;
+  const long sk_r0 = sk ? sk_total * unit0 / unit_step : 0, sk_r1 = sk ? sk_total * (unit0 + 1) / unit_step : 0;
+  const int sk_t0 = sk ? (int)(sk_r0 / p.num_kb) : 0;
+  auto get_piece = [&](int it, Piece& pc) -> bool {
+    int t;
+    if (sk) {
+      t = sk_t0 + it;
+      const long base = (long)t * p.num_kb;
+      const long g0 = max(sk_r0, base), g1 = min(sk_r1, base + p.num_kb);
+      if (g0 >= g1) return false;
+      pc.z = 0;
+      pc.kb0 = (int)(g0 - base);
+      pc.kb1 = (int)(g1 - base);
+      pc.kind = pc.kb0 > 0 ? 1 : pc.kb1 < p.num_kb ? 2 : 0;
+    } else {
+      const long u = (long)unit0 + (long)it * unit_step;
+      if (u >= p.num_units) return false;
+      pc.z = (int)u / p.num_tiles;
+      t = (int)u - pc.z * p.num_tiles;
+      const int ks = p.batch > 1 ? 0 : pc.z;
+      pc.kb0 = ks * p.kb_per;
+      pc.kb1 = min(p.num_kb, pc.kb0 + p.kb_per);
+      pc.kind = 0;
+    }
+    pc.tile = p.reverse ? p.num_tiles - 1 - t : t;
+    return true;
+  };
+  Piece pc0;
+  if (!WR && warp == (C::SPLIT_LOAD ? 3 : 0) && lane == 0 && get_piece(0, pc0)) {
+    const int tn = pc0.tile % p.tiles_n;
+    const int bzb = p.b_batched ? pc0.z : 0;
+    const int kb0 = pc0.kb0, kb1 = min(pc0.kb1, kb0 + kWPrefetchKb);
     for (int kb = kb0; kb < kb1; ++kb)
 #pragma unroll
       for (int j = 0; j < C::NSUB; ++j)
@@ -287,9 +358,6 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
   griddep_wait();
   griddep_launch_dependents();
 
-  // Work units of this CTA: unit0, unit0 + unit_step, ...  (A dynamic schedule -- units
-  // claimed from a global counter and handed to the other roles through a shared-memory
-  // queue -- evened out the CTAs' finishing times but measured 1-2% slower end to end.)
   auto take_unit = [&](int it) -> int {
     const long u = (long)unit0 + (long)it * unit_step;
     return u < p.num_units ? (int)u : -1;
@@ -306,7 +374,7 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
     uint32_t ph = 0;
     uint32_t armed = 0, armed_ph = 0;  // bit s: stage s armed at least once; its last parity
     // resident weights: all num_kb k-blocks of the single N tile, once, on `wfull`
-    const bool w_issued = WR && do_a && unit0 < p.num_units;
+    const bool w_issued = WR && do_a && get_piece(0, pc0);
     if (w_issued && lane == 0) {
       mbar_arrive_expect_tx(wfull, (uint32_t)p.num_kb * C::B_STAGE);
       for (int kb = 0; kb < p.num_kb; ++kb)
@@ -316,17 +384,16 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
     }
     __syncwarp();
     for (int it = 0; !warp_aborted(abort_flag); ++it) {
-      const int u = take_unit(it);
-      if (u < 0) break;
-      const int z = u / p.num_tiles, t = u - z * p.num_tiles;
-      const int tile = p.reverse ? p.num_tiles - 1 - t : t;
-      const int ks = p.batch > 1 ? 0 : z, bz = p.batch > 1 ? z : 0;
+      Piece pc;
+      if (!get_piece(it, pc)) break;
+      const int tile = pc.tile;
+      const int bz = p.batch > 1 ? pc.z : 0;
       const int bzb = p.b_batched ? bz : 0;  // batch plane of W
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       int m0 = tm * TM + (int)rank * kBM;
       if (m0 >= p.M) m0 = tm * TM;  // a pair's second half past the end: load valid rows, store none
       const int nb0 = tn * BN + (int)rank * C::BNC;
-      const int kb0 = ks * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
+      const int kb0 = pc.kb0, kb1 = pc.kb1;
       int w0 = 0, h0 = 0, img = 0;
       // im2col walk state for the next box: channel offset c0 inside tap (r, q)
       int c0 = 0, r = 0, q = 0, tap = 0;
@@ -421,11 +488,11 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
       int it = 0;
       bool issued = false;
       for (;; ++it) {
-        const int u = take_unit(it);
-        if (u < 0 || warp_aborted(abort_flag)) break;
+        Piece pc;
+        if (!get_piece(it, pc) || warp_aborted(abort_flag)) break;
         const int b = it % C::NACC;
         const uint32_t aph = (it / C::NACC) & 1;
-        const int kb0 = (p.batch > 1 ? 0 : u / p.num_tiles) * p.kb_per, kb1 = min(p.num_kb, kb0 + p.kb_per);
+        const int kb0 = pc.kb0, kb1 = pc.kb1;
         if (!warp_wait(&tempty[b], aph ^ 1, abort_flag, kTimeoutNs)) break;
         if (WR && it == 0 && !warp_wait(wfull, 0, abort_flag, kTimeoutNs)) break;  // resident weights
         tc_fence_after();
@@ -544,11 +611,13 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
     const bool partial = p.ksplit > 1;
     const bool unit_alpha = p.alpha == 1.0f;
     for (;; ++it) {
-      const int u = take_unit(it);
-      if (u < 0) break;
-      const int z = u / p.num_tiles, t = u - z * p.num_tiles;  // z: K slice or batch -> output plane
-      const int tile = p.reverse ? p.num_tiles - 1 - t : t;
+      Piece pc;
+      if (!get_piece(it, pc)) break;
+      const int z = pc.z;  // K slice or batch -> output plane
+      const int tile = pc.tile;
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+      // stream-K tail piece: raw partial sums to this worker's slot, no epilogue
+      const bool raw = partial || pc.kind == 1;
       const int m0 = tm * TM + (int)rank * kBM, n0 = tn * BN;
       const int b = it % C::NACC;
       const uint32_t aph = (it / C::NACC) & 1;
@@ -563,12 +632,45 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
 #pragma unroll
       for (int i = 0; i < MYCH; ++i) {
         const int col = n0 + 32 * (MS == 2 ? i : i * C::EPI_GROUPS + eo) + lane;
-        bias_reg[i] = (!partial && p.bias && col < p.N) ? __ldg(p.bias + col) : 0.0f;
+        bias_reg[i] = (!raw && p.bias && col < p.N) ? __ldg(p.bias + col) : 0.0f;
       }
       if (!warp_wait_backoff(&tfull[b], aph, abort_flag, kTimeoutNs)) break;
       tc_fence_after();
       const int row0 = m0 + (MS == 2 ? eg * kBM : 0) + wq * 32;
       const bool rows_live = row0 < p.M;
+      // stream-K slot layout: [chunk of 32 columns][lane quarter][column][row in quarter], so
+      // that a warp's 32 rows of one column are one 128-byte line and its part of a chunk is
+      // one contiguous 4 KiB block
+      constexpr size_t kSlot = (size_t)kBM * MS * BN;
+      const size_t sk_wbase = (size_t)(((MS == 2 ? eg * (BN / 32) : 0) * 4 + wq) * 1024);
+      // Head of a split tile: the workers after this one whose ranges start inside the tile
+      // (unit0 + 1 .. sk_j1 - 1) each left the rest of the tile's sum in their slots.  The
+      // first SK_NCAP of them are copied into this warp's share of the operand ring -- idle
+      // now, this is the CTA's last piece -- in one round trip, instead of one per chunk.
+      int sk_j1 = unit0 + 1, sk_jfast = unit0 + 1;
+      if (sk && pc.kind == 2) {
+        const long tend = (long)(sk_t0 + it + 1) * p.num_kb;
+        bool ok = true;
+        for (; ok && sk_j1 < unit_step && sk_total * sk_j1 / unit_step < tend; ++sk_j1)
+          ok = warp_wait_flag(p.sk_flags + sk_j1 * PAIR + rank, C::EPI_WARPS, abort_flag, kTimeoutNs);
+        if (!ok) break;
+        sk_jfast = min(sk_j1, unit0 + 1 + SK_NCAP);
+        if (rows_live && sk_jfast > unit0 + 1) {
+          float* stage = reinterpret_cast<float*>(sA) + (size_t)(warp - 4) * SK_NCAP * SK_MYCH * 1024;
+          for (int j = unit0 + 1; j < sk_jfast; ++j) {
+            const float* slot = p.sk_ws + (size_t)(j * PAIR + (int)rank) * kSlot + sk_wbase;
+            for (int c = 0; c < BN / 32 && n0 + c * 32 < p.N; ++c) {
+              if (MS == 1 && c % C::EPI_GROUPS != eo) continue;
+              const float* src = slot + (size_t)c * 4096;
+              float* dst = stage + ((j - unit0 - 1) * SK_MYCH + (MS == 2 ? c : c / C::EPI_GROUPS)) * 1024;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) cp_async_16(dst + (k * 32 + lane) * 4, src + (k * 32 + lane) * 4);
+            }
+          }
+          cp_async_wait_all();
+          __syncwarp();
+        }
+      }
       const uint32_t acc_col = b * (BN * MS) + (MS == 2 ? eg * BN : 0);
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = n0 + c * 32;
@@ -587,7 +689,31 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          if (!partial) {
+          const size_t sk_off = sk_wbase + (size_t)c * 4096 + lane;
+          if (pc.kind == 1) {
+            float* dst = p.sk_ws + (size_t)(unit0 * PAIR + (int)rank) * kSlot + sk_off;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) __stcg(dst + i * 32, v[i]);
+            continue;
+          }
+          if (pc.kind == 2) {
+            const float* stage = reinterpret_cast<const float*>(sA) + (size_t)(warp - 4) * SK_NCAP * SK_MYCH * 1024 +
+                                 (MS == 2 ? c : c / C::EPI_GROUPS) * 1024 + lane;
+            for (int j = unit0 + 1; j < sk_jfast; ++j) {
+              const float* src = stage + (j - unit0 - 1) * SK_MYCH * 1024;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += src[i * 32];
+            }
+            for (int j = sk_jfast; j < sk_j1; ++j) {
+              const float* src = p.sk_ws + (size_t)(j * PAIR + (int)rank) * kSlot + sk_off;
+              float q[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) q[i] = __ldcg(src + i * 32);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += q[i];
+            }
+          }
+          if (!raw) {
             if (!unit_alpha) {
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
@@ -655,6 +781,14 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
           mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
         else
           mbar_arrive(&tempty[b]);
+        if (pc.kind == 1) {  // publish this warp's part of the partial
+          __threadfence();
+          atomicAdd(p.sk_flags + unit0 * PAIR + (int)rank, 1);
+        } else if (pc.kind == 2) {  // done with the contributors' slots; the last reader clears
+          for (int j = unit0 + 1; j < sk_j1; ++j)
+            if (atomicAdd(p.sk_flags + j * PAIR + (int)rank, 1) == 2 * C::EPI_WARPS - 1)
+              atomicExch(p.sk_flags + j * PAIR + (int)rank, 0);
+        }
       }
     }
     // the stores' shared-memory reads are done before the CTA may exit; their global writes
@@ -895,21 +1029,23 @@ struct TilePlan {
   int bk = 32;   // K depth of a pipeline stage
   int ksplit = 1;
   int kb_per = 1;
+  int sk = 0;  // stream-K schedule over all slots
   size_t ws_bytes = 0;
 };
 
-// Optional override for tuning sweeps: SPINN_TC_TILES="bn,ksplit[,pair[,bk[,ms[,wr]]]]" (read
-// at each launch; a captured graph keeps the choice made when it was captured; wr: -1 = no,
-// 1 = yes, 0 = planner's choice).
-void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms, int* wr) {
+// Optional override for tuning sweeps: SPINN_TC_TILES="bn,ksplit[,pair[,bk[,ms[,wr[,sk]]]]]"
+// (read at each launch; a captured graph keeps the choice made when it was captured; wr and
+// sk: -1 = no, 1 = yes, 0 = planner's choice).
+void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms, int* wr, int* sk) {
   *bn = -1;
   *ks = 0;
   *pair = 0;
   *bk = 0;
   *ms = 0;
   *wr = 0;
+  *sk = 0;
   const char* e = getenv("SPINN_TC_TILES");
-  if (e && sscanf(e, "%d,%d,%d,%d,%d,%d", bn, ks, pair, bk, ms, wr) < 1) *bn = -1;
+  if (e && sscanf(e, "%d,%d,%d,%d,%d,%d,%d", bn, ks, pair, bk, ms, wr, sk) < 1) *bn = -1;
 }
 
 // Chooses the tile shape (BN, single CTA or CTA pair, stage depth) and the K split from a
@@ -924,10 +1060,23 @@ void forced_tiles(int* bn, int* ks, int* pair, int* bk, int* ms, int* wr) {
 // boxes, one W box per two MMAs) pay off.  A split adds the finish pass: (ksplit + 2) x M x N
 // floats at 8 TB/s (the partials are L2-resident).  64-deep stages and sub-tiles need channel
 // blocks of 16 or 32 and no fused residual (the residual ring would leave too few stages).
+//
+// Stream-K (allow_sk: a flag buffer is at hand, batch 1) spreads the tiles' k-blocks evenly
+// over every slot, so a last wave that would leave slots idle does not: the main loop costs
+// ceil(tiles x k-blocks / slots) stages, each ~10% dearer than the fit with every SM loading
+// (measured: 0.68 against 0.62 us for 256-wide pairs), plus ~10 us that ResNet-101's 14x14
+// and 7x7 layers measured beyond that at batches 64-256 (the head worker's exposed tail: a
+// contributor that ends with it, the partial-sum copy, then the epilogue).  So it pays where
+// a long reduction leaves a short last wave -- the 512-channel 7x7 3x3 layers at batch 256, 98
+// pair tiles on 74 slots: 110 -> 89 us -- and not for short ones.  Only for problems of at
+// most four waves of whole tiles: across many waves the tile order of the ordinary schedule
+// keeps L2 locality that stream-K ranges lose (the stem and the 56x56 1x1 layers measured
+// 10-25% slower), and the last wave matters little there.
 TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t ws_limit, int force_bn,
-                    bool allow_wr, int taps) {
-  int fbn, fks, fpair, fbk, fms, fwr;
-  forced_tiles(&fbn, &fks, &fpair, &fbk, &fms, &fwr);
+                    bool allow_wr, int taps, bool allow_sk) {
+  int fbn, fks, fpair, fbk, fms, fwr, fsk;
+  forced_tiles(&fbn, &fks, &fpair, &fbk, &fms, &fwr, &fsk);
+  if (fsk < 0 || fks > 1 || has_res || sms > kTcSkFlags) allow_sk = false;
   if (force_bn <= 0 && (fbn == 64 || fbn == 128 || fbn == 256)) force_bn = fbn;
   struct Shape {
     int bn, pair, bk, ms, wr;
@@ -947,8 +1096,9 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
   // fit (forced-tile sweep of ResNet-101's 3x3 layers at batch 256: 0.57-0.60 us per stage
   // against 0.405), while the pair and two-sub-tile shapes matched it.
   const double im2col_single64 = taps > 1 ? 1.3 : 1.0;
-  TilePlan best;
-  double best_cost = 1e300;
+  TilePlan best, best_sk;
+  double best_cost = 1e300, best_sk_cost = 1e300;
+  long best_waves = 0;
   for (const Shape& sh : shapes) {
     const int bn = sh.bn;
     if (force_bn > 0 && bn != force_bn) continue;
@@ -970,6 +1120,27 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
     const int num_kb = (K + sh.bk - 1) / sh.bk;
     const int tm = kBM * sh.pair * sh.ms;
     const long tiles = (long)((M + tm - 1) / tm) * ((N + bn - 1) / bn);
+    const double epi1 = sh.ms == 2 ? 0.8 * (bn / 32) : 0.8 * (bn / 32) / ((has_res && bn == 256) ? 1 : 2);
+    const long total_kb = tiles * num_kb;
+    const size_t sk_ws = (size_t)sms * kBM * sh.ms * bn * 4;  // one slot per CTA
+    if (allow_sk && !sh.wr && total_kb >= 2L * slots && sk_ws <= ws_limit) {
+      const long per = (total_kb + slots - 1) / slots;  // k-blocks per worker
+      const long pieces = (per + num_kb - 1) / num_kb + 1;
+      const double parts = per >= num_kb ? 1.0 : (double)((num_kb + per - 1) / per);
+      const double cost = 14.0 + std::max(per * per_stage * 1.1, pieces * epi1) + 9.0 + parts * (bn * sh.ms / 256.0);
+      if (cost < best_sk_cost - 1e-9) {
+        best_sk_cost = cost;
+        best_sk.bn = bn;
+        best_sk.pair = sh.pair;
+        best_sk.bk = sh.bk;
+        best_sk.ms = sh.ms;
+        best_sk.wr = 0;
+        best_sk.ksplit = 1;
+        best_sk.kb_per = num_kb;
+        best_sk.sk = 1;
+        best_sk.ws_bytes = sk_ws;
+      }
+    }
     for (int ks = 1; ks <= 32; ++ks) {
       const int kb_per = (num_kb + ks - 1) / ks;
       const int kse = (num_kb + kb_per - 1) / kb_per;  // slices actually used
@@ -982,11 +1153,12 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
       const long waves = (units + slots - 1) / slots;
       // epilogue: ~0.8 us per 32-column chunk and warp group; 256-wide residual tiles use one
       // group; with two M sub-tiles each group drains a whole sub-tile
-      const double epi = sh.ms == 2 ? 0.8 * (bn / 32) : 0.8 * (bn / 32) / ((has_res && bn == 256) ? 1 : 2);
+      const double epi = epi1;
       double cost = 14.0 + (waves - 1) * 2.0 + waves * std::max(kb_per * per_stage, epi);
       if (ks > 1) cost += (double)(ks + 2) * M * N * 4 / 8.0e6;
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
+        best_waves = waves;
         best.bn = bn;
         best.pair = sh.pair;
         best.bk = sh.bk;
@@ -998,6 +1170,7 @@ TilePlan plan_tiles(int M, int N, int K, int cb, bool has_res, int sms, size_t w
       }
     }
   }
+  if (best_sk_cost < 1e300 && (fsk > 0 || (best_waves <= 4 && best_sk_cost < best_cost - 1.0))) return best_sk;
   if (best_cost == 1e300) {  // forced shape infeasible: single-CTA tiles of the forced width, no split
     best.bn = force_bn > 0 ? force_bn : 256;
     best.pair = 1;
@@ -1021,7 +1194,7 @@ size_t tc_gemm_workspace_bytes(const TcGemmArgs& a) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   return plan_tiles(a.M, a.N, problem_k(a), problem_cb(a), a.res != nullptr, sm_count(dev), kWsCap, a.bn, true,
-                    a.a_mode == 0 ? a.kh * a.kw : 1)
+                    a.a_mode == 0 ? a.kh * a.kw : 1, a.sk != 0)
       .ws_bytes;
 }
 
@@ -1069,6 +1242,9 @@ bool tc_gemm_supported(const TcGemmArgs& a, std::string* why) {
   return true;
 }
 
+static std::atomic<uint64_t> g_streamk_launches{0};
+uint64_t tc_gemm_streamk_launches() { return g_streamk_launches.load(); }
+
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   std::string why;
   if (!tc_gemm_supported(a, &why)) {
@@ -1089,7 +1265,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   }
   const size_t ws_limit = (a.ws && a.batch == 1) ? std::min(a.ws_bytes, kWsCap) : 0;  // batched: no split
   const TilePlan tp = plan_tiles(a.M, a.N, K, cb, a.res != nullptr, sms, ws_limit, a.bn, a.batch == 1,
-                                 a.a_mode == 0 ? a.kh * a.kw : 1);
+                                 a.a_mode == 0 ? a.kh * a.kw : 1, a.sk && a.sk_flags && a.batch == 1);
   const int arows = kBM * tp.ms;  // A rows per box
   AMaps ma;
   CUtensorMap mb, my, mr;
@@ -1167,6 +1343,19 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
     return SPINN_CUDA_EINVAL;
   }
   p.num_units = (int)(tiles * zs);
+  if (tp.sk) {
+    // every slot is a worker (the grid is min(num_units, slots)); each gets >= 2 k-blocks
+    const long total = tiles * p.num_kb;
+    if (total > 0x7FFFFFFF) {
+      set_error("tcgen05 gemm: too many k-blocks for stream-K");
+      return SPINN_CUDA_EINVAL;
+    }
+    p.num_units = (int)total;
+    p.sk = 1;
+    p.sk_ws = a.ws;
+    p.sk_flags = a.sk_flags;
+    g_streamk_launches.fetch_add(1);
+  }
 
   p.has_res = a.res != nullptr && !split;
   p.act = a.act;

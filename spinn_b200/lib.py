@@ -91,6 +91,7 @@ _SIGS = {
     "spinn_cuda_host_alloc": (ctypes.c_void_p, [ctypes.c_size_t]),
     "spinn_cuda_host_free": (None, [ctypes.c_void_p]),
     "spinn_cuda_version": (ctypes.c_char_p, []),
+    "spinn_cuda_stat_streamk_launches": (ctypes.c_uint64, []),
 }
 
 

@@ -204,6 +204,85 @@ def test_gemm_cta_pair_tiles(cuda_lib, port_oracle, monkeypatch, case, tiles):
     assert rel_l2(y, ref) <= TOL, rel_l2(y, ref)
 
 
+# bn,ksplit,pair,bk,ms,wr,sk: stream-K forced with CTA pairs, 256/128-wide single CTAs and two
+# M sub-tiles
+SK_SHAPES = ["256,1,2,64,1,0,1", "128,1,2,64,1,0,1", "256,1,1,32,1,0,1", "128,1,1,64,1,0,1",
+             "64,1,1,32,2,0,1", "128,1,1,64,2,0,1"]
+SK_CONV_CASES = [
+    # n, c, h, w, oc, k, s, p, group, act, bias, res -- each has at least two k-blocks per
+    # worker for every SK shape, and tiles split over two or more workers
+    (2, 256, 28, 28, 200, 3, 1, 1, 1, 1, True, False),   # 3x3; last 256-row tile 32 rows; N ragged
+    (8, 256, 14, 14, 256, 3, 1, 1, 1, 3, True, False),   # ResNet 14x14 3x3 shape, SiLU
+    (16, 1024, 14, 14, 256, 1, 1, 0, 1, 0, False, False),  # 1x1, deep K, no bias
+    (8, 16, 64, 64, 64, 3, 1, 1, 1, 1, True, False),     # C=16 (64-B swizzle), 3-5 k-blocks a tile
+]
+
+
+def _sk_launches():
+    from spinn_b200 import lib
+    return lib.lib().spinn_cuda_stat_streamk_launches()
+
+
+@pytest.mark.parametrize("tiles", SK_SHAPES)
+@pytest.mark.parametrize("case", SK_CONV_CASES, ids=lambda c: "x".join(map(str, c[:9])))
+def test_conv2d_stream_k(cuda_lib, port_oracle, monkeypatch, case, tiles):
+    """Stream-K: every worker an equal share of the k-blocks across tile boundaries; a tile
+    split between workers is finished by the one holding its first k-blocks, which adds the
+    others' partial sums after a flag handoff.  Results match the oracle, the schedule really
+    ran, and repeated runs are bit-identical (partials added in worker order)."""
+    from spinn_b200 import runtime
+    monkeypatch.setenv("SPINN_TC_TILES", tiles)
+    n, c, h, w, oc, k, s, p, g, act, bias, res = case
+    rng = np.random.default_rng(hash(case) & 0xFFFF)
+    x, wt, b, r, yshape = _conv_case(rng, n, c, h, w, oc, k, s, p, g, act, bias, res)
+    params = runtime.conv_params((k, k), (s, s), (p, p, p, p), (1, 1), g, 0, act)
+    ref = port_oracle.conv2d(x, wt, b, r, (s, s), (p, p), (1, 1), g, act, yshape[2:])
+    outs = []
+    for _ in range(2):
+        before = _sk_launches()
+        y = np.full(yshape, np.nan, np.float32)
+        runtime.conv2d(x, wt, y, b, r, params)
+        assert _sk_launches() > before, "stream-K schedule not taken"
+        assert np.isfinite(y).all()
+        assert rel_l2(y, ref) <= TOL, rel_l2(y, ref)
+        outs.append(y)
+    assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("tiles", SK_SHAPES)
+def test_gemm_stream_k(cuda_lib, port_oracle, monkeypatch, tiles):
+    from spinn_b200 import runtime
+    monkeypatch.setenv("SPINN_TC_TILES", tiles)
+    rng = np.random.default_rng(17)
+    m, n, k = 1100, 300, 4000
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    c = rng.uniform(-1, 1, n).astype(np.float32)
+    y = np.zeros((m, n), np.float32)
+    before = _sk_launches()
+    runtime.gemm(a, b, y, c, runtime.gemm_params(0.5, 1.0, 0, 0))
+    assert _sk_launches() > before, "stream-K schedule not taken"
+    ref = port_oracle.gemm(a, b, c, m, n, k, 0, 0, 0.5, 1.0)
+    assert rel_l2(y, ref) <= TOL, rel_l2(y, ref)
+
+
+def test_stream_k_chosen_for_short_last_wave(cuda_lib, port_oracle):
+    """The planner takes stream-K by itself where whole tiles would leave a short last wave
+    behind a long reduction (ResNet's 7x7 512-channel 3x3 layer at 256 images: 98 pair tiles
+    of 72 k-blocks on 74 pair slots)."""
+    from spinn_b200 import runtime
+    rng = np.random.default_rng(23)
+    x, wt, b, r, yshape = _conv_case(rng, 256, 512, 7, 7, 512, 3, 1, 1, 1, 1, True, False)
+    params = runtime.conv_params((3, 3), (1, 1), (1, 1, 1, 1), (1, 1), 1, 0, 1)
+    before = _sk_launches()
+    y = np.zeros(yshape, np.float32)
+    runtime.conv2d(x, wt, y, b, r, params)
+    assert _sk_launches() > before
+    for sl in (slice(0, 2), slice(254, 256)):  # first and last rows of the problem
+        ref = port_oracle.conv2d(x[sl], wt, b, None, (1, 1), (1, 1), (1, 1), 1, 1, yshape[2:])
+        assert rel_l2(y[sl], ref) <= TOL, rel_l2(y[sl], ref)
+
+
 @pytest.mark.parametrize("tiles", [None, "256,1,2", "128,1,1", "64,1,1,64,2"])
 def test_matmul_batched_one_launch(cuda_lib, port_oracle, monkeypatch, tiles):
     """Batched MatMul runs as one launch over [batch][M][K] planes (3-D tensor maps, the batch

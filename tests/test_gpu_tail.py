@@ -16,6 +16,13 @@ from conftest import rel_l2
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _whole_tiles(monkeypatch):
+    """The fused tail is compared bit for bit (1e-6) with the separate launches, which must
+    then run as whole tiles: a stream-K launch sums a split tile's parts in another order."""
+    monkeypatch.setenv("SPINN_NO_SK", "1")
+
+
 def _tail_graph(batch, hw, n1, k1, n2, relu_reduce=True, seed=11):
     from spinn_b200 import netdef
     return netdef.bottleneck_tail(batch, hw, n1, k1, n2, relu_reduce, seed)
