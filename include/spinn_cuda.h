@@ -244,6 +244,21 @@ const char *spinn_cuda_version(void);
  * CTA an equal share of the problem's k-blocks across tile boundaries). */
 uint64_t spinn_cuda_stat_streamk_launches(void);
 
+/* Diagnostics (host only, no GPU needed): the tile plan the tcgen05 planner makes for an
+ * M x N x K problem with channel blocks of `channel_block` (4/8/16/32) floats, `taps` filter
+ * taps (1 for a GEMM), on `sms` SMs: out7 = {tile width, CTA pair (2) or single (1), stage
+ * depth, M sub-tiles, resident weights, K split, stream-K}.  SPINN_TC_TILES, when set, applies
+ * as it does to launches. */
+int spinn_cuda_diag_tile_plan(int m, int n, int k, int channel_block, int has_residual, int sms, int taps,
+                              int allow_streamk, int *out7);
+/* Diagnostics (host only): piece `piece` of stream-K worker `worker` of `workers` over
+ * num_tiles x num_kb k-blocks: returns 1 and out4 = {tile, first k-block, end k-block, kind
+ * (0 whole tile, 1 tail part, 2 head part)}, 0 past the worker's last piece, or an error. */
+int spinn_cuda_diag_streamk_piece(int num_tiles, int num_kb, int worker, int workers, int piece, int *out4);
+/* Diagnostics (host only): 1 when worker `worker` holds a tail part of tile `tile`, judged as
+ * the head worker of that tile does (the worker's range starts before the tile's end). */
+int spinn_cuda_diag_streamk_contributes(int num_tiles, int num_kb, int worker, int workers, int tile);
+
 #ifdef __cplusplus
 }
 #endif

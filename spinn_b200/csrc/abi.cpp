@@ -368,6 +368,36 @@ __attribute__((visibility("default"))) uint64_t spinn_cuda_stat_streamk_launches
   return spinn::tc_gemm_streamk_launches();
 }
 
+__attribute__((visibility("default"))) int spinn_cuda_diag_tile_plan(int m, int n, int k, int channel_block,
+                                                                     int has_residual, int sms, int taps,
+                                                                     int allow_streamk, int* out7) {
+  if (!out7 || m <= 0 || n <= 0 || k <= 0 || sms <= 0 || taps <= 0 ||
+      (channel_block != 4 && channel_block != 8 && channel_block != 16 && channel_block != 32)) {
+    set_error("spinn_cuda_diag_tile_plan: invalid arguments");
+    return SPINN_CUDA_EINVAL;
+  }
+  tc_gemm_plan_for(m, n, k, channel_block, has_residual != 0, sms, taps, allow_streamk != 0, out7);
+  return 0;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_diag_streamk_piece(int num_tiles, int num_kb, int worker,
+                                                                         int workers, int piece, int* out4) {
+  if (!out4 || num_tiles <= 0 || num_kb <= 0 || workers <= 0 || worker < 0 || worker >= workers || piece < 0 ||
+      (long long)num_tiles * num_kb < workers) {
+    set_error("spinn_cuda_diag_streamk_piece: invalid arguments");
+    return SPINN_CUDA_EINVAL;
+  }
+  const SkRange r = sk_range(num_tiles, num_kb, worker, workers);
+  if (!sk_piece(r, piece, &out4[0], &out4[1], &out4[2], &out4[3])) return 0;
+  return 1;
+}
+
+__attribute__((visibility("default"))) int spinn_cuda_diag_streamk_contributes(int num_tiles, int num_kb,
+                                                                               int worker, int workers, int tile) {
+  if (num_tiles <= 0 || num_kb <= 0 || workers <= 0 || worker < 0 || (long long)num_tiles * num_kb < workers) return 0;
+  return sk_contributes(sk_range(num_tiles, num_kb, 0, workers), worker, tile) ? 1 : 0;
+}
+
 __attribute__((visibility("default"))) void* spinn_cuda_host_alloc(size_t bytes) {
   void* p = nullptr;
   if (cudaHostAlloc(&p, bytes, cudaHostAllocDefault) != cudaSuccess) {

@@ -117,6 +117,44 @@ struct TcGemmArgs {
   int* sk_flags = nullptr;
 };
 constexpr int kTcSkFlags = 512;
+
+// Stream-K work split, shared by the kernel and the host-side checks.  Worker w of G owns
+// k-blocks [w T / G, (w + 1) T / G) of the T = num_tiles x num_kb k-blocks laid out tile after
+// tile (T >= G: every range is non-empty).  Piece i of a worker is its part [kb0, kb1) of
+// tile t0 + i; kind 0 is a whole tile, 1 a tail piece (the range starts inside the tile: only
+// ever a worker's first piece), 2 the head of a tile that later workers finish (only ever its
+// last piece).
+struct SkRange {
+  long long r0, r1, total;
+  int t0, num_kb, workers;
+};
+__host__ __device__ inline SkRange sk_range(int num_tiles, int num_kb, int w, int workers) {
+  SkRange r;
+  r.total = (long long)num_tiles * num_kb;
+  r.r0 = r.total * w / workers;
+  r.r1 = r.total * (w + 1) / workers;
+  r.t0 = (int)(r.r0 / num_kb);
+  r.num_kb = num_kb;
+  r.workers = workers;
+  return r;
+}
+__host__ __device__ inline bool sk_piece(const SkRange& r, int i, int* t, int* kb0, int* kb1, int* kind) {
+  *t = r.t0 + i;
+  const long long base = (long long)*t * r.num_kb;
+  const long long g0 = r.r0 > base ? r.r0 : base;
+  const long long g1 = r.r1 < base + r.num_kb ? r.r1 : base + r.num_kb;
+  if (g0 >= g1) return false;
+  *kb0 = (int)(g0 - base);
+  *kb1 = (int)(g1 - base);
+  *kind = *kb0 > 0 ? 1 : *kb1 < r.num_kb ? 2 : 0;
+  return true;
+}
+// Whether worker j (> the tile's head worker) holds a tail piece of tile t: its range starts
+// before the tile's end.  The contributors of a head piece are the workers after its own
+// for which this holds, in order.
+__host__ __device__ inline bool sk_contributes(const SkRange& r, int j, int t) {
+  return j < r.workers && r.total * j / r.workers < (long long)(t + 1) * r.num_kb;
+}
 // Workspace a launch of `a` would use (0 when it would not split), for planners.
 size_t tc_gemm_workspace_bytes(const TcGemmArgs& a);
 // Checks whether the tcgen05 path accepts the problem (alignment, corner ranges ...).
@@ -124,6 +162,9 @@ bool tc_gemm_supported(const TcGemmArgs& a, std::string* why);
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);
 // Launches so far (process-wide) that ran the stream-K schedule.
 uint64_t tc_gemm_streamk_launches();
+// The tile plan a launch of this problem would use on `sms` SMs (no workspace limit below the
+// launcher's cap): {bn, pair, bk, ms, wr, ksplit, sk}.  Host-only; for checks of the planner.
+void tc_gemm_plan_for(int M, int N, int K, int cb, bool has_res, int sms, int taps, bool allow_sk, int out[7]);
 // Number of K blocks (32 wide) and padded K the weight matrix must have.
 inline int tc_num_kb(int K) { return (K + 31) / 32; }
 

@@ -311,20 +311,12 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
   // shared-memory queue -- evened out the CTAs' finishing times but measured 1-2% slower end
   // to end).  Stream-K: consecutive tiles covering the worker's k-block range.
   const bool sk = !RES && !WR && p.sk != 0;
-  const long sk_total = (long)p.num_tiles * p.num_kb;
-  const long sk_r0 = sk ? sk_total * unit0 / unit_step : 0, sk_r1 = sk ? sk_total * (unit0 + 1) / unit_step : 0;
-  const int sk_t0 = sk ? (int)(sk_r0 / p.num_kb) : 0;
+  const SkRange skr = sk ? sk_range(p.num_tiles, p.num_kb, unit0, unit_step) : SkRange{};
   auto get_piece = [&](int it, Piece& pc) -> bool {
     int t;
     if (sk) {
-      t = sk_t0 + it;
-      const long base = (long)t * p.num_kb;
-      const long g0 = max(sk_r0, base), g1 = min(sk_r1, base + p.num_kb);
-      if (g0 >= g1) return false;
+      if (!sk_piece(skr, it, &t, &pc.kb0, &pc.kb1, &pc.kind)) return false;
       pc.z = 0;
-      pc.kb0 = (int)(g0 - base);
-      pc.kb1 = (int)(g1 - base);
-      pc.kind = pc.kb0 > 0 ? 1 : pc.kb1 < p.num_kb ? 2 : 0;
     } else {
       const long u = (long)unit0 + (long)it * unit_step;
       if (u >= p.num_units) return false;
@@ -649,9 +641,8 @@ __global__ void __launch_bounds__(Cfg<BN, CB, RES, PAIR, BK_, MS_, WR_>::THREADS
       // now, this is the CTA's last piece -- in one round trip, instead of one per chunk.
       int sk_j1 = unit0 + 1, sk_jfast = unit0 + 1;
       if (sk && pc.kind == 2) {
-        const long tend = (long)(sk_t0 + it + 1) * p.num_kb;
         bool ok = true;
-        for (; ok && sk_j1 < unit_step && sk_total * sk_j1 / unit_step < tend; ++sk_j1)
+        for (; ok && sk_contributes(skr, sk_j1, skr.t0 + it); ++sk_j1)
           ok = warp_wait_flag(p.sk_flags + sk_j1 * PAIR + rank, C::EPI_WARPS, abort_flag, kTimeoutNs);
         if (!ok) break;
         sk_jfast = min(sk_j1, unit0 + 1 + SK_NCAP);
@@ -1244,6 +1235,17 @@ bool tc_gemm_supported(const TcGemmArgs& a, std::string* why) {
 
 static std::atomic<uint64_t> g_streamk_launches{0};
 uint64_t tc_gemm_streamk_launches() { return g_streamk_launches.load(); }
+
+void tc_gemm_plan_for(int M, int N, int K, int cb, bool has_res, int sms, int taps, bool allow_sk, int out[7]) {
+  const TilePlan tp = plan_tiles(M, N, K, cb, has_res, sms, kWsCap, 0, true, taps, allow_sk);
+  out[0] = tp.bn;
+  out[1] = tp.pair;
+  out[2] = tp.bk;
+  out[3] = tp.ms;
+  out[4] = tp.wr;
+  out[5] = tp.ksplit;
+  out[6] = tp.sk;
+}
 
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream) {
   std::string why;

@@ -92,6 +92,9 @@ _SIGS = {
     "spinn_cuda_host_free": (None, [ctypes.c_void_p]),
     "spinn_cuda_version": (ctypes.c_char_p, []),
     "spinn_cuda_stat_streamk_launches": (ctypes.c_uint64, []),
+    "spinn_cuda_diag_tile_plan": (ctypes.c_int, [ctypes.c_int] * 8 + [ctypes.POINTER(ctypes.c_int)]),
+    "spinn_cuda_diag_streamk_piece": (ctypes.c_int, [ctypes.c_int] * 5 + [ctypes.POINTER(ctypes.c_int)]),
+    "spinn_cuda_diag_streamk_contributes": (ctypes.c_int, [ctypes.c_int] * 5),
 }
 
 
