@@ -79,6 +79,11 @@ int spinn_cuda_sync(void);
  * context stays usable. */
 int spinn_cuda_selftest_wait_expiry(uint64_t timeout_ns);
 
+/* Diagnostic: the same for the bounded wait on a stream-K handoff flag (acquire loads of a
+ * word another CTA raises): one warp waits on a flag nothing raises; SPINN_CUDA_ETIMEOUT is the
+ * expected result, the context stays usable. */
+int spinn_cuda_selftest_flag_wait_expiry(uint64_t timeout_ns);
+
 /* Releases the calling thread's session (stream, scratch, cached weights). */
 void spinn_cuda_shutdown(void);
 

@@ -330,6 +330,16 @@ __attribute__((visibility("default"))) int spinn_cuda_sync(void) {
   return check_session(S);
 }
 
+__attribute__((visibility("default"))) int spinn_cuda_selftest_flag_wait_expiry(uint64_t timeout_ns) {
+  int rc = ensure_session();
+  if (rc) return rc;
+  Session& S = g_sess;
+  rc = launch_flag_wait_selftest(device_error_flag(S.device), timeout_ns, S.stream);
+  if (rc) return rc;
+  SPINN_CUDA_TRY(cudaStreamSynchronize(S.stream));
+  return check_session(S);
+}
+
 __attribute__((visibility("default"))) int spinn_cuda_selftest_wait_expiry(uint64_t timeout_ns) {
   int rc = ensure_session();
   if (rc) return rc;

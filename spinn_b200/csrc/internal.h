@@ -160,6 +160,9 @@ size_t tc_gemm_workspace_bytes(const TcGemmArgs& a);
 // Checks whether the tcgen05 path accepts the problem (alignment, corner ranges ...).
 bool tc_gemm_supported(const TcGemmArgs& a, std::string* why);
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t stream);
+// One-warp kernel whose bounded wait on a stream-K flag that nothing raises expires after
+// timeout_ns (<= 1 s) and raises *err.
+int launch_flag_wait_selftest(int* err, uint64_t timeout_ns, cudaStream_t s);
 // Launches so far (process-wide) that ran the stream-K schedule.
 uint64_t tc_gemm_streamk_launches();
 // The tile plan a launch of this problem would use on `sms` SMs (no workspace limit below the

@@ -223,6 +223,16 @@ __device__ __forceinline__ bool warp_wait_flag(const int* f, int target, volatil
   }
 }
 
+// A stream-K flag that nothing ever raises, and one warp that waits on it with the kernels'
+// bounded wait: the wait must expire, raise the error word and return.
+__device__ int g_flag_never_raised = 0;
+__global__ void __launch_bounds__(32) flag_wait_expiry_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
+  __syncwarp();
+  if (!warp_wait_flag(&g_flag_never_raised, 1, &abort_flag, timeout_ns) && threadIdx.x == 0) atomicExch(err, 1);
+}
+
 // PAIR = 1: one CTA per 128 x BN tile.  PAIR = 2: a cluster of two CTAs per 256 x BN tile
 // with one cta_group::2 MMA stream issued by the leader (rank 0); each CTA loads its own 128
 // rows of A and BN/2 rows of W.  Barrier roles in pair mode: `full` of the leader counts the
@@ -1231,6 +1241,14 @@ bool tc_gemm_supported(const TcGemmArgs& a, std::string* why) {
     if (a.kpad < a.K) return fail("weight K smaller than K");
   }
   return true;
+}
+
+int launch_flag_wait_selftest(int* err, uint64_t timeout_ns, cudaStream_t s) {
+  SPINN_CHECK_ARG(err != nullptr && timeout_ns > 0 && timeout_ns <= 1000000000ull,
+                  "flag wait self-test: timeout %llu ns outside (0, 1 s]", (unsigned long long)timeout_ns);
+  flag_wait_expiry_kernel<<<1, 32, 0, s>>>(err, (unsigned long long)timeout_ns);
+  SPINN_CUDA_TRY(cudaGetLastError());
+  return 0;
 }
 
 static std::atomic<uint64_t> g_streamk_launches{0};

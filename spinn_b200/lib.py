@@ -69,6 +69,7 @@ _SIGS = {
     "spinn_cuda_run_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_submit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_selftest_wait_expiry": (ctypes.c_int, [ctypes.c_uint64]),
+    "spinn_cuda_selftest_flag_wait_expiry": (ctypes.c_int, [ctypes.c_uint64]),
     "spinn_cuda_wait": (ctypes.c_int, [ctypes.c_void_p]),
     "spinn_cuda_run_profiled": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "spinn_cuda_io_ptr": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
